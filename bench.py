@@ -1,0 +1,423 @@
+#!/usr/bin/env python
+"""Headline benchmark: pooled host->GPU bandwidth into GPU0.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+One step moves ``--bytes`` (default 4 GiB, far larger than the 126 MB L2)
+of uniform-random bytes from a page-locked host buffer into GPU0 over the
+direct PCIe lane plus N-1 relay lanes.  The total work is
+fixed as N grows (strong scaling).  Every step is submitted and waited through
+the data plane; the K timed steps are bracketed by a barrier and a device
+synchronisation on both sides and timed with CUDA events on GPU0; the
+reported time is the max over ranks.  Under torchrun every rank joins the
+barriers, rank 0 drives the data plane, which holds contexts on all N GPUs
+(one data-plane process per node, as in the reference's worker).
+
+``--impl reference`` runs the unmodified reference (installed under
+baseline/_ref) through its own public runtime API: one persistent
+``_turbobus.Runtime``, its own profiler and planner, ``fetch_plan_to_gpu`` +
+``wait`` per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "pooled host->GPU GB/s into one GPU"
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--bytes", type=int, default=4 << 30)
+    p.add_argument("--chunk", type=int, default=16 << 20)
+    p.add_argument("--slots", type=int, default=3)
+    p.add_argument("--ctas", type=int, default=2, help="lane-kernel CTAs per lane")
+    p.add_argument("--direction", choices=["h2d", "d2h"], default="h2d")
+    p.add_argument("--no-checksum", action="store_true", help="skip the fused per-chunk checksum")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--json-out", default="")
+    return p.parse_args(argv)
+
+
+# ---- distributed plumbing -------------------------------------------------------------
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", self.local_rank))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg is not None:
+            import torch
+
+            self.pg.barrier(device_ids=[self.local_rank])
+            torch.cuda.synchronize()
+
+    def max(self, value: float) -> float:
+        if self.pg is None:
+            return value
+        import torch
+
+        t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{self.local_rank}")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+# ---- clocks -------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: int):
+        self.gpus = gpus
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._t:
+            self._t.join(timeout=2)
+        sm, mx, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if idx >= self.gpus:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                pass
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+            "power_w_max": max(power) if power else None,
+        }
+
+
+# ---- host data --------------------------------------------------------------------------
+
+def fill_random(arr, seed: int = 0, threads: int = 16):
+    import numpy as np
+
+    parts = np.array_split(arr, threads)
+
+    def work(i):
+        g = np.random.default_rng(seed + i)
+        p = parts[i]
+        step = 64 << 20
+        for o in range(0, p.size, step):
+            seg = p[o:o + step]
+            seg[:] = np.frombuffer(g.bytes(seg.size), dtype=np.uint8)
+
+    ths = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+
+
+# ---- our implementation ---------------------------------------------------------------
+
+def run_ours(args, dist: Dist) -> dict:
+    import numpy as np
+    import torch
+
+    from pcie_pool_b200.parallel.engine import D2H, H2D, PoolEngine
+    from pcie_pool_b200.parallel.planning import plan_lanes
+    from pcie_pool_b200.utils.checksum import combine
+    from pcie_pool_b200.utils.host_memory import PinnedHostBuffer
+
+    N = args.gpus
+    devices = list(range(N))
+    n = args.bytes
+    out: dict = {}
+    if dist.rank == 0:
+        torch.cuda.set_device(0)
+        host = PinnedHostBuffer(n, fill=None)
+        fill_random(host.numpy(), seed=1234)
+        dev = torch.empty(n, dtype=torch.uint8, device="cuda:0")
+        if args.direction == "d2h":
+            dev.copy_(torch.from_numpy(host.numpy()).to("cuda:0"))
+        eng = PoolEngine(devices, slot_bytes=max(args.chunk, 1 << 20), slots=args.slots,
+                         ctas_per_lane=args.ctas, timeout_s=20.0)
+        lanes = plan_lanes(n, args.chunk, devices, target=0)
+        direction = H2D if args.direction == "h2d" else D2H
+        checksum = not args.no_checksum
+        kernel_per_step = 1 if (checksum or N > 1) else 0
+
+        def step():
+            r = eng.run(direction, 0, host.ptr, n, dev.data_ptr(), n, lanes, checksum=checksum)
+            if not r.ok:
+                raise RuntimeError(r.error)
+            return r
+
+        for _ in range(args.warmup):
+            step()
+    dist.barrier()
+    res = None
+    elapsed_ms = 0.0
+    clocks = ClockSampler(N)
+    if dist.rank == 0:
+        torch.cuda.synchronize()
+        clocks.start()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            res = step()
+        e1.record()
+        torch.cuda.synchronize()
+        elapsed_ms = e0.elapsed_time(e1)
+        clk = clocks.stop()
+    dist.barrier()
+    elapsed_ms = dist.max(elapsed_ms)
+    if dist.rank == 0:
+        verified = None
+        if checksum and direction == H2D:
+            C = __import__("pcie_pool_b200._C", fromlist=["x"])
+            host_sum = C.checksum_host(host.ptr, n)
+            got = combine(_shift_chunk_sums(res, lanes))
+            verified = (tuple(int(x) for x in host_sum) == got)
+        out = {
+            "elapsed_ms": elapsed_ms,
+            "clocks": clk,
+            "lane_ms": [(l.device, round(l.cuda_ms, 3), l.bytes) for l in res.lanes],
+            "verified": verified,
+            "gpu_launches": kernel_per_step * args.steps,
+            "transfer_cuda_ms": res.cuda_ms,
+        }
+        if not args.no_e2e:
+            try:
+                out["e2e"] = run_e2e(args, eng, host, dev, lanes)
+            except Exception as exc:  # pragma: no cover - reported in the JSON line
+                out["e2e"] = {"error": f"{type(exc).__name__}: {exc}"}
+        del eng
+        host.release()
+    return out
+
+
+def _shift_chunk_sums(res, lanes):
+    """Per-chunk checksums are chunk-local; re-base them onto the whole buffer
+    so their sum equals the checksum of the full host buffer."""
+    i = 0
+    out = []
+    for lane in lanes:
+        for s in lane.src_off:
+            a, w = int(res.checksums[i][0]), int(res.checksums[i][1])
+            out.append((a, (w + (int(s) // 4) * a) & (2**64 - 1)))
+            i += 1
+    return out
+
+
+def run_e2e(args, eng, host, dev, lanes) -> dict:
+    """Same metric through the public client API (TurboBusClient -> daemon ->
+    executor -> engine), inputs from the pinned host store, result read back."""
+    from pcie_pool_b200.e2e import public_api_pooled_load
+
+    return public_api_pooled_load(args, eng, host, dev)
+
+
+# ---- reference implementation -----------------------------------------------------------
+
+def run_reference(args, dist: Dist) -> dict:
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "turbobus").exists():
+        return {"unavailable": "reference not installed under baseline/_ref"}
+    sys.path.insert(0, str(ref_root))
+    import torch
+
+    out: dict = {}
+    N = args.gpus
+    n = args.bytes
+    if dist.rank == 0:
+        from turbobus import runtime_engine
+        from turbobus.planner_engine import PlannerEngine
+        from turbobus.runtime_engine import RuntimeOptions
+
+        native = runtime_engine._turbobus
+        if native is None:
+            return {"unavailable": "reference native extension failed to import"}
+        torch.cuda.set_device(0)
+        host_t = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+        fill_random(host_t.numpy(), seed=1234)
+        dev = torch.empty(n, dtype=torch.uint8, device="cuda:0")
+        opts = RuntimeOptions(chunk_bytes=args.chunk)
+        rt = native.Runtime(opts.to_native())
+        relays = list(range(1, N))
+        rt.init(0, relays)
+        profile = rt.profile(256 << 20, False)
+        plan = PlannerEngine().plan(n, args.chunk, profile, "pool", direction=args.direction)
+        nplan = runtime_engine._native_transfer_plan(plan)
+
+        def step():
+            if args.direction == "h2d":
+                h = rt.fetch_plan_to_gpu(host_t.data_ptr(), n, dev.data_ptr(), n, nplan)
+            else:
+                h = rt.offload_plan_to_cpu(dev.data_ptr(), n, host_t.data_ptr(), n, nplan)
+            rt.wait(h)
+            return rt.stats(h)
+
+        for _ in range(args.warmup):
+            step()
+    dist.barrier()
+    elapsed_ms = 0.0
+    clocks = ClockSampler(N)
+    if dist.rank == 0:
+        torch.cuda.synchronize()
+        clocks.start()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            st = step()
+        e1.record()
+        torch.cuda.synchronize()
+        elapsed_ms = e0.elapsed_time(e1)
+        clk = clocks.stop()
+    dist.barrier()
+    elapsed_ms = dist.max(elapsed_ms)
+    if dist.rank == 0:
+        verified = bool(torch.equal(dev.cpu(), host_t)) if args.direction == "h2d" else None
+        out = {
+            "elapsed_ms": elapsed_ms,
+            "clocks": clk,
+            "verified": verified,
+            "gpu_launches": 0,
+            "transfer_cuda_ms": st.cuda_elapsed_ms,
+            "lane_ms": [(p.relay_device, round(p.cuda_elapsed_ms, 3), p.bytes) for p in st.path_stats],
+            "profile": {
+                "direct_h2d_gibps": profile.direct_h2d_bw_gbps,
+                "relays": [(r.relay_device, r.h2d_bw_gbps, r.p2p_bw_gbps, r.effective_bw_gbps)
+                           for r in profile.relays],
+            },
+        }
+        del rt
+    return out
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    dist = Dist()
+    if args.impl == "reference":
+        res = run_reference(args, dist)
+    else:
+        res = run_ours(args, dist)
+    if dist.rank == 0:
+        if "unavailable" in res:
+            line = {"impl": "reference", "unavailable": res["unavailable"]}
+        else:
+            total = args.bytes * args.steps
+            ms = res["elapsed_ms"]
+            value = total / 1e9 / (ms / 1e3)
+            N = args.gpus
+            line = {
+                "metric": METRIC,
+                "value": round(value, 3),
+                "unit": "GB/s",
+                "n_gpus": N,
+                "steps": args.steps,
+                "warmup": args.warmup,
+                "ms_per_step": round(ms / args.steps, 3),
+                "higher_is_better": True,
+                "scaling": "strong",
+                "vs_baseline": None,
+                "dtype": "uint8 (raw bytes)",
+                "data": "synthetic (uniform-random bytes, seeded)",
+                "config": {
+                    "model": "pooled-transfer sweep point (BASELINE config 2)",
+                    "direction": args.direction,
+                    "transfer_bytes": args.bytes,
+                    "chunk_bytes": args.chunk,
+                    "target_gpu": 0,
+                    "relay_gpus": list(range(1, N)),
+                    "parallelism": f"direct+{N - 1}relay",
+                    "l2": "inputs larger than L2 (each step moves a fresh 4 GiB stream)",
+                },
+                "clocks": res.get("clocks"),
+                "gpu_launches": res.get("gpu_launches"),
+                "verified": res.get("verified"),
+                "lane_ms": res.get("lane_ms"),
+            }
+            if args.impl == "reference":
+                line["impl"] = "reference"
+                line["profile"] = res.get("profile")
+            else:
+                line["impl"] = "ours"
+                if "e2e" in res:
+                    line["e2e"] = res["e2e"]
+        s = json.dumps(line)
+        print(s, flush=True)
+        if args.json_out:
+            Path(args.json_out).write_text(s + "\n")
+    dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,513 @@
+// Fused lane kernels for sm_100a (see pool_kernels.h for the protocol).
+//
+// Data path per CTA: a kStages-deep ring of kTileBytes shared-memory stages.
+// One elected thread issues 1-D TMA bulk copies (cp.async.bulk, never with
+// .multicast::cluster) from the source -- for landing that is the relay GPU's
+// staging slot reached through the peer mapping over NVLink -- into shared
+// memory, tracked by per-stage mbarriers with complete_tx.  All threads fold
+// the tile into the chunk checksum straight from shared memory, then the
+// elected thread writes the tile out with a bulk shared->global store.
+//
+// Synchronisation with the copy engines uses two monotonically increasing
+// 32-bit counters per lane (ready / free) compared wrap-around safely; every
+// wait is bounded and ends in an error status, never a trap.
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include "device_utils.cuh"
+#include "pool_kernels.h"
+
+namespace ppb {
+namespace {
+
+using namespace dev;
+
+struct Tile {
+  const uint8_t* src;
+  uint8_t* dst;
+  uint64_t pos;  // byte position inside the chunk stream (checksum index)
+  uint32_t n;
+};
+
+__device__ __forceinline__ void record_error(int* status, int code, int lane, int chunk,
+                                             int detail) {
+  if (atomicCAS(status, 0, code) == 0) {
+    status[1] = lane;
+    status[2] = chunk;
+    status[3] = detail;
+  }
+  __threadfence_system();
+}
+
+__device__ __forceinline__ int find_lane(const LaneKernelParams& p, LaneDesc& out) {
+  for (uint32_t i = 0; i < p.num_lanes; ++i) {
+    const LaneDesc d = p.lanes[i];
+    if (blockIdx.x >= d.cta_begin && blockIdx.x < d.cta_begin + d.cta_count) {
+      out = d;
+      return static_cast<int>(i);
+    }
+  }
+  return -1;
+}
+
+// Byte-granular fallback for ragged or misaligned pieces.  Threads of the CTA
+// stride over [0, n); checksum contributions are accumulated per byte, which
+// equals the word definition because the checksum is linear in the words.
+__device__ void copy_generic(const uint8_t* src, uint8_t* dst, uint64_t n, uint64_t pos,
+                             bool store, bool do_csum, Csum& cs) {
+  for (uint64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const uint8_t b = ld_cg_u8(src + i);
+    if (store) dst[i] = b;
+    if (do_csum) {
+      const uint64_t at = pos + i;
+      const unsigned long long v = static_cast<unsigned long long>(b) << (8u * (at & 3u));
+      cs.s += v;
+      cs.w += (at / 4u + 1u) * v;
+    }
+  }
+}
+
+// Pipelined bulk-copy loop over the tiles j, j+G, j+2G, ... of one chunk.
+// `q` is the CTA's running tile counter: stage = q % kStages and the mbarrier
+// phase parity = (q / kStages) & 1.  Returns false on a copy timeout.
+template <class Geom>
+__device__ bool run_tiles(const Geom& geom, uint32_t ntiles, uint32_t j, uint32_t G, bool store,
+                          bool do_csum, uint32_t& q, uint64_t* bars, uint8_t* smem,
+                          Csum& cs, uint64_t timeout_ns) {
+  const uint32_t my_n = ntiles > j ? (ntiles - j + G - 1) / G : 0;
+  if (my_n == 0) return true;
+  const uint32_t base = q;
+  if (threadIdx.x == 0) {
+    if (store) bulk_wait_read<0>();  // earlier stores no longer read any stage
+    for (uint32_t k = 0; k < my_n && k < static_cast<uint32_t>(kStages); ++k) {
+      const Tile t = geom(j + k * G);
+      const uint32_t s = (base + k) % kStages;
+      mbar_arrive_expect_tx(&bars[s], t.n);
+      bulk_g2s(smem + size_t(s) * kTileBytes, t.src, t.n, &bars[s]);
+    }
+  }
+  bool ok = true;
+  uint32_t k = 0;
+  for (; k < my_n; ++k) {
+    const uint32_t s = (base + k) % kStages;
+    const uint32_t parity = ((base + k) / kStages) & 1u;
+    const Tile t = geom(j + k * G);
+    const bool got = mbar_wait(&bars[s], parity, globaltimer_ns() + timeout_ns);
+    if (!__syncthreads_and(got)) {
+      ok = false;
+      break;
+    }
+    uint8_t* stage = smem + size_t(s) * kTileBytes;
+    if (do_csum) {
+      const uint4* v = reinterpret_cast<const uint4*>(stage);
+      const uint32_t nv = t.n >> 4;
+      const uint64_t w0 = t.pos >> 2;
+      for (uint32_t i = threadIdx.x; i < nv; i += blockDim.x) csum_vec(cs, v[i], w0 + 4ull * i);
+    }
+    __syncthreads();  // every reader is done with this stage
+    if (threadIdx.x == 0) {
+      if (store) {
+        bulk_s2g(t.dst, stage, t.n);
+        bulk_commit();
+      }
+      if (k + kStages < my_n) {
+        if (store) bulk_wait_read<0>();
+        const Tile nt = geom(j + (k + kStages) * G);
+        mbar_arrive_expect_tx(&bars[s], nt.n);
+        bulk_g2s(stage, nt.src, nt.n, &bars[s]);
+      }
+    }
+  }
+  if (!ok) {
+    // Give the copies already in flight a bounded chance to land before the
+    // CTA leaves, so no bulk copy targets shared memory of an exited CTA.
+    const uint32_t issued = my_n < k + kStages ? my_n : k + kStages;
+    for (uint32_t r = k; r < issued; ++r) {
+      const uint32_t s = (base + r) % kStages;
+      mbar_wait(&bars[s], ((base + r) / kStages) & 1u, globaltimer_ns() + timeout_ns);
+    }
+    q = base + issued;
+    return false;
+  }
+  q = base + my_n;
+  return true;
+}
+
+struct CopyGeom {
+  const uint8_t* src;
+  uint8_t* dst;
+  uint32_t body;
+  __device__ Tile operator()(uint32_t k) const {
+    const uint32_t off = k * kTileBytes;
+    const uint32_t n = body - off < kTileBytes ? body - off : kTileBytes;
+    return Tile{src + off, dst ? dst + off : nullptr, off, n};
+  }
+};
+
+// Fixed-size units at scattered device addresses (paged-KV block lanes).
+// `scatter` = true: chunk stream -> unit addresses; false: gather.
+struct UnitGeom {
+  const uint8_t* stream_src;  // scatter: staged chunk; gather: unused
+  uint8_t* stream_dst;        // gather: staging slot; scatter: unused
+  const uint64_t* unit_addr;  // already offset to the chunk's first unit
+  uint32_t unit_bytes;
+  uint32_t tiles_per_unit;
+  bool scatter;
+  __device__ Tile operator()(uint32_t k) const {
+    const uint32_t u = k / tiles_per_unit;
+    const uint32_t sub = (k - u * tiles_per_unit) * kTileBytes;
+    const uint32_t n = unit_bytes - sub < kTileBytes ? unit_bytes - sub : kTileBytes;
+    const uint64_t pos = uint64_t(u) * unit_bytes + sub;
+    uint8_t* ua = reinterpret_cast<uint8_t*>(unit_addr[u]) + sub;
+    if (scatter) return Tile{stream_src + pos, ua, pos, n};
+    return Tile{ua, stream_dst ? stream_dst + pos : nullptr, pos, n};
+  }
+};
+
+// Variable ranges, pre-split on the host to at most kTileBytes each.
+struct RangeGeom {
+  const uint8_t* stream_src;
+  uint8_t* stream_dst;
+  const uint64_t* range_addr;  // offset to the chunk's first range
+  const uint32_t* range_bytes;
+  const uint64_t* range_pos;   // position of each range inside the chunk stream
+  bool scatter;
+  __device__ Tile operator()(uint32_t k) const {
+    const uint64_t pos = range_pos[k];
+    const uint32_t n = range_bytes[k];
+    uint8_t* ra = reinterpret_cast<uint8_t*>(range_addr[k]);
+    if (scatter) return Tile{stream_src + pos, ra, pos, n};
+    return Tile{ra, stream_dst ? stream_dst + pos : nullptr, pos, n};
+  }
+};
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// Contiguous copy of one chunk (bulk body + generic ragged tail).
+__device__ bool move_contiguous(const uint8_t* src, uint8_t* dst, uint32_t bytes, uint32_t j,
+                                uint32_t G, bool store, bool do_csum, uint32_t& q,
+                                uint64_t* bars, uint8_t* smem, Csum& cs, uint64_t timeout_ns) {
+  const bool fast = aligned16(src) && (!store || aligned16(dst));
+  if (!fast) {
+    // Misaligned chunk: split evenly across the group with the byte path.
+    const uint64_t per = (uint64_t(bytes) + G - 1) / G;
+    const uint64_t b0 = per * j;
+    if (b0 < bytes) {
+      const uint64_t n = bytes - b0 < per ? bytes - b0 : per;
+      copy_generic(src + b0, store ? dst + b0 : nullptr, n, b0, store, do_csum, cs);
+    }
+    return true;
+  }
+  const uint32_t body = bytes & ~15u;
+  const uint32_t ntiles = (body + kTileBytes - 1) / kTileBytes;
+  if (!run_tiles(CopyGeom{src, store ? dst : nullptr, body}, ntiles, j, G, store, do_csum, q,
+                 bars, smem, cs, timeout_ns))
+    return false;
+  if (body != bytes && j == 0) {
+    copy_generic(src + body, store ? dst + body : nullptr, bytes - body, body, store, do_csum,
+                 cs);
+  }
+  return true;
+}
+
+// ---- bf16 -> fp8 e4m3 with one fp32 scale per 128x128 block ------------------
+// scale = amax / 448 (IEEE division, 1.0 for an all-zero block); q = e4m3(x /
+// scale) with round-to-nearest-even and saturation to +-448 (the hardware
+// cvt.rn.satfinite.e4m3x2.f32 conversion).  256 threads cover one block: two
+// threads per row, 64 columns (128 bytes) each.
+__device__ bool land_fp8_chunk(const LaneKernelParams& p, const ChunkDesc& c,
+                               const uint8_t* src, uint32_t j, uint32_t G, bool do_csum,
+                               Csum& cs, float* red) {
+  const QuantTensor T = p.tensors[c.tensor];
+  const uint32_t C = T.cols;
+  const uint32_t ncb = C / 128u;
+  const uint32_t row0 = c.unit0;
+  const uint64_t row_bytes = uint64_t(C) * 2u;
+  const uint32_t nrows = static_cast<uint32_t>(c.bytes / row_bytes);
+  const uint32_t nrb = (nrows + 127u) / 128u;
+  const uint32_t nblocks = nrb * ncb;
+  const uint32_t r = threadIdx.x >> 1;
+  const uint32_t half = threadIdx.x & 1u;
+  for (uint32_t b = j; b < nblocks; b += G) {
+    const uint32_t rb = b / ncb;
+    const uint32_t cb = b - rb * ncb;
+    const uint32_t row_local = rb * 128u + r;
+    const bool valid = row_local < nrows;
+    const uint64_t byte_off = uint64_t(row_local) * row_bytes + (uint64_t(cb) * 128u + half * 64u) * 2u;
+    uint4 v[8];
+    float amax = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = ld_cg_v4(src + byte_off + 16u * i);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (do_csum) csum_vec(cs, v[i], (byte_off >> 2) + 4u * i);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    float bmax = 0.f;
+    for (int w = 0; w < kLaneThreads / 32; ++w) bmax = fmaxf(bmax, red[w]);
+    __syncthreads();
+    const float scale = bmax > 0.f ? __fdiv_rn(bmax, 448.0f) : 1.0f;
+    if (valid) {
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[i]);
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const float2 f0 = __bfloat1622float2(h[e]);
+          const float2 f1 = __bfloat1622float2(h[e + 1]);
+          const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
+              make_float2(__fdiv_rn(f0.x, scale), __fdiv_rn(f0.y, scale)), __NV_SATFINITE,
+              __NV_E4M3);
+          const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+              make_float2(__fdiv_rn(f1.x, scale), __fdiv_rn(f1.y, scale)), __NV_SATFINITE,
+              __NV_E4M3);
+          packed[i * 2 + e / 2] = uint32_t(lo) | (uint32_t(hi) << 16);
+        }
+      }
+      uint8_t* qrow = T.q + uint64_t(row0 + row_local) * C + uint64_t(cb) * 128u + half * 64u;
+      uint4* qo = reinterpret_cast<uint4*>(qrow);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        qo[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+    }
+    if (threadIdx.x == 0) T.scales[uint64_t(row0 / 128u + rb) * ncb + cb] = scale;
+  }
+  return true;
+}
+
+// ---- landing kernel (H2D) -------------------------------------------------------
+
+__global__ void __launch_bounds__(kLaneThreads, 1) land_kernel(const LaneKernelParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(kStages) * kTileBytes);
+  __shared__ unsigned long long red[2 * (kLaneThreads / 32)];
+  __shared__ float fred[kLaneThreads / 32];
+  __shared__ int s_ok;
+
+  LaneDesc L;
+  const int lane = find_lane(p, L);
+  if (lane < 0) return;
+  const uint32_t j = blockIdx.x - L.cta_begin;
+  const uint32_t G = L.cta_count;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  uint32_t q = 0;
+  const bool do_csum = p.checksum != 0;
+
+  for (uint32_t ci = 0; ci < L.chunk_count; ++ci) {
+    const uint32_t cidx = L.chunk_begin + ci;
+    const ChunkDesc c = p.chunks[cidx];
+    if (threadIdx.x == 0) {
+      const bool ok = wait_flag_geq(L.ready, c.seq, globaltimer_ns() + p.timeout_ns);
+      if (ok) fence_proxy_async_global();
+      s_ok = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_ok) {
+      if (threadIdx.x == 0) {
+        record_error(p.status, kStatusReadyTimeout, lane, static_cast<int>(cidx), int(c.seq));
+        // Unblock the producer for every remaining chunk of this lane.
+        if (L.freec) st_release_sys(L.freec, c.seq + 0x40000000u);
+      }
+      return;
+    }
+    const uint8_t* src =
+        L.in_place ? (p.dev + c.dev_off) : (L.ring + uint64_t(c.slot) * L.slot_bytes);
+    const bool store = !L.in_place;
+    Csum cs{0ull, 0ull};
+    bool ok = true;
+    switch (p.op) {
+      case kOpCopy:
+        ok = move_contiguous(src, p.dev + c.dev_off, c.bytes, j, G, store, do_csum, q, bars, smem,
+                             cs, p.timeout_ns);
+        break;
+      case kOpScatterUnits: {
+        const uint32_t tpu = (p.unit_bytes + kTileBytes - 1) / kTileBytes;
+        const uint32_t nunits = c.bytes / p.unit_bytes;
+        ok = run_tiles(UnitGeom{src, nullptr, p.unit_addr + c.unit0, p.unit_bytes, tpu, true},
+                       nunits * tpu, j, G, store, do_csum, q, bars, smem, cs, p.timeout_ns);
+        break;
+      }
+      case kOpScatterRanges:
+        ok = run_tiles(RangeGeom{src, nullptr, p.range_addr + c.unit0, p.range_bytes + c.unit0,
+                                 p.range_pos + c.unit0, true},
+                       c.count, j, G, store, do_csum, q, bars, smem, cs, p.timeout_ns);
+        break;
+      case kOpFp8Quant:
+        ok = land_fp8_chunk(p, c, src, j, G, do_csum, cs, fred);
+        break;
+      default:
+        ok = false;
+    }
+    if (!ok) {
+      if (threadIdx.x == 0) {
+        record_error(p.status, p.op > kOpScatterRanges ? kStatusBadArgument : kStatusCopyTimeout,
+                     lane, static_cast<int>(cidx), int(c.seq));
+        if (L.freec) st_release_sys(L.freec, c.seq + 0x40000000u);
+      }
+      return;
+    }
+    if (do_csum) csum_block_commit(cs, p.csum + 2ull * cidx, red);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t old = G > 1 ? atom_add_acq_rel_gpu(p.done + cidx, 1u) : 0u;
+      if (old == G - 1 && L.freec) st_release_sys(L.freec, c.seq);
+    }
+  }
+  if (threadIdx.x == 0) bulk_wait_all<0>();
+}
+
+// ---- push kernel (D2H) ------------------------------------------------------------
+
+__global__ void __launch_bounds__(kLaneThreads, 1) push_kernel(const LaneKernelParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(kStages) * kTileBytes);
+  __shared__ unsigned long long red[2 * (kLaneThreads / 32)];
+  __shared__ int s_ok;
+
+  LaneDesc L;
+  const int lane = find_lane(p, L);
+  if (lane < 0) return;
+  const uint32_t j = blockIdx.x - L.cta_begin;
+  const uint32_t G = L.cta_count;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  uint32_t q = 0;
+  const bool do_csum = p.checksum != 0;
+
+  for (uint32_t ci = 0; ci < L.chunk_count; ++ci) {
+    const uint32_t cidx = L.chunk_begin + ci;
+    const ChunkDesc c = p.chunks[cidx];
+    if (!L.in_place) {
+      if (threadIdx.x == 0) {
+        s_ok = wait_flag_geq(L.freec, c.seq - L.slots, globaltimer_ns() + p.timeout_ns) ? 1 : 0;
+      }
+      __syncthreads();
+      if (!s_ok) {
+        if (threadIdx.x == 0) {
+          record_error(p.status, kStatusFreeTimeout, lane, static_cast<int>(cidx), int(c.seq));
+          st_release_sys(L.ready, c.seq + 0x40000000u);
+        }
+        return;
+      }
+    }
+    uint8_t* slot = L.in_place ? nullptr : (L.ring + uint64_t(c.slot) * L.slot_bytes);
+    const bool store = !L.in_place;
+    Csum cs{0ull, 0ull};
+    bool ok = true;
+    switch (p.op) {
+      case kOpCopy:
+        ok = move_contiguous(p.dev + c.dev_off, slot, c.bytes, j, G, store, do_csum, q, bars,
+                             smem, cs, p.timeout_ns);
+        break;
+      case kOpGatherUnits: {
+        const uint32_t tpu = (p.unit_bytes + kTileBytes - 1) / kTileBytes;
+        const uint32_t nunits = c.bytes / p.unit_bytes;
+        ok = run_tiles(UnitGeom{nullptr, slot, p.unit_addr + c.unit0, p.unit_bytes, tpu, false},
+                       nunits * tpu, j, G, store, do_csum, q, bars, smem, cs, p.timeout_ns);
+        break;
+      }
+      case kOpGatherRanges:
+        ok = run_tiles(RangeGeom{nullptr, slot, p.range_addr + c.unit0, p.range_bytes + c.unit0,
+                                 p.range_pos + c.unit0, false},
+                       c.count, j, G, store, do_csum, q, bars, smem, cs, p.timeout_ns);
+        break;
+      default:
+        ok = false;
+    }
+    if (!ok) {
+      if (threadIdx.x == 0) {
+        record_error(p.status, p.op == kOpCopy || p.op == kOpGatherUnits || p.op == kOpGatherRanges
+                                   ? kStatusCopyTimeout
+                                   : kStatusBadArgument,
+                     lane, static_cast<int>(cidx), int(c.seq));
+        if (!L.in_place) st_release_sys(L.ready, c.seq + 0x40000000u);
+      }
+      return;
+    }
+    if (do_csum) csum_block_commit(cs, p.csum + 2ull * cidx, red);
+    if (threadIdx.x == 0 && store) {
+      // Our bulk stores into the slot must be performed before the chunk is
+      // published to the copy engine of the relay.
+      bulk_wait_all<0>();
+      fence_proxy_async_global();
+      fence_sys();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t old = G > 1 ? atom_add_acq_rel_gpu(p.done + cidx, 1u) : 0u;
+      if (old == G - 1 && !L.in_place) st_release_sys(L.ready, c.seq);
+    }
+  }
+  if (threadIdx.x == 0) bulk_wait_all<0>();
+}
+
+bool g_attr_set[64] = {false};
+
+cudaError_t prepare_attrs() {
+  int dev = 0;
+  cudaError_t rc = cudaGetDevice(&dev);
+  if (rc != cudaSuccess) return rc;
+  if (dev >= 0 && dev < 64 && g_attr_set[dev]) return cudaSuccess;
+  rc = cudaFuncSetAttribute(land_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            static_cast<int>(kLaneSmemBytes));
+  if (rc != cudaSuccess) return rc;
+  rc = cudaFuncSetAttribute(push_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            static_cast<int>(kLaneSmemBytes));
+  if (rc != cudaSuccess) return rc;
+  if (dev >= 0 && dev < 64) g_attr_set[dev] = true;
+  return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t launch_land(const LaneKernelParams& p, int grid, cudaStream_t stream) {
+  cudaError_t rc = prepare_attrs();
+  if (rc != cudaSuccess) return rc;
+  land_kernel<<<grid, kLaneThreads, kLaneSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_push(const LaneKernelParams& p, int grid, cudaStream_t stream) {
+  cudaError_t rc = prepare_attrs();
+  if (rc != cudaSuccess) return rc;
+  push_kernel<<<grid, kLaneThreads, kLaneSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+int lane_kernel_max_ctas(int device) {
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  int per_sm = 0;
+  if (prepare_attrs() == cudaSuccess) {
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, land_kernel, kLaneThreads,
+                                                  kLaneSmemBytes);
+  }
+  cudaSetDevice(prev);
+  return per_sm * sms;
+}
+
+}  // namespace ppb
