@@ -1,1 +1,5 @@
-"""api"""
+"""Public client API."""
+
+from .client import DaemonIntentClient, TurboBusClient
+
+__all__ = ["DaemonIntentClient", "TurboBusClient"]

@@ -1,0 +1,139 @@
+"""CUDA backend: the native core (``pcie_pool_b200._C``) plus ``PoolRuntime``.
+
+Same facade as the reference's ``CudaNativeBackend``
+(turbobus/backends/cuda.py:9-172) so the worker and client layers stay
+backend-agnostic; a runtime here is a persistent ``PoolRuntime``.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Iterable
+
+from ..schema import TransferMode
+
+IPC_HANDLE_BYTES = 64
+
+
+class CudaNativeBackend:
+    def __init__(self, native_loader=None) -> None:
+        self._loader = native_loader
+
+    def _native(self):
+        if self._loader is not None:
+            return self._loader()
+        from .._native import native
+
+        return native()
+
+    def require_available(self) -> None:
+        self._native()
+
+    def require_torch(self) -> None:
+        import torch  # noqa: F401
+
+    def set_device(self, device_index: int) -> None:
+        d = int(device_index)
+        if d < 0:
+            raise ValueError("device_index must be non-negative")
+        self._native().set_device(d)
+
+    def transfer_mode_value(self, mode: TransferMode | str) -> TransferMode:
+        return TransferMode(mode)
+
+    def create_runtime(self, options: Any) -> Any:
+        from ..runtime_engine import PoolRuntime
+
+        self.require_available()
+        return PoolRuntime(options)
+
+    def initialize_runtime(self, runtime: Any, target_device: int, relay_gpus: Iterable[int]) -> None:
+        init = getattr(runtime, "init", None)
+        if not callable(init):
+            raise RuntimeError("runtime does not support initialization")
+        init(int(target_device), [int(g) for g in relay_gpus])
+
+    def make_ranges(self, ranges: Iterable, source_bytes: int, destination_bytes: int) -> list:
+        from ..runtime_engine import validate_ranges
+
+        return validate_ranges(ranges, source_bytes, destination_bytes)
+
+    def make_transfer_plan(self, plan: Any) -> Any:
+        from ..plan_trace import transfer_plan_to_dict, validate_plan_dict
+
+        d = transfer_plan_to_dict(plan)
+        validate_plan_dict(d)
+        return d
+
+    def register_host_memory(self, host_ptr: int, bytes_: int) -> None:
+        if int(host_ptr) <= 0:
+            raise ValueError("host_ptr must be positive")
+        if int(bytes_) <= 0:
+            raise ValueError("bytes must be positive")
+        self._native().host_register(int(host_ptr), int(bytes_))
+
+    def unregister_host_memory(self, host_ptr: int) -> None:
+        if int(host_ptr) <= 0:
+            raise ValueError("host_ptr must be positive")
+        self._native().host_unregister(int(host_ptr))
+
+    def export_device_ipc_handle(self, device_ptr: int) -> bytes:
+        if int(device_ptr) <= 0:
+            raise ValueError("device_ptr must be positive")
+        return ipc_handle_bytes(bytes(self._native().export_ipc_handle(int(device_ptr))))
+
+    def open_device_ipc_handle(self, cuda_ipc_handle: bytes | bytearray | str, device_index: int = 0) -> int:
+        ptr = int(self._native().open_ipc_handle(coerce_ipc_handle(cuda_ipc_handle), int(device_index)))
+        if ptr <= 0:
+            raise RuntimeError("native runtime returned an invalid CUDA IPC pointer")
+        return ptr
+
+    def close_device_ipc_handle(self, device_ptr: int) -> None:
+        if int(device_ptr) <= 0:
+            raise ValueError("device_ptr must be positive")
+        self._native().close_ipc_handle(int(device_ptr))
+
+    def fetch_plan_to_gpu(self, runtime, host_ptr, host_bytes, target_ptr, target_bytes, plan):
+        fn = getattr(runtime, "fetch_plan_to_gpu", None)
+        if not callable(fn):
+            raise RuntimeError("runtime does not support exact transfer plans")
+        return fn(host_ptr, host_bytes, target_ptr, target_bytes, plan)
+
+    def offload_plan_to_cpu(self, runtime, target_ptr, target_bytes, host_ptr, host_bytes, plan):
+        fn = getattr(runtime, "offload_plan_to_cpu", None)
+        if not callable(fn):
+            raise RuntimeError("runtime does not support exact transfer plans")
+        return fn(target_ptr, target_bytes, host_ptr, host_bytes, plan)
+
+    def wait(self, runtime, handle) -> None:
+        fn = getattr(runtime, "wait", None)
+        if not callable(fn):
+            raise RuntimeError("runtime does not support transfer waiting")
+        fn(handle)
+
+    def stats(self, runtime, handle):
+        fn = getattr(runtime, "stats", None)
+        if not callable(fn):
+            raise RuntimeError("runtime does not support transfer stats")
+        return fn(handle)
+
+
+def coerce_ipc_handle(handle: bytes | bytearray | str) -> bytes:
+    if isinstance(handle, str):
+        try:
+            return ipc_handle_bytes(bytes.fromhex(handle))
+        except ValueError as exc:
+            if "64 bytes" in str(exc):
+                raise
+            raise ValueError("cuda_ipc_handle string must be hex encoded") from exc
+    return ipc_handle_bytes(bytes(handle))
+
+
+def ipc_handle_bytes(handle: bytes) -> bytes:
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError("cuda_ipc_handle must be 64 bytes")
+    return handle
+
+
+default_cuda_backend = CudaNativeBackend()
+
+__all__ = ["CudaNativeBackend", "coerce_ipc_handle", "default_cuda_backend"]

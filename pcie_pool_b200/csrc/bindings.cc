@@ -95,6 +95,7 @@ PYBIND11_MODULE(_C, m) {
       .def_readwrite("slot_bytes", &EngineOptions::slot_bytes)
       .def_readwrite("slots", &EngineOptions::slots)
       .def_readwrite("ctas_per_lane", &EngineOptions::ctas_per_lane)
+      .def_readwrite("coalesce_bytes", &EngineOptions::coalesce_bytes)
       .def_readwrite("timeout_s", &EngineOptions::timeout_s)
       .def_readwrite("enable_peer_access", &EngineOptions::enable_peer_access);
 

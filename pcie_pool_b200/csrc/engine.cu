@@ -602,6 +602,33 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
       next[li] = k + 1;
       const auto& c = L.chunks[k];
       DeviceGuard lg(R.device);
+      if (!R.staged) {
+        // Plain direct lane: merge chunks that are contiguous on both sides
+        // into one copy-engine transfer (up to coalesce_bytes) and publish
+        // the last chunk's sequence number once for the whole group.
+        size_t end = k + 1;
+        uint64_t run = c.bytes;
+        while (end < L.chunks.size()) {
+          const auto& nx = L.chunks[end];
+          const auto& pv = L.chunks[end - 1];
+          if (nx.src_off != pv.src_off + pv.bytes || nx.dst_off != pv.dst_off + pv.bytes ||
+              run + nx.bytes > options_.coalesce_bytes)
+            break;
+          run += nx.bytes;
+          ++end;
+        }
+        next[li] = end;
+        const uint32_t last_seq = R.ring ? static_cast<uint32_t>(R.seq0 + end) : 0u;
+        const bool pub = static_cast<int>(li) != s.debug_drop_publish;
+        if (h2d) {
+          PPB_CUDA(cudaMemcpyAsync(devp + c.dst_off, host + c.src_off, run, cudaMemcpyHostToDevice, R.stream));
+          if (R.in_place && pub) stream_write(R.stream, R.ring->ready, last_seq);
+        } else {
+          PPB_CUDA(cudaMemcpyAsync(const_cast<uint8_t*>(host) + c.dst_off, devp + c.src_off, run,
+                                   cudaMemcpyDeviceToHost, R.stream));
+        }
+        continue;
+      }
       const uint32_t seq = R.ring ? static_cast<uint32_t>(R.seq0 + k + 1) : 0u;
       uint8_t* slot = R.staged ? R.ring->base + ((R.seq0 + k) % options_.slots) * options_.slot_bytes : nullptr;
       const bool publish = static_cast<int>(li) != s.debug_drop_publish;

@@ -37,7 +37,8 @@ namespace ppb {
 struct EngineOptions {
   uint64_t slot_bytes = 16ull << 20;
   int slots = 3;
-  int ctas_per_lane = 2;
+  int ctas_per_lane = 4;
+  uint64_t coalesce_bytes = 64ull << 20;  // max merged plain direct-lane copy
   double timeout_s = 10.0;  // device-side bound on every wait of a lane kernel
   bool enable_peer_access = true;
 };

@@ -1,0 +1,177 @@
+"""Executes admitted intents: the piece the reference's daemon lacks (its
+SUBMIT_TRANSFER_INTENT plans, issues a ticket and returns; nothing consumes
+the ticket).
+
+``IntentExecutor`` runs each admitted ticket on a ``DataPlane`` in a worker
+thread, outside the daemon lock, and reports RUNNING / COMPLETE / FAILED with
+measured per-lane statistics back to the daemon.  Data planes:
+
+* ``EngineDataPlane`` - the native PoolEngine on real GPUs; resolves buffer
+  registrations (shared pinned host memory by shm name, CUDA IPC device
+  handles, or in-process addresses) and moves the plan's chunks through the
+  direct + relay lanes with the fused landing kernel (checksum on);
+* ``mock.MockDataPlane`` - a simulated node on the CPU (tests, config 1).
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+import traceback
+from concurrent.futures import ThreadPoolExecutor
+from dataclasses import dataclass, field
+from typing import Any, Protocol
+
+from ..schema import BufferRegistration, ExecutionTicket, TransferIntent
+
+
+@dataclass
+class ExecutionResult:
+    ok: bool
+    bytes_completed: int
+    error: str | None = None
+    measured: dict[str, Any] = field(default_factory=dict)
+
+
+class DataPlane(Protocol):
+    def execute(self, ticket: ExecutionTicket, src: BufferRegistration, dst: BufferRegistration,
+                intent: TransferIntent | None) -> ExecutionResult:
+        ...
+
+
+class IntentExecutor:
+    """Thread-pool executor bound to one daemon."""
+
+    def __init__(self, data_plane: DataPlane, max_workers: int = 4) -> None:
+        self.data_plane = data_plane
+        self._pool = ThreadPoolExecutor(max_workers=max_workers, thread_name_prefix="pcie-pool-exec")
+        self._canceled: set[str] = set()
+        self._lock = threading.Lock()
+        self.completed: list[str] = []
+
+    def bind(self, daemon) -> None:
+        self._daemon = daemon
+
+    def submit(self, daemon, transfer_id: str, ticket: ExecutionTicket, src: BufferRegistration | None,
+               dst: BufferRegistration | None, intent: TransferIntent | None) -> None:
+        self._pool.submit(self._run, daemon, transfer_id, ticket, src, dst, intent)
+
+    def cancel(self, transfer_id: str) -> None:
+        with self._lock:
+            self._canceled.add(transfer_id)
+
+    def _run(self, daemon, tid: str, ticket: ExecutionTicket, src, dst, intent) -> None:
+        with self._lock:
+            if tid in self._canceled:
+                return
+        daemon.executor_started(tid)
+        t0 = time.perf_counter()
+        try:
+            if src is None or dst is None:
+                raise RuntimeError("ticket buffers are no longer registered")
+            res = self.data_plane.execute(ticket, src, dst, intent)
+        except Exception as exc:  # noqa: BLE001 - every data-plane error fails the transfer
+            res = ExecutionResult(ok=False, bytes_completed=0,
+                                  error=f"{type(exc).__name__}: {exc}",
+                                  measured={"traceback": traceback.format_exc(limit=5)})
+        res.measured.setdefault("host_ms", (time.perf_counter() - t0) * 1e3)
+        daemon.executor_finished(tid, ok_=res.ok, bytes_completed=res.bytes_completed, error=res.error,
+                                 measured=res.measured)
+        with self._lock:
+            self.completed.append(tid)
+
+    def shutdown(self, wait: bool = True) -> None:
+        self._pool.shutdown(wait=wait)
+
+
+class EngineDataPlane:
+    """Runs tickets on the native PoolEngine (all GPUs of the node)."""
+
+    def __init__(self, engine=None, devices=None, *, checksum: bool = True, **engine_kw) -> None:
+        self._engine = engine
+        self._devices = devices
+        self._engine_kw = engine_kw
+        self.checksum = checksum
+        self._host_maps: dict[str, tuple[Any, int]] = {}
+        self._ipc: dict[str, int] = {}
+        self._lock = threading.Lock()
+
+    @property
+    def engine(self):
+        if self._engine is None:
+            from ..parallel.engine import PoolEngine
+
+            if self._devices is None:
+                import torch
+
+                self._devices = list(range(torch.cuda.device_count()))
+            self._engine = PoolEngine(self._devices, **self._engine_kw)
+        return self._engine
+
+    # -- buffer resolution ------------------------------------------------------------------
+    def host_pointer(self, buf: BufferRegistration) -> int:
+        if buf.handle_type == "shared_pinned_cpu":
+            name = str(buf.metadata["shared_memory_name"])
+            with self._lock:
+                if name not in self._host_maps:
+                    from multiprocessing import shared_memory
+
+                    from .._native import native
+
+                    shm = shared_memory.SharedMemory(name=name)
+                    import numpy as np
+
+                    base = np.frombuffer(shm.buf, dtype=np.uint8).ctypes.data
+                    if not native().is_pinned(base):
+                        native().host_register(base, shm.size)
+                    self._host_maps[name] = (shm, base)
+                _shm, base = self._host_maps[name]
+            return base + int(buf.metadata["offset_bytes"])
+        if buf.address is None:
+            raise ValueError(f"buffer {buf.buffer_id} has no host address")
+        return int(buf.address)
+
+    def device_pointer(self, buf: BufferRegistration) -> int:
+        if buf.handle_type == "cuda_ipc_device":
+            h = str(buf.metadata["cuda_ipc_handle"])
+            with self._lock:
+                if h not in self._ipc:
+                    from .._native import native
+
+                    self._ipc[h] = native().open_ipc_handle(bytes.fromhex(h), int(buf.device_index or 0))
+                return self._ipc[h]
+        if buf.address is None:
+            raise ValueError(f"buffer {buf.buffer_id} has no device address")
+        return int(buf.address)
+
+    # -- execution ------------------------------------------------------------------------------
+    def execute(self, ticket: ExecutionTicket, src: BufferRegistration, dst: BufferRegistration,
+                intent: TransferIntent | None) -> ExecutionResult:
+        from ..parallel.engine import D2H, H2D, lanes_from_plan
+
+        h2d = ticket.direction == "h2d"
+        host_buf, dev_buf = (src, dst) if h2d else (dst, src)
+        target = int(dev_buf.device_index or 0)
+        host_ptr = self.host_pointer(host_buf)
+        dev_ptr = self.device_pointer(dev_buf)
+        lanes = lanes_from_plan(ticket.plan, target)
+        eng = self.engine
+        r = eng.run(H2D if h2d else D2H, target, host_ptr, host_buf.size_bytes, dev_ptr, dev_buf.size_bytes,
+                    lanes, checksum=self.checksum)
+        measured = {
+            "cuda_ms": r.cuda_ms, "gib_per_s": r.gib_per_s, "gb_per_s": r.gb_per_s,
+            "submit_to_complete_ms": r.submit_to_complete_ms,
+            "path_stats": [{"kind": "direct" if l.direct else "relay", "direction": ticket.direction,
+                            "target_device": target, "relay_device": -1 if l.direct else l.device,
+                            "bytes": int(l.bytes), "chunk_count": int(l.chunks),
+                            "cuda_ms": float(l.cuda_ms),
+                            "gib_per_second": (l.bytes / (1 << 30)) / (l.cuda_ms / 1e3) if l.cuda_ms > 0 else 0.0}
+                           for l in r.lanes],
+        }
+        if self.checksum and r.checksums is not None and r.checksums.size:
+            measured["chunk_checksums"] = [[int(a), int(b)] for a, b in r.checksums]
+        return ExecutionResult(ok=r.ok, bytes_completed=r.bytes if r.ok else 0,
+                               error=None if r.ok else r.error, measured=measured)
+
+
+__all__ = ["DataPlane", "EngineDataPlane", "ExecutionResult", "IntentExecutor"]

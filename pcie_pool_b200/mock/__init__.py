@@ -1,1 +1,167 @@
-"""mock"""
+"""A simulated node for CPU-only runs: N "GPUs" whose memory is host memory,
+lanes that are threads, and a data plane with the engine's contract.
+
+Used for BASELINE config 1 (daemon + planner + client end to end on a world
+of 4 simulated GPUs), for host-side fault injection (a lane that raises,
+stalls past a deadline or corrupts a chunk) and by the tests.  Every chunk's
+lane assignment is recorded so a run can prove each chunk moved exactly once
+on the lane the plan chose.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import Any, Callable
+
+import numpy as np
+
+from ..daemon.executor import ExecutionResult
+from ..schema import BufferRegistration, ExecutionTicket, TransferIntent
+from ..utils.checksum import checksum_bytes
+
+
+class MockLaneError(RuntimeError):
+    pass
+
+
+@dataclass
+class FaultPlan:
+    """Host-side fault injection for the mock lanes."""
+
+    fail_lane: int | None = None       # lane device that raises on its first chunk
+    stall_lane: int | None = None      # lane device that sleeps stall_seconds per chunk
+    stall_seconds: float = 0.0
+    corrupt_lane: int | None = None    # lane device that flips one byte in its first chunk
+    deadline_seconds: float = 30.0     # per-transfer watchdog
+
+
+@dataclass
+class MockWorld:
+    """``gpu_count`` simulated devices, each with a bandwidth (GiB/s) used only
+    to report modelled lane times."""
+
+    gpu_count: int = 4
+    lane_gibps: float = 50.0
+    p2p_gibps: float = 600.0
+    memory: dict[int, dict[int, np.ndarray]] = field(default_factory=dict)
+
+    def alloc(self, device: int, nbytes: int) -> np.ndarray:
+        """Device memory of a simulated GPU (host bytes), kept alive here."""
+        if not 0 <= device < self.gpu_count:
+            raise ValueError("device index out of range")
+        arr = np.zeros(nbytes, dtype=np.uint8)
+        self.memory.setdefault(device, {})[arr.ctypes.data] = arr
+        return arr
+
+    def profile(self, target: int = 0) -> dict[str, Any]:
+        """A daemon profile entry for this world (GiB/s)."""
+        return {"target_device": target, "direct_h2d_bw_gbps": self.lane_gibps,
+                "direct_d2h_bw_gbps": self.lane_gibps,
+                "relays": [{"relay_device": g, "target_device": target, "h2d_bw_gbps": self.lane_gibps,
+                            "d2h_bw_gbps": self.lane_gibps, "p2p_bw_gbps": self.p2p_gibps,
+                            "effective_bw_gbps": self.lane_gibps, "effective_d2h_bw_gbps": self.lane_gibps,
+                            "p2p_enabled": True} for g in range(self.gpu_count) if g != target]}
+
+
+class MockDataPlane:
+    """Moves the bytes of a ticket's plan between in-process buffers, one
+    thread per lane, honouring the plan's chunk-to-lane assignment."""
+
+    def __init__(self, world: MockWorld | None = None, faults: FaultPlan | None = None,
+                 checksum: bool = True) -> None:
+        self.world = world or MockWorld()
+        self.faults = faults or FaultPlan()
+        self.checksum = checksum
+        self.trace: list[dict[str, Any]] = []
+        self._lock = threading.Lock()
+
+    def execute(self, ticket: ExecutionTicket, src: BufferRegistration, dst: BufferRegistration,
+                intent: TransferIntent | None) -> ExecutionResult:
+        if src.address is None or dst.address is None:
+            raise MockLaneError("mock data plane needs in-process buffer addresses")
+        plan = ticket.plan
+        lanes = []
+        for asg in plan.get("assignments", []) or []:
+            p = asg["path"]
+            dev = int(p["target_device"]) if p["kind"] == "direct" else int(p["relay_device"])
+            lanes.append((dev, p["kind"], [(int(c["src_offset"]), int(c["dst_offset"]), int(c["bytes"]))
+                                            for c in asg.get("chunks", []) or []]))
+        return self.run_lanes(ticket.direction, int(src.address), int(src.size_bytes),
+                              int(dst.address), int(dst.size_bytes), lanes,
+                              transfer_id=str(ticket.metadata.get("transfer_id", ticket.ticket_id)))
+
+    def run_lanes(self, direction: str, src: int, src_bytes: int, dst: int, dst_bytes: int,
+                  lanes: list[tuple[int, str, list[tuple[int, int, int]]]],
+                  transfer_id: str = "") -> ExecutionResult:
+        f = self.faults
+        results: dict[int, dict[str, Any]] = {}
+        errors: list[str] = []
+        sums: dict[tuple[int, int], tuple[int, int]] = {}
+
+        def lane_worker(idx: int, dev: int, kind: str, chunks: list[tuple[int, int, int]]) -> None:
+            t0 = time.perf_counter()
+            moved = 0
+            for k, (so, do, n) in enumerate(chunks):
+                if so < 0 or do < 0 or so + n > src_bytes or do + n > dst_bytes:
+                    errors.append(f"lane {dev}: chunk {k} out of bounds")
+                    return
+                if f.fail_lane == dev:
+                    errors.append(f"lane {dev}: injected failure")
+                    return
+                if f.stall_lane == dev and f.stall_seconds:
+                    time.sleep(f.stall_seconds)
+                if time.perf_counter() - t0 > f.deadline_seconds:
+                    errors.append(f"lane {dev}: deadline exceeded")
+                    return
+                ctypes.memmove(dst + do, src + so, n)
+                if f.corrupt_lane == dev and k == 0:
+                    b = ctypes.c_uint8.from_address(dst + do)
+                    b.value ^= 0xFF
+                if self.checksum:
+                    landed = np.ctypeslib.as_array((ctypes.c_uint8 * n).from_address(dst + do))
+                    sent = np.ctypeslib.as_array((ctypes.c_uint8 * n).from_address(src + so))
+                    sums[(idx, k)] = checksum_bytes(landed)
+                    if checksum_bytes(sent) != sums[(idx, k)]:
+                        errors.append(f"lane {dev}: checksum mismatch on chunk {k}")
+                        return
+                moved += n
+                with self._lock:
+                    self.trace.append({"transfer_id": transfer_id, "lane": dev, "kind": kind,
+                                       "src_offset": so, "dst_offset": do, "bytes": n})
+            results[idx] = {"device": dev, "kind": kind, "bytes": moved, "chunks": len(chunks),
+                            "host_ms": (time.perf_counter() - t0) * 1e3}
+
+        ths = [threading.Thread(target=lane_worker, args=(i, d, k, c)) for i, (d, k, c) in enumerate(lanes)]
+        t0 = time.perf_counter()
+        for t in ths:
+            t.start()
+        for t in ths:
+            t.join(timeout=f.deadline_seconds + 5)
+        host_ms = (time.perf_counter() - t0) * 1e3
+        total = sum(r["bytes"] for r in results.values())
+        gib = self.world.lane_gibps
+        path_stats = [{"kind": r["kind"], "direction": direction,
+                       "relay_device": -1 if r["kind"] == "direct" else r["device"],
+                       "bytes": r["bytes"], "chunk_count": r["chunks"],
+                       "model_ms": r["bytes"] / (gib * (1 << 30)) * 1e3, "host_ms": r["host_ms"]}
+                      for _, r in sorted(results.items())]
+        measured = {"host_ms": host_ms, "path_stats": path_stats, "simulated": True}
+        if errors:
+            return ExecutionResult(ok=False, bytes_completed=total, error="; ".join(errors), measured=measured)
+        return ExecutionResult(ok=True, bytes_completed=total, measured=measured)
+
+
+def chunk_lane_map(trace: list[dict[str, Any]]) -> dict[int, int]:
+    """src_offset -> lane for every traced chunk (raises if a chunk moved twice)."""
+    out: dict[int, int] = {}
+    for rec in trace:
+        if rec["src_offset"] in out:
+            raise AssertionError(f"chunk at {rec['src_offset']} moved twice")
+        out[rec["src_offset"]] = rec["lane"]
+    return out
+
+
+__all__ = ["FaultPlan", "MockDataPlane", "MockLaneError", "MockWorld", "chunk_lane_map"]

@@ -105,8 +105,8 @@ class PoolEngine:
     """Persistent multi-GPU data plane (one per process)."""
 
     def __init__(self, devices: Sequence[int], slot_bytes: int = 16 << 20, slots: int = 3,
-                 ctas_per_lane: int = 2, timeout_s: float = 10.0,
-                 enable_peer_access: bool = True) -> None:
+                 ctas_per_lane: int = 4, timeout_s: float = 10.0,
+                 enable_peer_access: bool = True, coalesce_bytes: int = 64 << 20) -> None:
         C = native()
         opt = C.EngineOptions()
         opt.slot_bytes = int(slot_bytes)
@@ -114,6 +114,7 @@ class PoolEngine:
         opt.ctas_per_lane = int(ctas_per_lane)
         opt.timeout_s = float(timeout_s)
         opt.enable_peer_access = bool(enable_peer_access)
+        opt.coalesce_bytes = int(coalesce_bytes)
         self._C = C
         self._eng = C.PoolEngine(list(int(d) for d in devices), opt)
         self.devices = list(int(d) for d in devices)

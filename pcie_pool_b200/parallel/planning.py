@@ -1,6 +1,15 @@
-"""Lane planning for the data plane: split a transfer into chunks and assign
-them to lanes with the native earliest-finish policy (or evenly when no
-bandwidth profile is known)."""
+"""Lane planning for the data plane: split a transfer into chunks and give
+each lane a share proportional to its bandwidth.
+
+Two layouts:
+  * ``blocked`` (default) - each lane streams one contiguous span of the
+    buffer, so plain direct-lane chunks merge into large copy-engine
+    transfers;
+  * ``interleaved`` - chunk i goes to the lane the assignment loop picks
+    (round robin without a profile).
+Chunk counts per lane come from the native earliest-finish assignment when a
+bandwidth profile is given.
+"""
 
 from __future__ import annotations
 
@@ -32,17 +41,22 @@ def assign(sizes: np.ndarray, bw_gibps: Sequence[float], latency_s: Sequence[flo
 def plan_lanes(total: int, chunk: int, devices: Sequence[int], target: int,
                bw_gibps: Sequence[float] | None = None, latency_s: Sequence[float] = (),
                policy: str = "earliest_finish", src_start: int = 0,
-               dst_start: int = 0) -> list[Lane]:
+               dst_start: int = 0, layout: str = "blocked") -> list[Lane]:
     """Chunk [0, total) and spread the chunks over the lanes of ``devices``
     (``target`` is the direct lane).  Without a profile every lane is assumed
-    equally fast and chunks go round-robin, interleaved so every lane streams
-    from across the whole buffer."""
+    equally fast."""
+    if layout not in ("blocked", "interleaved"):
+        raise ValueError("layout must be 'blocked' or 'interleaved'")
     offs, sizes = chunk_offsets(total, chunk)
     devs = list(devices)
     if bw_gibps is None:
         idx = np.arange(offs.size) % len(devs)
     else:
         idx = assign(sizes, bw_gibps, latency_s, policy)
+    if layout == "blocked":
+        # same per-lane chunk counts, contiguous spans in lane order
+        counts = np.bincount(idx, minlength=len(devs))
+        idx = np.repeat(np.arange(len(devs)), counts)
     lanes = []
     for li, dev in enumerate(devs):
         sel = idx == li
@@ -50,6 +64,5 @@ def plan_lanes(total: int, chunk: int, devices: Sequence[int], target: int,
             continue
         lanes.append(Lane(int(dev), offs[sel] + np.uint64(src_start),
                           offs[sel] + np.uint64(dst_start), sizes[sel].copy()))
-    # direct lane first for readability of stats
     lanes.sort(key=lambda l: (l.device != target, l.device))
     return lanes

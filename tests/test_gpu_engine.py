@@ -195,10 +195,10 @@ def test_ranges_unpack_and_pack(need_gpu):
     rng = np.random.default_rng(9)
     sizes = (rng.integers(1, 2048, size=40) * 16).astype(np.uint32)  # <= 32 KiB each
     total = int(sizes.sum())
-    dst = torch.zeros(total * 2, dtype=torch.uint8, device="cuda:0")
-    # each range lands at a shuffled, 16-aligned offset
+    # each range lands in its own shuffled 32 KiB slot (16-aligned start)
+    dst = torch.zeros(40 * 32768, dtype=torch.uint8, device="cuda:0")
     slots = rng.permutation(40)
-    offs = np.concatenate([[0], np.cumsum(sizes.astype(np.int64) * 2)[:-1]])
+    offs = np.arange(40, dtype=np.int64) * 32768
     addrs = (dst.data_ptr() + offs[slots]).astype(np.uint64)
     # two chunks: first 25 ranges, then 15
     pos = np.zeros(40, np.uint64)
