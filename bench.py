@@ -44,7 +44,7 @@ def parse_args(argv=None):
     p.add_argument("--bytes", type=int, default=4 << 30)
     p.add_argument("--chunk", type=int, default=16 << 20)
     p.add_argument("--slots", type=int, default=3)
-    p.add_argument("--ctas", type=int, default=2, help="lane-kernel CTAs per lane")
+    p.add_argument("--ctas", type=int, default=4, help="lane-kernel CTAs per lane")
     p.add_argument("--direction", choices=["h2d", "d2h"], default="h2d")
     p.add_argument("--no-checksum", action="store_true", help="skip the fused per-chunk checksum")
     p.add_argument("--no-e2e", action="store_true")
@@ -206,19 +206,41 @@ def run_ours(args, dist: Dist) -> dict:
             dev.copy_(torch.from_numpy(host.numpy()).to("cuda:0"))
         eng = PoolEngine(devices, slot_bytes=max(args.chunk, 1 << 20), slots=args.slots,
                          ctas_per_lane=args.ctas, timeout_s=20.0)
-        lanes = plan_lanes(n, args.chunk, devices, target=0)
         direction = H2D if args.direction == "h2d" else D2H
+        dname = args.direction
         checksum = not args.no_checksum
         kernel_per_step = 1 if (checksum or N > 1) else 0
+        # Calibration (outside the timed region): the link probe measures the
+        # lanes solo and together and picks the lane set with the highest
+        # aggregate; warm-up steps then refine the per-lane weights.
+        profile = None
+        lane_set, weights = devices, None
+        if N > 1:
+            from pcie_pool_b200.parallel.linkprobe import concurrent_lane_plan, probe_profile
 
-        def step():
-            r = eng.run(direction, 0, host.ptr, n, dev.data_ptr(), n, lanes, checksum=checksum)
+            profile = probe_profile(eng, 0, devices[1:], nbytes=min(n, 1 << 30), chunk=args.chunk)
+            picked = concurrent_lane_plan(profile, dname)
+            if picked is not None:
+                lane_set, weights = picked
+        from pcie_pool_b200.parallel.balance import LaneBalancer
+
+        balancer = LaneBalancer(alpha=0.5)
+        if weights is not None:
+            balancer.seed(0, dname, dict(zip(lane_set, weights)))
+        state = {"lanes": plan_lanes(n, args.chunk, lane_set, target=0, bw_gibps=weights)}
+
+        def step(adapt: bool = False):
+            r = eng.run(direction, 0, host.ptr, n, dev.data_ptr(), n, state["lanes"], checksum=checksum)
             if not r.ok:
                 raise RuntimeError(r.error)
+            if adapt and len(lane_set) > 1:
+                balancer.observe(0, dname, r)
+                w = balancer.weights(0, dname, lane_set)
+                state["lanes"] = plan_lanes(n, args.chunk, lane_set, target=0, bw_gibps=w)
             return r
 
         for _ in range(args.warmup):
-            step()
+            step(adapt=True)
     dist.barrier()
     res = None
     elapsed_ms = 0.0
@@ -239,6 +261,7 @@ def run_ours(args, dist: Dist) -> dict:
     elapsed_ms = dist.max(elapsed_ms)
     if dist.rank == 0:
         verified = None
+        lanes = state["lanes"]
         if checksum and direction == H2D:
             C = __import__("pcie_pool_b200._C", fromlist=["x"])
             host_sum = C.checksum_host(host.ptr, n)
@@ -251,10 +274,14 @@ def run_ours(args, dist: Dist) -> dict:
             "verified": verified,
             "gpu_launches": kernel_per_step * args.steps,
             "transfer_cuda_ms": res.cuda_ms,
+            "lane_set": list(lane_set),
+            "probe": None if profile is None else profile.get("concurrent"),
         }
-        if not args.no_e2e:
+        if not args.no_e2e and direction == H2D:
             try:
-                out["e2e"] = run_e2e(args, eng, host, dev, lanes)
+                from pcie_pool_b200.e2e import public_api_pooled_load
+
+                out["e2e"] = public_api_pooled_load(args, eng, host, dev, profile)
             except Exception as exc:  # pragma: no cover - reported in the JSON line
                 out["e2e"] = {"error": f"{type(exc).__name__}: {exc}"}
         del eng
@@ -273,14 +300,6 @@ def _shift_chunk_sums(res, lanes):
             out.append((a, (w + (int(s) // 4) * a) & (2**64 - 1)))
             i += 1
     return out
-
-
-def run_e2e(args, eng, host, dev, lanes) -> dict:
-    """Same metric through the public client API (TurboBusClient -> daemon ->
-    executor -> engine), inputs from the pinned host store, result read back."""
-    from pcie_pool_b200.e2e import public_api_pooled_load
-
-    return public_api_pooled_load(args, eng, host, dev)
 
 
 # ---- reference implementation -----------------------------------------------------------
@@ -409,6 +428,8 @@ def main(argv=None) -> int:
                 line["profile"] = res.get("profile")
             else:
                 line["impl"] = "ours"
+                line["lane_set"] = res.get("lane_set")
+                line["probe"] = res.get("probe")
                 if "e2e" in res:
                     line["e2e"] = res["e2e"]
         s = json.dumps(line)

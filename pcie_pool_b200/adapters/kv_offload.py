@@ -1,0 +1,139 @@
+"""Paged-KV save / restore on the pooled data plane.
+
+A request's KV prefix (every layer, K and V, ``n`` blocks) is saved to one
+page-locked host region laid out ``[layer][lane][block index]`` -- per layer
+exactly the reference connector's CPU slot order ``start + lane*n + index``
+(turbobus/adapters/vllm_kv_connector.py:189-208).  Saving is ONE device->host
+transfer whose push kernel gathers every block through the request's block
+table; restoring is ONE host->device transfer whose landing kernel scatters
+host-contiguous chunks into the (permuted) block table.  The reference moves
+each 32 KiB block lane as a separate range and chunk (131,072 per 32k-token
+request when the block table is permuted).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Sequence
+
+import numpy as np
+
+from .vllm import block_table_units
+
+
+@dataclass
+class KVTransferStats:
+    bytes: int
+    units: int
+    cuda_ms: float
+    gb_per_s: float
+    lanes: list
+
+
+class PagedKVOffloader:
+    """Save / restore vLLM-layout KV prefixes through a ``PoolEngine``."""
+
+    def __init__(self, engine, kv_caches: Sequence, target: int, relays: Sequence[int] = (),
+                 units_per_chunk: int = 128, checksum: bool = True, balancer=None) -> None:
+        self.engine = engine
+        self.kv_caches = list(kv_caches)
+        if not self.kv_caches:
+            raise ValueError("at least one KV cache tensor is required")
+        self.target = int(target)
+        self.relays = [int(r) for r in relays if int(r) != int(target)]
+        self.units_per_chunk = int(units_per_chunk)
+        self.checksum = checksum
+        self.balancer = balancer
+        _addrs, self.unit_bytes = block_table_units(self.kv_caches[:1], [0])
+        lanes = int(self.kv_caches[0].shape[0]) if len(self.kv_caches[0].shape) >= 3 else 1
+        self.units_per_block = lanes * len(self.kv_caches)
+
+    def prefix_bytes(self, block_count: int) -> int:
+        return int(block_count) * self.units_per_block * self.unit_bytes
+
+    def _segments(self, nunits: int, host_off: int, span_blocks: int | None, nblocks: int):
+        """(host offset, first unit, unit count) runs.  With ``span_blocks``
+        larger than the request the host region keeps ``span_blocks`` slots
+        per (layer, lane) and only the first ``nblocks`` of each move."""
+        if span_blocks is None or span_blocks == nblocks:
+            return [(host_off, 0, nunits)]
+        if span_blocks < nblocks:
+            raise ValueError("span_blocks must be >= the number of blocks moved")
+        spans = nunits // max(1, nblocks)
+        return [(host_off + s * span_blocks * self.unit_bytes, s * nblocks, nblocks) for s in range(spans)]
+
+    def _lanes(self, segments, direction: str, h2d: bool):
+        from ..parallel.engine import Lane
+
+        devices = [self.target, *self.relays]
+        hs, us, cs = [], [], []
+        for hoff, u0, n in segments:
+            st = np.arange(0, n, self.units_per_chunk, dtype=np.int64)
+            hs.append(hoff + st * self.unit_bytes)
+            us.append(u0 + st)
+            cs.append(np.minimum(self.units_per_chunk, n - st))
+        host_offs, starts, counts = np.concatenate(hs), np.concatenate(us), np.concatenate(cs)
+        if len(devices) == 1:
+            idx = np.zeros(starts.size, dtype=np.int64)
+        else:
+            w = None if self.balancer is None else self.balancer.weights(self.target, direction, devices)
+            if w is None:
+                idx = np.arange(starts.size) % len(devices)
+            else:
+                from ..parallel.planning import assign
+
+                idx = assign((counts * self.unit_bytes).astype(np.uint64), w)
+            # contiguous span per lane keeps each lane's host reads sequential
+            n_per = np.bincount(idx, minlength=len(devices))
+            idx = np.repeat(np.arange(len(devices)), n_per)
+        lanes = []
+        for li, dev in enumerate(devices):
+            sel = idx == li
+            if not np.any(sel):
+                continue
+            host = host_offs[sel].astype(np.uint64)
+            nbytes = (counts[sel] * self.unit_bytes).astype(np.uint64)
+            zeros = np.zeros(host.size, dtype=np.uint64)
+            u0 = starts[sel].astype(np.uint32)
+            lanes.append(Lane(dev, host, zeros, nbytes, unit0=u0) if h2d else Lane(dev, zeros, host, nbytes, unit0=u0))
+        return lanes
+
+    def _run(self, h2d: bool, block_ids: Sequence[int], host_ptr: int, host_bytes: int,
+             host_off: int = 0, span_blocks: int | None = None) -> KVTransferStats:
+        from .._native import native
+        from ..parallel.engine import D2H, H2D
+
+        C = native()
+        addrs, unit = block_table_units(self.kv_caches, block_ids)
+        nunits = int(addrs.size)
+        nblocks = len(block_ids)
+        segs = self._segments(nunits, host_off, span_blocks, nblocks)
+        need = max(h + n * unit for h, _, n in segs)
+        if need > host_bytes:
+            raise ValueError("host backing is smaller than the KV prefix")
+        direction = "h2d" if h2d else "d2h"
+        lanes = self._lanes(segs, direction, h2d)
+        kv0 = self.kv_caches[0]
+        r = self.engine.run(H2D if h2d else D2H, self.target, host_ptr, host_bytes, kv0.data_ptr(),
+                            kv0.numel() * kv0.element_size(), lanes,
+                            op=C.OP_SCATTER_UNITS if h2d else C.OP_GATHER_UNITS, checksum=self.checksum,
+                            unit_bytes=unit, unit_addrs=addrs)
+        r.raise_for_status()
+        if self.balancer is not None:
+            self.balancer.observe(self.target, direction, r)
+        return KVTransferStats(bytes=r.bytes, units=nunits, cuda_ms=r.cuda_ms, gb_per_s=r.gb_per_s,
+                               lanes=[(l.device, l.bytes, round(l.cuda_ms, 3)) for l in r.lanes])
+
+    def save(self, block_ids: Sequence[int], host_ptr: int, host_bytes: int, host_off: int = 0) -> KVTransferStats:
+        """GPU blocks -> host region (gather through the block table)."""
+        return self._run(False, block_ids, host_ptr, host_bytes, host_off)
+
+    def restore(self, block_ids: Sequence[int], host_ptr: int, host_bytes: int,
+                host_off: int = 0, span_blocks: int | None = None) -> KVTransferStats:
+        """Host region -> GPU blocks (scatter through the block table).  A
+        region saved with ``span_blocks`` blocks restores its first
+        ``len(block_ids)`` blocks when given ``span_blocks``."""
+        return self._run(True, block_ids, host_ptr, host_bytes, host_off, span_blocks)
+
+
+__all__ = ["KVTransferStats", "PagedKVOffloader"]
