@@ -164,4 +164,84 @@ def chunk_lane_map(trace: list[dict[str, Any]]) -> dict[int, int]:
     return out
 
 
-__all__ = ["FaultPlan", "MockDataPlane", "MockLaneError", "MockWorld", "chunk_lane_map"]
+class MockCudaBackend:
+    """Stand-in for the CUDA backend in worker tests: IPC handles are 64
+    random bytes mapped to in-process addresses; host registration is
+    recorded, not performed."""
+
+    def __init__(self) -> None:
+        self.handles: dict[bytes, int] = {}
+        self.open: dict[int, bytes] = {}
+        self.registered: dict[int, int] = {}
+        self.device = 0
+
+    def set_device(self, device_index: int) -> None:
+        self.device = int(device_index)
+
+    def export_device_ipc_handle(self, device_ptr: int) -> bytes:
+        import os
+
+        h = os.urandom(64)
+        self.handles[h] = int(device_ptr)
+        return h
+
+    def open_device_ipc_handle(self, handle, device_index: int = 0) -> int:
+        h = bytes.fromhex(handle) if isinstance(handle, str) else bytes(handle)
+        if h not in self.handles:
+            raise RuntimeError("unknown CUDA IPC handle")
+        ptr = self.handles[h]
+        self.open[ptr] = h
+        return ptr
+
+    def close_device_ipc_handle(self, device_ptr: int) -> None:
+        self.open.pop(int(device_ptr), None)
+
+    def register_host_memory(self, host_ptr: int, nbytes: int) -> None:
+        self.registered[int(host_ptr)] = int(nbytes)
+
+    def unregister_host_memory(self, host_ptr: int) -> None:
+        self.registered.pop(int(host_ptr), None)
+
+
+class MockWorkerExecutor:
+    """Worker executor over the mock lanes: runs the ticket's scoped plan
+    (direct + authorized relays) between the bound resources' addresses."""
+
+    def __init__(self, plane: MockDataPlane | None = None) -> None:
+        self.plane = plane or MockDataPlane()
+        self.calls = 0
+
+    def execute(self, request, staging_slot):
+        from ..worker.helper import _failed
+
+        return _failed(request, staging_slot, "mock worker execution requires bound resources")
+
+    def execute_bound(self, request, staging_slot, resources):
+        from ..worker.cuda_executor import scoped_plan
+        from ..worker.helper import WorkerTransferResult, WorkerTransferState, _failed
+
+        self.calls += 1
+        dp = request.data_plane
+        h2d = dp.direction == "h2d"
+        target = int((dp.dst_handle if h2d else dp.src_handle).device_index or 0)
+        plan = scoped_plan(request, target)
+        lanes = []
+        for a in plan["assignments"]:
+            p = a["path"]
+            dev = target if p["kind"] == "direct" else int(p["relay_device"])
+            lanes.append((dev, p["kind"], [(c["src_offset"], c["dst_offset"], c["bytes"]) for c in a["chunks"]]))
+        src, sb, dst, db = ((resources.host_ptr, resources.host_bytes, resources.device_ptr, resources.device_bytes)
+                            if h2d else
+                            (resources.device_ptr, resources.device_bytes, resources.host_ptr, resources.host_bytes))
+        r = self.plane.run_lanes(dp.direction, src, sb, dst, db, lanes, transfer_id=request.transfer_id)
+        if not r.ok:
+            return _failed(request, staging_slot, r.error)
+        d_c = sum(len(c) for _d, k, c in lanes if k == "direct")
+        return WorkerTransferResult(request.transfer_id, WorkerTransferState.COMPLETE, bytes_completed=r.bytes_completed,
+                                    metadata={"executor": "mock_worker", "staging_slot_id": staging_slot.slot_id,
+                                              "path": f"{'pool' if d_c else 'relay'}_{dp.direction}",
+                                              "path_stats": r.measured.get("path_stats", [])})
+
+
+__all__ = ["FaultPlan", "MockCudaBackend", "MockDataPlane", "MockLaneError", "MockWorkerExecutor", "MockWorld",
+           "chunk_lane_map"]
