@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import threading
 import uuid
 from dataclasses import dataclass, field
 from multiprocessing import resource_tracker, shared_memory
@@ -20,6 +21,7 @@ from typing import Any
 from .schema import BufferRegistration, DaemonResponse
 
 _OWNED_NAMES: set[str] = set()
+_ATTACH_LOCK = threading.Lock()
 
 
 def _shm_name(prefix: str) -> str:
@@ -37,14 +39,17 @@ def _open_borrowed(name: str) -> shared_memory.SharedMemory:
     try:
         return shared_memory.SharedMemory(name=name, create=False, track=False)
     except TypeError:  # Python < 3.13 has no ``track``
-        shm = shared_memory.SharedMemory(name=name, create=False)
-        tn = _tracker_name(shm)
-        if os.name == "posix" and tn not in _OWNED_NAMES:
+        # Attaching would register the name with the resource tracker, which
+        # processes started by ``multiprocessing`` share with their parent; a
+        # register + unregister pair here would drop the owner's registration.
+        # Skip the registration for the duration of the attach instead.
+        with _ATTACH_LOCK:
+            saved = resource_tracker.register
+            resource_tracker.register = lambda *_a, **_k: None
             try:
-                resource_tracker.unregister(tn, "shared_memory")
-            except Exception:  # noqa: BLE001 - tracker may not know it
-                pass
-        return shm
+                return shared_memory.SharedMemory(name=name, create=False)
+            finally:
+                resource_tracker.register = saved
 
 
 def default_backend():

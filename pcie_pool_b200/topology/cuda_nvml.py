@@ -16,6 +16,7 @@ from __future__ import annotations
 import csv
 import ctypes
 import os
+import re
 import subprocess
 import time
 from dataclasses import dataclass
@@ -264,9 +265,15 @@ def fabric_capability(token: str) -> dict[str, object] | None:
     return None
 
 
+_ANSI = re.compile(r"\x1b\[[0-9;]*[A-Za-z]")
+
+
 def fabric_links_from_matrix(gpu_ids: set[int], lines: Sequence[str]) -> tuple[FabricLinkRecord, ...]:
-    rows = [ln.split() for ln in lines if str(ln).strip()]
-    header = next((r for r in rows if r and r[0].startswith("GPU")), None)
+    # nvidia-smi underlines the header row with ANSI escapes; the header is the
+    # first row whose first token is a GPU column name and whose second token
+    # is another column name (data rows have a cell there instead)
+    rows = [_ANSI.sub("", str(ln)).split() for ln in lines if str(ln).strip()]
+    header = next((r for r in rows if len(r) > 1 and r[0].startswith("GPU") and r[1].startswith("GPU")), None)
     if not header:
         return ()
 

@@ -48,7 +48,8 @@ class WorkerManagedRelayVerificationResult:
     worker_relay_chunks: int
     daemon_reservations_released: bool
     daemon_relay_active_chunks: int
-    gb_per_s: float = 0.0
+    gb_per_s: float = 0.0          # end to end: daemon RPCs, worker start-up and binding included
+    data_plane_gb_per_s: float = 0.0  # device-timed engine transfer as reported by the executor
 
     def as_dict(self) -> dict[str, object]:
         return asdict(self)
@@ -252,7 +253,9 @@ def verify(direction: str = "h2d", *, target_gpu: int = 0, relay_gpu: int = 1, b
                        res.worker_completion.get("final_state"),
                        worker_path=res.path, worker_direct_bytes=d_b, worker_direct_chunks=d_c,
                        worker_relay_bytes=r_b, worker_relay_chunks=r_c, daemon_reservations_released=released,
-                       daemon_relay_active_chunks=active, gb_per_s=round(n / secs / 1e9, 3))
+                       daemon_relay_active_chunks=active, gb_per_s=round(n / secs / 1e9, 3),
+                       data_plane_gb_per_s=round(float(wres.get("gb_per_s") or res.measured.get("gb_per_s") or 0.0),
+                                                 3))
         finally:
             if cpu is not None:
                 cpu.release()
