@@ -24,11 +24,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import statistics
-import subprocess
 import sys
-import threading
-import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -92,94 +88,9 @@ class Dist:
             self.pg.destroy_process_group()
 
 
-# ---- clocks -------------------------------------------------------------------------
+# ---- clocks and host data ---------------------------------------------------------------
 
-class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, gpus: int):
-        self.gpus = gpus
-        self.proc = None
-        self.lines: list[str] = []
-        self._t = None
-
-    def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
-            return
-        self._t = threading.Thread(target=self._read, daemon=True)
-        self._t.start()
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
-    def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        if self._t:
-            self._t.join(timeout=2)
-        sm, mx, reasons, power = [], [], set(), []
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                idx = int(parts[0])
-            except ValueError:
-                continue
-            if idx >= self.gpus:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-                power.append(float(parts[3]))
-            except ValueError:
-                pass
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        return {
-            "sm_mhz": statistics.median(sm) if sm else None,
-            "sm_max_mhz": max(mx) if mx else None,
-            "reasons": sorted(reasons),
-            "samples": len(sm),
-            "power_w_max": max(power) if power else None,
-        }
-
-
-# ---- host data --------------------------------------------------------------------------
-
-def fill_random(arr, seed: int = 0, threads: int = 16):
-    import numpy as np
-
-    parts = np.array_split(arr, threads)
-
-    def work(i):
-        g = np.random.default_rng(seed + i)
-        p = parts[i]
-        step = 64 << 20
-        for o in range(0, p.size, step):
-            seg = p[o:o + step]
-            seg[:] = np.frombuffer(g.bytes(seg.size), dtype=np.uint8)
-
-    ths = [threading.Thread(target=work, args=(i,)) for i in range(threads)]
-    for t in ths:
-        t.start()
-    for t in ths:
-        t.join()
+from pcie_pool_b200.benchmarks.common import ClockSampler, fill_random  # noqa: E402
 
 
 # ---- our implementation ---------------------------------------------------------------
@@ -190,7 +101,7 @@ def run_ours(args, dist: Dist) -> dict:
 
     from pcie_pool_b200.parallel.engine import D2H, H2D, PoolEngine
     from pcie_pool_b200.parallel.planning import plan_lanes
-    from pcie_pool_b200.utils.checksum import combine
+    from pcie_pool_b200.utils.checksum import combine, rebase_chunk_sums
     from pcie_pool_b200.utils.host_memory import PinnedHostBuffer
 
     N = args.gpus
@@ -265,7 +176,7 @@ def run_ours(args, dist: Dist) -> dict:
         if checksum and direction == H2D:
             C = __import__("pcie_pool_b200._C", fromlist=["x"])
             host_sum = C.checksum_host(host.ptr, n)
-            got = combine(_shift_chunk_sums(res, lanes))
+            got = combine(rebase_chunk_sums(res.checksums, lanes))
             verified = (tuple(int(x) for x in host_sum) == got)
         out = {
             "elapsed_ms": elapsed_ms,
@@ -286,19 +197,6 @@ def run_ours(args, dist: Dist) -> dict:
                 out["e2e"] = {"error": f"{type(exc).__name__}: {exc}"}
         del eng
         host.release()
-    return out
-
-
-def _shift_chunk_sums(res, lanes):
-    """Per-chunk checksums are chunk-local; re-base them onto the whole buffer
-    so their sum equals the checksum of the full host buffer."""
-    i = 0
-    out = []
-    for lane in lanes:
-        for s in lane.src_off:
-            a, w = int(res.checksums[i][0]), int(res.checksums[i][1])
-            out.append((a, (w + (int(s) // 4) * a) & (2**64 - 1)))
-            i += 1
     return out
 
 

@@ -7,6 +7,7 @@
 
 #include <cstring>
 
+#include "host_ops.h"
 #include "native_ops.h"
 #include "planner.h"
 #include "ppb_common.h"
@@ -94,6 +95,20 @@ void bind_ops(py::module_& m) {
   m.def(
       "checksum_host",
       [](uint64_t ptr, uint64_t bytes) { return checksum_host(reinterpret_cast<const void*>(ptr), bytes); },
+      py::call_guard<py::gil_scoped_release>());
+  m.def(
+      "fill_normal_bf16",
+      [](uint64_t ptr, uint64_t n, float mean, float stddev, uint64_t seed, int threads) {
+        fill_normal_bf16(reinterpret_cast<void*>(ptr), n, mean, stddev, seed, threads);
+      },
+      py::arg("ptr"), py::arg("n"), py::arg("mean") = 0.0f, py::arg("stddev") = 1.0f, py::arg("seed") = 0,
+      py::arg("threads") = 0, py::call_guard<py::gil_scoped_release>());
+  m.def(
+      "fill_random_bytes",
+      [](uint64_t ptr, uint64_t n, uint64_t seed, int threads) {
+        fill_random_bytes(reinterpret_cast<void*>(ptr), n, seed, threads);
+      },
+      py::arg("ptr"), py::arg("n"), py::arg("seed") = 0, py::arg("threads") = 0,
       py::call_guard<py::gil_scoped_release>());
 }
 

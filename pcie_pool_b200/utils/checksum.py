@@ -53,3 +53,18 @@ def checksum_at(data, start_byte: int) -> tuple[int, int]:
     s, w = checksum_bytes(data)
     shift = start_byte // 4
     return s, (w + shift * s) & _MASK
+
+
+def rebase_chunk_sums(checksums, lanes):
+    """Per-chunk checksums (chunk-local word index, in lane order) re-based
+    onto the whole host buffer via each chunk's host offset, so that
+    ``combine`` of the result equals the checksum of the full buffer when the
+    chunks tile it.  ``lanes`` are the H2D lanes of the transfer (``src_off``
+    is the host offset, a multiple of 4)."""
+    out, i = [], 0
+    for lane in lanes:
+        for s in lane.src_off:
+            a, w = int(checksums[i][0]), int(checksums[i][1])
+            out.append((a, (w + (int(s) // 4) * a) & _MASK))
+            i += 1
+    return out
