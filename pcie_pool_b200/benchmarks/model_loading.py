@@ -1,270 +1,202 @@
-"""Llama-3-8B-shape weight load into GPU0 (BASELINE configs 3a / 3b).
+"""Daemon-first model-weight loading benchmark (intent CLI).
 
-    python -m pcie_pool_b200.benchmarks.model_loading --gpus 8 --variant bf16
-    python -m pcie_pool_b200.benchmarks.model_loading --gpus 8 --variant fp8
-    python -m pcie_pool_b200.benchmarks.model_loading --gpus 8 --variant bf16 --impl reference
+    python -m pcie_pool_b200.benchmarks.model_loading --daemon-socket-path S \\
+        --session-id SID --source-buffer-id HOST --destination-buffer-id GPU \\
+        --bucket-count 8 --bucket-bytes 33554432 --iterations 5
 
-The packed host image (8,030,261,248 bf16 parameters, N(0, 0.02), 16.06 GB,
-page-locked) is loaded into GPU0 over the direct lane plus ``gpus-1`` relay
-lanes.  ``bf16`` lands the image as-is (plain copy, per-chunk checksums);
-``fp8`` lands every matrix as e4m3 codes with fp32 scales per 128x128 block,
-quantized inside the landing kernel, and the 1-D norm weights as bf16.
-``--api`` also times the bf16 load through the public API
-(``ModelWeightLoader`` -> ``TurboBusClient`` -> daemon -> executor -> engine).
-Each timed load is bracketed by CUDA events on GPU0 after warm-up loads; the
-reported ``value`` is seconds per load (lower is better).  ``--impl
-reference`` loads the same image through the reference's own runtime and
-planner (bf16 only: the reference has no quantizing landing).
+Each iteration submits one ``model_weights`` intent of ``bucket_count``
+ranges through ``TurboBusClient`` and (with ``--wait-timeout-seconds`` > 0)
+waits for its receipt; ``load_ms`` covers submit + wait.  Output JSON is
+``{config, warmup_samples, samples, summary}`` and a compact
+``MODEL_LOAD_SUMMARY`` text block with ``daemon_receipt``-style lines, the
+shapes of turbobus benchmarks/model_loading.py:142-356.  Because the daemon
+here executes intents, the receipts carry the measured per-lane stats and a
+waited iteration covers the actual data movement.
 """
 
 from __future__ import annotations
 
 import argparse
+import json
+import statistics
+import sys
 import time
+import uuid
+from pathlib import Path
 
-import numpy as np
-
-from .common import ClockSampler, calibrate, emit, reference_plan, reference_runtime
-
-
-def parse_args(argv=None):
-    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=3)
-    p.add_argument("--warmup", type=int, default=2)
-    p.add_argument("--variant", choices=["bf16", "fp8"], default="bf16")
-    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--chunk", type=int, default=16 << 20)
-    p.add_argument("--api", action="store_true", help="also time the bf16 load through the public API")
-    p.add_argument("--layers", type=int, default=0, help="override the layer count (smaller smoke runs)")
-    p.add_argument("--json-out", default="")
-    return p.parse_args(argv)
+from ..api import TurboBusClient
+from ..schema import TransferReceipt, WorkloadKind
+from .daemon_support import (add_daemon_options, benchmark_job_id, make_benchmark_transfer_intent, receipt_to_trace,
+                             receipt_trace_line)
 
 
-def _manifest(layers: int):
-    from dataclasses import replace
-
-    from ..models.llama import llama3_8b, weight_manifest
-
-    cfg = llama3_8b()
-    if layers:
-        cfg = replace(cfg, layers=int(layers), name=f"llama-3-8b-shape-{layers}L")
-    return weight_manifest(cfg)
+def bucket_ranges(bucket_count: int, bucket_bytes: int) -> tuple[dict[str, int], ...]:
+    return tuple({"src_offset": i * int(bucket_bytes), "dst_offset": i * int(bucket_bytes), "bytes": int(bucket_bytes)}
+                 for i in range(int(bucket_count)))
 
 
-def _host_image(manifest):
-    from .._native import native
-    from ..utils.host_memory import PinnedHostBuffer
-
-    host = PinnedHostBuffer(manifest.total_bytes, fill=None)
-    native().fill_normal_bf16(host.ptr, manifest.total_bytes // 2, 0.0, 0.02, 20240601, 0)
-    return host
+def _wait_timeout(args) -> float | None:
+    t = getattr(args, "wait_timeout_seconds", None)
+    return None if t is None or float(t) <= 0 else float(t)
 
 
-def _verify_bf16(host, res, lanes, total) -> bool:
-    from .._native import native
-    from ..utils.checksum import combine, rebase_chunk_sums
-
-    want = tuple(int(x) for x in native().checksum_host(host.ptr, total))
-    return combine(rebase_chunk_sums(res.checksums, lanes)) == want
-
-
-def _verify_fp8(host, manifest, loaded) -> bool:
-    import torch
-
-    from ..utils.fp8 import block_quant
-
-    raw = host.numpy()
-    ok = True
-    pick = [t for t in manifest.matrices() if ".k_proj." in t.name][:1] + manifest.matrices()[-1:]
-    for t in pick:
-        rows, cols = t.shape
-        w = raw[t.offset:t.offset + t.nbytes].view(np.uint16).reshape(rows, cols)
-        f = torch.from_numpy(w.view(np.int16).copy()).view(torch.bfloat16).float().numpy()
-        if rows > 4096:  # the vocab matrices: check the first 2048 rows (16 row-blocks)
-            f = f[:2048]
-        q_ref, s_ref = block_quant(f)
-        q = loaded.tensors[t.name][:f.shape[0]].cpu().numpy()
-        s = loaded.scales[t.name][:s_ref.shape[0]].cpu().numpy()
-        ok &= bool(np.array_equal(q, q_ref)) and bool(np.array_equal(s, s_ref))
-    for t in manifest.vectors()[:3]:
-        got = loaded.tensors[t.name].view(torch.int16).cpu().numpy().view(np.uint16)
-        ok &= bool(np.array_equal(got, raw[t.offset:t.offset + t.nbytes].view(np.uint16)))
-    return ok
+def sample_from_receipt(receipt: TransferReceipt, intent, elapsed_ms: float, iteration: int, phase: str,
+                        prefix: str) -> dict:
+    t = receipt_to_trace(receipt)
+    gib = (int(t["bytes_total"]) / (1 << 30)) / (elapsed_ms / 1e3) if elapsed_ms > 0 else 0.0
+    return {"iteration": int(iteration), "phase": phase, f"{prefix}_ms": elapsed_ms,
+            f"{prefix}_gib_per_second": gib,
+            "intent": {"intent_id": intent.intent_id, "job_id": intent.job_id, "session_id": intent.session_id,
+                       "source_buffer_id": intent.source_buffer_id,
+                       "destination_buffer_id": intent.destination_buffer_id,
+                       "workload_kind": intent.workload_kind.value, "total_bytes": intent.total_bytes,
+                       "ranges": list(intent.ranges), "policy_hints": dict(intent.policy_hints),
+                       "metadata": dict(intent.metadata)},
+            "receipt": t, "bytes": int(t["bytes_total"]), "bytes_completed": int(t["bytes_completed"]),
+            "direct_bytes": int(t["direct_bytes"]), "relay_bytes": int(t["relay_bytes"]),
+            "direct_chunks": int(t["direct_chunks"]), "relay_chunks": int(t["relay_chunks"]),
+            "measured_cuda_ms": float(t.get("measured_cuda_ms", 0.0)), "decision_id": str(t["decision_id"]),
+            "topology_snapshot_id": str(t["topology_snapshot_id"]), "ticket_id": str(t["ticket_id"]),
+            "fallback_reason": str(t.get("fallback_reason", "") or "")}
 
 
-def run_ours(a) -> dict:
-    import torch
+def build_intent(args, *, iteration: int, phase: str):
+    return make_benchmark_transfer_intent(
+        intent_id=f"{args.intent_prefix}-{args.run_id}-{phase}-{iteration}", workload_kind=WorkloadKind.MODEL_WEIGHTS,
+        job_id=args.job_id, session_id=args.session_id, source_buffer_id=args.source_buffer_id,
+        destination_buffer_id=args.destination_buffer_id, direction="h2d",
+        total_bytes=int(args.bucket_count) * int(args.bucket_bytes),
+        ranges=bucket_ranges(args.bucket_count, args.bucket_bytes),
+        metadata={"benchmark": "model-loading", "phase": phase, "iteration": int(iteration), "policy": args.policy,
+                  "storage_layout": args.storage_layout, "bucket_count": int(args.bucket_count),
+                  "bucket_bytes": int(args.bucket_bytes), "chunk_bytes": int(args.chunk_bytes)})
 
-    from ..models.loader import PooledWeightLoader
-    from ..parallel.engine import PoolEngine
 
-    manifest = _manifest(a.layers)
-    total = manifest.total_bytes
-    devices = list(range(a.gpus))
-    torch.cuda.set_device(0)
-    host = _host_image(manifest)
-    eng = PoolEngine(devices, slot_bytes=a.chunk, slots=3, ctas_per_lane=4, timeout_s=30.0)
-    lane_set, weights, balancer, profile = calibrate(eng, 0, devices, total, a.chunk)
-    loader = PooledWeightLoader(eng, 0, [d for d in lane_set if d != 0], chunk_bytes=a.chunk, balancer=balancer)
-    dst = torch.empty(total, dtype=torch.uint8, device="cuda:0") if a.variant == "bf16" else None
-
-    def load():
-        if a.variant == "bf16":
-            return loader.load_bf16(host.ptr, total, manifest, device_buffer=dst)
-        return loader.load_fp8(host.ptr, total, manifest)
-
-    for _ in range(a.warmup):
-        last = load()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(a.gpus).start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+def submit_load_intent(client, args, *, iteration: int, phase: str) -> dict:
+    intent = build_intent(args, iteration=iteration, phase=phase)
     t0 = time.perf_counter()
-    e0.record()
-    for _ in range(a.steps):
-        last = load()
-    e1.record()
-    torch.cuda.synchronize()
-    wall = (time.perf_counter() - t0) / a.steps
-    clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / a.steps
-    if a.variant == "bf16":
-        # one more load with its lanes kept: the per-chunk checksums, re-based
-        # onto the image, must equal the host checksum of the whole image
-        from ..parallel.engine import H2D
-
-        lanes = loader.bf16_lanes(total)
-        r = eng.run(H2D, 0, host.ptr, total, dst.data_ptr(), total, lanes, checksum=True)
-        verified = r.ok and _verify_bf16(host, r, lanes, total)
-    else:
-        verified = _verify_fp8(host, manifest, last)
-    out = {"ms": ms, "wall_ms": wall * 1e3, "verified": verified, "clocks": clk, "bytes": total,
-           "lane_set": lane_set, "lanes": last.stats.lanes, "transfers_per_load": last.stats.transfers,
-           "probe": None if profile is None else profile.get("concurrent")}
-    if a.api and a.variant == "bf16":
-        out["api"] = _api_load(a, eng, host, dst, manifest, profile)
-    del last, dst
-    host.release()
-    return out
+    receipt = client.submit_transfer_intent(intent)
+    if _wait_timeout(args) is not None:
+        receipt = client.wait_transfer_receipt(intent.intent_id, timeout_seconds=_wait_timeout(args))
+    return sample_from_receipt(receipt, intent, (time.perf_counter() - t0) * 1e3, iteration, phase, "load")
 
 
-def _api_load(a, eng, host, dst, manifest, profile) -> dict:
-    """bf16 load through ModelWeightLoader on an in-process daemon."""
-    import torch
-
-    from ..adapters import AdapterTransferContext, ModelWeightLoader
-    from ..api import TurboBusClient
-    from ..e2e import build_inprocess_node
-    from ..schema import WorkloadKind
-
-    total = manifest.total_bytes
-    devices = list(range(a.gpus))
-    _daemon, dc = build_inprocess_node(eng, devices, 0, profile)
-    sid = dc.register_session(0, devices[1:], max_inflight_chunks=1 << 16).payload["session"]["session_id"]
-    dc.register_job("llama-load", session_id=sid)
-    dc.register_buffer("weights-host", "llama-load", "cpu_pinned", total, address=host.ptr, pinned=True)
-    dc.register_buffer("weights-gpu0", "llama-load", "gpu", total, device_index=0, address=dst.data_ptr())
-    ctx = AdapterTransferContext("llama-load", sid, "weights-host", "weights-gpu0",
-                                 workload_kind=WorkloadKind.MODEL_WEIGHTS, metadata={"chunk_bytes": a.chunk},
-                                 wait_timeout_seconds=600)
-
-    class _Mem:  # byte-count stand-in for the packed image (the loader reads offsets only)
-        def __init__(self, n):
-            self.n = n
-
-        def numel(self):
-            return self.n
-
-        def element_size(self):
-            return 1
-
-    bucket = 512 << 20
-    count = (total + bucket - 1) // bucket
-
-    def load(i):
-        ld = ModelWeightLoader(TurboBusClient(daemon=dc), ctx)
-        hb, rest = _Mem(total), total
-        for k in range(count):
-            n = min(bucket, rest)
-            ld.add_bucket(f"w{k}", hb, hb, bucket_id=k, cpu_offset=k * bucket, gpu_offset=k * bucket, byte_count=n)
-            rest -= n
-        ld.load_all()
-        ld.wait_all()
-        return ld
-
-    load(0)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for i in range(a.steps):
-        ld = load(i + 1)
-    torch.cuda.synchronize()
-    s = (time.perf_counter() - t0) / a.steps
-    st = ld.transfer_stats_many(ld.names())
-    return {"load_s": round(s, 4), "gb_per_s": round(total / 1e9 / s, 3), "buckets": count,
-            "direct_chunks": st.direct_chunks, "relay_chunks": st.relay_chunks,
-            "path": "ModelWeightLoader -> TurboBusClient -> daemon -> executor -> PoolEngine"}
+def summarize(samples: list[dict], prefix: str = "load") -> dict:
+    keys = ("bytes", "bytes_completed", "direct_bytes", "relay_bytes", "direct_chunks", "relay_chunks")
+    if not samples:
+        return {"iterations": 0, f"median_{prefix}_ms": 0.0, "median_gib_per_second": 0.0, **{k: 0 for k in keys},
+                "decision_ids": [], "topology_snapshot_ids": [], "ticket_ids": [], "receipt_ids": [],
+                "fallback_reasons": []}
+    return {"iterations": len(samples),
+            f"median_{prefix}_ms": statistics.median(s[f"{prefix}_ms"] for s in samples),
+            "median_gib_per_second": statistics.median(s[f"{prefix}_gib_per_second"] for s in samples),
+            "median_measured_cuda_ms": statistics.median(s.get("measured_cuda_ms", 0.0) for s in samples),
+            **{k: int(statistics.median(s[k] for s in samples)) for k in keys},
+            "decision_ids": sorted({s["decision_id"] for s in samples}),
+            "topology_snapshot_ids": sorted({s["topology_snapshot_id"] for s in samples}),
+            "ticket_ids": sorted({s["ticket_id"] for s in samples}),
+            "receipt_ids": sorted({str(s["receipt"].get("receipt_id")) for s in samples if s["receipt"].get("receipt_id")}),
+            "fallback_reasons": sorted({s["fallback_reason"] for s in samples if s["fallback_reason"]})}
 
 
-def run_reference(a) -> dict:
-    import torch
+def config_dict(args) -> dict:
+    return {"session_id": args.session_id, "job_id": args.job_id, "source_buffer_id": args.source_buffer_id,
+            "destination_buffer_id": args.destination_buffer_id, "workload_kind": WorkloadKind.MODEL_WEIGHTS.value,
+            "bucket_count": int(args.bucket_count), "bucket_bytes": int(args.bucket_bytes),
+            "storage_layout": args.storage_layout, "chunk_bytes": int(args.chunk_bytes), "warmup": int(args.warmup),
+            "iterations": int(args.iterations), "policy": args.policy, "run_id": args.run_id,
+            "daemon_socket_path": args.daemon_socket_path, "wait_timeout_seconds": args.wait_timeout_seconds}
 
-    if a.variant != "bf16":
-        return {"unavailable": "the reference has no quantizing landing path (bf16 only)"}
-    manifest = _manifest(a.layers)
-    total = manifest.total_bytes
-    torch.cuda.set_device(0)
-    rt, why = reference_runtime(a.gpus, a.chunk)
-    if rt is None:
-        return {"unavailable": why}
-    host_t = torch.empty(total, dtype=torch.uint8, pin_memory=True)
-    from .._native import native
 
-    native().fill_normal_bf16(host_t.data_ptr(), total // 2, 0.0, 0.02, 20240601, 0)
-    dst = torch.empty(total, dtype=torch.uint8, device="cuda:0")
-    nplan, _profile = reference_plan(rt, total, a.chunk)
+def run_benchmark(args, *, client=None) -> dict:
+    client = client or TurboBusClient(socket_path=args.daemon_socket_path)
+    warm = [submit_load_intent(client, args, iteration=i, phase="warmup") for i in range(int(args.warmup))]
+    samples = [submit_load_intent(client, args, iteration=i, phase="measure") for i in range(int(args.iterations))]
+    return {"config": config_dict(args), "warmup_samples": warm, "samples": samples, "summary": summarize(samples)}
 
-    def load():
-        h = rt.fetch_plan_to_gpu(host_t.data_ptr(), total, dst.data_ptr(), total, nplan)
-        rt.wait(h)
 
-    for _ in range(a.warmup):
-        load()
-    torch.cuda.synchronize()
-    clocks = ClockSampler(a.gpus).start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(a.steps):
-        load()
-    e1.record()
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / a.steps
-    verified = bool(torch.equal(dst[:1 << 24].cpu(), host_t[:1 << 24])) and bool(
-        torch.equal(dst[-(1 << 24):].cpu(), host_t[-(1 << 24):]))
-    del rt
-    return {"ms": ms, "verified": verified, "clocks": clk, "bytes": total}
+def receipt_from_trace(t: dict) -> TransferReceipt:
+    return TransferReceipt(receipt_id=t["receipt_id"], ticket_id=t["ticket_id"], intent_id=t["intent_id"],
+                           decision_id=t["decision_id"], topology_snapshot_id=t["topology_snapshot_id"],
+                           job_id=t["job_id"], session_id=t["session_id"], state=t["state"],
+                           bytes_total=t["bytes_total"], bytes_completed=t["bytes_completed"],
+                           started_at=t.get("started_at", 0.0), completed_at=t.get("completed_at"),
+                           path_stats=tuple(t.get("path_stats", ())), error=t.get("error"),
+                           metadata=t.get("metadata", {}))
+
+
+def compact_summary(result: dict) -> str:
+    c, s = result["config"], result["summary"]
+    lines = ["MODEL_LOAD_SUMMARY_BEGIN",
+             f"model_load_config session_id={c['session_id']} job_id={c['job_id']} "
+             f"source_buffer_id={c['source_buffer_id']} destination_buffer_id={c['destination_buffer_id']} "
+             f"bucket_count={c['bucket_count']} bucket_bytes={c['bucket_bytes']} storage_layout={c['storage_layout']} "
+             f"chunk_bytes={c['chunk_bytes']} iterations={c['iterations']} policy={c['policy']} "
+             f"daemon_socket_path={c['daemon_socket_path']}",
+             f"model_load_summary median_load_ms={s['median_load_ms']:.3f} "
+             f"median_gib_s={s['median_gib_per_second']:.3f} bytes={s['bytes']} bytes_completed={s['bytes_completed']} "
+             f"direct_bytes={s['direct_bytes']} relay_bytes={s['relay_bytes']} direct_chunks={s['direct_chunks']} "
+             f"relay_chunks={s['relay_chunks']}"]
+    for x in result["samples"]:
+        lines.append(f"model_load_sample iteration={x['iteration']} load_ms={x['load_ms']:.3f} "
+                     f"gib_s={x['load_gib_per_second']:.3f} decision_id={x['decision_id']} "
+                     f"topology_snapshot_id={x['topology_snapshot_id']} ticket_id={x['ticket_id']}")
+        lines.append(receipt_trace_line(receipt_from_trace(x["receipt"]), prefix="model_load_receipt"))
+    lines.append("MODEL_LOAD_SUMMARY_END")
+    return "\n".join(lines)
+
+
+def write_outputs(args, result: dict, summary_text: str) -> None:
+    if args.json_output:
+        p = Path(args.json_output)
+        p.parent.mkdir(parents=True, exist_ok=True)
+        p.write_text(json.dumps(result, indent=2) + "\n", encoding="utf-8")
+    if args.summary_output:
+        p = Path(args.summary_output)
+        p.parent.mkdir(parents=True, exist_ok=True)
+        p.write_text(summary_text + "\n", encoding="utf-8")
+    if not args.no_copy_summary:
+        sys.stdout.write(summary_text + "\n")
+
+
+def build_parser() -> argparse.ArgumentParser:
+    p = argparse.ArgumentParser(description="Submit model weight loading intents through the public client")
+    p.add_argument("--session-id", required=True)
+    p.add_argument("--job-id", default=benchmark_job_id("model-loading"))
+    p.add_argument("--source-buffer-id", required=True)
+    p.add_argument("--destination-buffer-id", required=True)
+    p.add_argument("--bucket-count", type=int, default=8)
+    p.add_argument("--bucket-bytes", type=int, default=32 << 20)
+    p.add_argument("--storage-layout", choices=["packed", "separate"], default="packed")
+    p.add_argument("--chunk-bytes", type=int, default=4 << 20)
+    p.add_argument("--warmup", type=int, default=0)
+    p.add_argument("--iterations", type=int, default=5)
+    p.add_argument("--policy", default="daemon-default")
+    p.add_argument("--run-id", default=str(uuid.uuid4()))
+    p.add_argument("--intent-prefix", default="model-load")
+    p.add_argument("--wait-timeout-seconds", type=float, default=0.0)
+    p.add_argument("--json-output")
+    p.add_argument("--summary-output")
+    p.add_argument("--no-copy-summary", action="store_true")
+    add_daemon_options(p)
+    return p
+
+
+def validate_args(args) -> None:
+    for name in ("bucket_count", "bucket_bytes", "chunk_bytes", "iterations"):
+        if int(getattr(args, name)) <= 0:
+            raise SystemExit(f"--{name.replace('_', '-')} must be positive")
+    if int(args.warmup) < 0:
+        raise SystemExit("--warmup must be non-negative")
+    if not args.daemon_socket_path:
+        raise SystemExit("--daemon-socket-path is required")
 
 
 def main(argv=None) -> int:
-    a = parse_args(argv)
-    res = run_reference(a) if a.impl == "reference" else run_ours(a)
-    if "unavailable" in res:
-        emit({"impl": a.impl, "unavailable": res["unavailable"]}, a.json_out)
-        return 0
-    ms = res["ms"]
-    line = {"metric": "Llama-3-8B-shape weight load into GPU0", "value": round(ms / 1e3, 4), "unit": "s",
-            "higher_is_better": False, "gb_per_s": round(res["bytes"] / 1e9 / (ms / 1e3), 3),
-            "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "impl": a.impl, "variant": a.variant,
-            "verified": res.get("verified"), "clocks": res.get("clocks"),
-            "config": {"model": _manifest(a.layers).config.name, "params": _manifest(a.layers).param_count,
-                       "image_bytes": res["bytes"], "chunk_bytes": a.chunk, "target_gpu": 0,
-                       "relay_gpus": list(range(1, a.gpus)),
-                       "landing": "bf16 copy" if a.variant == "bf16" else "fp8 e4m3 + fp32 128x128 scales",
-                       "data": "synthetic bf16 N(0, 0.02), seeded"}}
-    for k in ("wall_ms", "lane_set", "lanes", "transfers_per_load", "probe", "api"):
-        if k in res:
-            line[k] = res[k]
-    emit(line, a.json_out)
+    args = build_parser().parse_args(argv)
+    validate_args(args)
+    result = run_benchmark(args)
+    write_outputs(args, result, compact_summary(result))
     return 0
 
 

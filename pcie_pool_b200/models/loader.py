@@ -56,7 +56,12 @@ def _assign(sizes: np.ndarray, weights: Sequence[float] | None, nlanes: int) -> 
 
 class PooledWeightLoader:
     def __init__(self, engine, target: int, relays: Sequence[int] = (), *, chunk_bytes: int = 16 << 20,
-                 balancer=None, lane_weights: Sequence[float] | None = None, checksum: bool = True) -> None:
+                 balancer=None, lane_weights: Sequence[float] | None = None, checksum: bool = True,
+                 fp8_ctas_per_lane: int = 12) -> None:
+        # The fp8 landing does the quantization arithmetic (amax reduction and
+        # an IEEE division per element) in the landing CTAs; 4 CTAs land
+        # ~27 GB/s of bf16, so fp8 lanes get more CTAs to stay PCIe-bound.
+        self.fp8_ctas_per_lane = int(fp8_ctas_per_lane)
         self.engine = engine
         self.target = int(target)
         self.relays = [int(r) for r in relays if int(r) != int(target)]
@@ -192,7 +197,8 @@ class PooledWeightLoader:
             vlane = Lane(self.target, np.array(so, np.uint64), np.array(vo, np.uint64), np.array(nb, np.uint64))
         t0 = time.perf_counter()
         r = self.engine.run(H2D, self.target, host_ptr, host_bytes, qbuf.data_ptr(), q_total, lanes,
-                            op=C.OP_FP8_QUANT, checksum=self.checksum, tensors=table)
+                            op=C.OP_FP8_QUANT, checksum=self.checksum, tensors=table,
+                            ctas_per_lane=self.fp8_ctas_per_lane)
         r.raise_for_status()
         cuda_ms, moved, lane_stats = r.cuda_ms, r.bytes, [(l.device, l.bytes, round(l.cuda_ms, 3)) for l in r.lanes]
         self._observe(r)
