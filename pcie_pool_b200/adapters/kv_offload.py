@@ -18,7 +18,7 @@ from typing import Sequence
 
 import numpy as np
 
-from .vllm import block_table_units
+from .vllm import block_table_units, kv_layout
 
 
 @dataclass
@@ -34,7 +34,7 @@ class PagedKVOffloader:
     """Save / restore vLLM-layout KV prefixes through a ``PoolEngine``."""
 
     def __init__(self, engine, kv_caches: Sequence, target: int, relays: Sequence[int] = (),
-                 units_per_chunk: int = 128, checksum: bool = True, balancer=None) -> None:
+                 units_per_chunk: int = 128, checksum: bool = True, balancer=None, sync_stream: bool = True) -> None:
         self.engine = engine
         self.kv_caches = list(kv_caches)
         if not self.kv_caches:
@@ -44,9 +44,10 @@ class PagedKVOffloader:
         self.units_per_chunk = int(units_per_chunk)
         self.checksum = checksum
         self.balancer = balancer
-        _addrs, self.unit_bytes = block_table_units(self.kv_caches[:1], [0])
-        lanes = int(self.kv_caches[0].shape[0]) if len(self.kv_caches[0].shape) >= 3 else 1
-        self.units_per_block = lanes * len(self.kv_caches)
+        self.sync_stream = sync_stream
+        lay = kv_layout(self.kv_caches[0])
+        self.unit_bytes = lay.unit_bytes
+        self.units_per_block = lay.lanes * len(self.kv_caches)
 
     def prefix_bytes(self, block_count: int) -> int:
         return int(block_count) * self.units_per_block * self.unit_bytes
@@ -114,6 +115,13 @@ class PagedKVOffloader:
         direction = "h2d" if h2d else "d2h"
         lanes = self._lanes(segs, direction, h2d)
         kv0 = self.kv_caches[0]
+        if self.sync_stream:
+            # the engine runs on its own streams: work already queued on the
+            # caller's stream (the forward that wrote these blocks, or reads
+            # of the blocks about to be overwritten) must finish first
+            import torch
+
+            torch.cuda.current_stream(kv0.device).synchronize()
         r = self.engine.run(H2D if h2d else D2H, self.target, host_ptr, host_bytes, kv0.data_ptr(),
                             kv0.numel() * kv0.element_size(), lanes,
                             op=C.OP_SCATTER_UNITS if h2d else C.OP_GATHER_UNITS, checksum=self.checksum,

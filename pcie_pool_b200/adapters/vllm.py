@@ -200,6 +200,33 @@ def make_vllm_layer_range_refs_from_ids(request_id: str, block_ids: Iterable[int
     return refs
 
 
+@dataclass(frozen=True)
+class KVLayout:
+    """How one layer's KV tensor addresses a block: ``lanes`` units per block
+    (2 when K and V are separate planes), the byte strides between lanes and
+    between blocks, and the bytes of one unit."""
+
+    lanes: int
+    lane_stride: int
+    block_stride: int
+    unit_bytes: int
+    num_blocks: int
+
+
+def kv_layout(kv) -> KVLayout:
+    """Layout of a vLLM KV cache tensor.  ``[2, num_blocks, ...]`` (K and V
+    planes, e.g. the FlashAttention backend) has two units per block;
+    ``[num_blocks, 2, ...]`` (K and V adjacent inside a block, e.g. FlashInfer)
+    and ``[num_blocks, ...]`` have one unit covering the whole block."""
+    es = kv.element_size()
+    shape = tuple(int(d) for d in kv.shape)
+    if len(shape) >= 3 and shape[0] == 2 and shape[1] != 2:
+        return KVLayout(2, kv.stride(0) * es, kv.stride(1) * es, kv.stride(1) * es, shape[1])
+    if len(shape) < 2:
+        raise ValueError("vLLM KV tensor must have at least two dimensions")
+    return KVLayout(1, 0, kv.stride(0) * es, kv.stride(0) * es, shape[0])
+
+
 def block_table_units(kv_caches: Iterable, block_ids: Iterable[int]) -> tuple[np.ndarray, int]:
     """Device address of every (layer, lane, block) unit of a request in the
     CPU backing order [layer][lane][index] -> (uint64 addresses, unit bytes).
@@ -210,16 +237,14 @@ def block_table_units(kv_caches: Iterable, block_ids: Iterable[int]) -> tuple[np
     ids = np.asarray(list(block_ids), dtype=np.int64)
     out, unit = [], None
     for kv in kv_caches:
-        bb = block_bytes_from_vllm_kv_tensor(kv)
+        lay = kv_layout(kv)
         if unit is None:
-            unit = bb
-        elif bb != unit:
+            unit = lay.unit_bytes
+        elif lay.unit_bytes != unit:
             raise ValueError("all layers must share one block size")
-        lanes = int(kv.shape[0]) if len(kv.shape) >= 3 else 1
         base = int(kv.data_ptr())
-        for lane in range(lanes):
-            lane_off = lane * kv.stride(0) * kv.element_size() if lanes > 1 else 0
-            out.append(base + lane_off + ids * (kv.stride(1) * kv.element_size()))
+        for lane in range(lay.lanes):
+            out.append(base + lane * lay.lane_stride + ids * lay.block_stride)
     if unit is None:
         raise ValueError("no KV caches given")
     return np.concatenate(out).astype(np.uint64), int(unit)
@@ -232,6 +257,6 @@ make_layer_block_refs_from_ids = make_vllm_layer_block_refs_from_ids
 make_layer_range_refs_from_ids = make_vllm_layer_range_refs_from_ids
 
 __all__ = ["VllmKVBlockRef", "VllmKVGroup", "VllmKVSlotAdapter", "block_bytes_from_vllm_kv_tensor",
-           "block_table_units", "contiguous_runs", "make_vllm_block_refs_from_ids",
+           "KVLayout", "block_table_units", "contiguous_runs", "kv_layout", "make_vllm_block_refs_from_ids",
            "make_vllm_layer_block_refs_from_ids", "make_vllm_layer_groups_from_kv_caches",
            "make_vllm_layer_range_refs_from_ids", "vllm_block_name"]

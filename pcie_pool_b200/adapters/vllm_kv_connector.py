@@ -30,7 +30,7 @@ from typing import Any
 
 from ..offload_store import AdapterTransferContext, TransferStats, summarize_transfer_handles
 from ..schema import WorkloadKind
-from .vllm import block_bytes_from_vllm_kv_tensor, make_vllm_layer_range_refs_from_ids
+from .vllm import kv_layout, make_vllm_layer_range_refs_from_ids
 from .vllm_integration import extract_vllm_block_ids, normalize_block_id_groups
 
 try:  # pragma: no cover - depends on an installed vLLM build
@@ -142,11 +142,15 @@ class TurboBusPrefixStore:
 
 
 def _lanes_per_layer(kv) -> int:
-    return int(kv.shape[0]) if len(kv.shape) >= 3 else 1
+    return kv_layout(kv).lanes
+
+
+def _unit_bytes(kv) -> int:
+    return kv_layout(kv).unit_bytes
 
 
 def _signature(block_count: int, kv_caches: list[Any]) -> tuple:
-    return (int(block_count),) + tuple((_lanes_per_layer(kv), block_bytes_from_vllm_kv_tensor(kv)) for kv in kv_caches)
+    return (int(block_count),) + tuple((_lanes_per_layer(kv), _unit_bytes(kv)) for kv in kv_caches)
 
 
 class TurboBusCPUBackingPool:
@@ -170,7 +174,7 @@ class TurboBusCPUBackingPool:
     def _allocate(block_count: int, kv_caches: list[Any]):
         import torch
 
-        per = [max(1, block_count * _lanes_per_layer(kv)) * block_bytes_from_vllm_kv_tensor(kv) for kv in kv_caches]
+        per = [max(1, block_count * _lanes_per_layer(kv)) * _unit_bytes(kv) for kv in kv_caches]
         whole = torch.empty(sum(per), dtype=torch.uint8, pin_memory=torch.cuda.is_available())
         views, off = [], 0
         for n in per:
@@ -237,6 +241,7 @@ class TurboBusConnectorConfig:
     max_saved_prefixes: int
     data_path: str = "engine"
     relay_gpus: tuple[int, ...] = ()
+    load_async: bool = False
 
     @classmethod
     def from_vllm_config(cls, vllm_config) -> "TurboBusConnectorConfig":
@@ -267,6 +272,7 @@ class TurboBusConnectorConfig:
             max_saved_prefixes=int(_extra(vllm_config, "turbobus.max_saved_prefixes",
                                           int(env("TURBOBUS_MAX_SAVED_PREFIXES", "0") or 0))),
             data_path=str(_extra(vllm_config, "turbobus.data_path", env("TURBOBUS_DATA_PATH", "engine"))),
+            load_async=_as_bool(_extra(vllm_config, "turbobus.load_async", env("TURBOBUS_LOAD_ASYNC", "0") == "1")),
             relay_gpus=tuple(int(x) for x in (relays or ())))
 
 
@@ -396,7 +402,7 @@ class TurboBusConnector(KVConnectorBase_V1, SupportsHMA):
             target = int(kvs[0].device.index)
             devs = [target, *[r for r in self.config.relay_gpus if r != target]]
             eng = PoolEngine(devs, slot_bytes=max(self.config.chunk_bytes, 1 << 20), slots=3)
-            upc = max(1, self.config.chunk_bytes // block_bytes_from_vllm_kv_tensor(kvs[0]))
+            upc = max(1, self.config.chunk_bytes // _unit_bytes(kvs[0]))
             self._offloader = PagedKVOffloader(eng, kvs, target, devs[1:], units_per_chunk=upc,
                                                balancer=LaneBalancer())
         return self._offloader
@@ -437,7 +443,10 @@ class TurboBusConnector(KVConnectorBase_V1, SupportsHMA):
                "available_tokens": max(0, avail)}
         self.state.events.append(rec)
         _emit(**rec)
-        return max(0, avail), avail > 0
+        # The restore runs synchronously inside start_load_kv, before the
+        # forward that reads the blocks, so the load is not asynchronous
+        # unless turbobus.load_async asks for vLLM's async-load protocol.
+        return max(0, avail), bool(self.config.load_async and avail > 0)
 
     def update_state_after_alloc(self, request, blocks, num_external_tokens: int) -> None:
         p = _params(request)
@@ -531,7 +540,8 @@ class TurboBusConnector(KVConnectorBase_V1, SupportsHMA):
                 self.state.events.append({"event": "load_ready", "request_id": r.request_id,
                                           "block_count": len(r.block_ids), "restore_enabled": False})
                 _emit("load_ready", request_id=r.request_id, block_count=len(r.block_ids), restore_enabled=False)
-            self.state.finished_recving.add(r.request_id)
+            if self.config.load_async:
+                self.state.finished_recving.add(r.request_id)
         _emit("start_load_done", requests=len(md.requests), restore_enabled=self.restore_enabled,
               elapsed_ms=f"{(time.perf_counter() - t0) * 1e3:.3f}")
 
@@ -657,7 +667,9 @@ class TurboBusConnector(KVConnectorBase_V1, SupportsHMA):
         rid = str(getattr(request, "request_id", "unknown"))
         if rid not in self.state.save_request_ids:
             return False, None
-        return True, {"turbobus.prefix_key": _prefix_key(p),
+        # The save already completed inside wait_for_save of the step that
+        # computed the prefix, so the blocks can be freed at once.
+        return False, {"turbobus.prefix_key": _prefix_key(p),
                       "turbobus.matched_tokens": _matched_for_save(p, self.vllm_block_size)}
 
     def request_finished_all_groups(self, request, block_ids: tuple[list[int], ...]):

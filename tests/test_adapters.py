@@ -242,11 +242,13 @@ def test_connector_match_needs_restore_enabled_and_saved_prefix():
     from pcie_pool_b200.adapters import vllm_kv_connector as K
 
     K._PREFIX_STORE.put(TurboBusSavedPrefix("p", [], 4, 64))
-    assert on.get_num_new_matched_tokens(r, 0) == (64, True)
-    assert on.get_num_new_matched_tokens(r, 32) == (32, True)
+    assert on.get_num_new_matched_tokens(r, 0) == (64, False)  # loaded synchronously in start_load_kv
+    assert on.get_num_new_matched_tokens(r, 32) == (32, False)
     full = Req(params=dict(r.kv_transfer_params), num_tokens=64)
-    assert on.get_num_new_matched_tokens(full, 0) == (63, True)  # last token is always computed
-    assert [e["event"] for e in get_connector_events()][-3:] == ["match", "match", "match"]
+    assert on.get_num_new_matched_tokens(full, 0) == (63, False)  # last token is always computed
+    asy = TurboBusConnector(Cfg({"turbobus.restore_enabled": True, "turbobus.load_async": True}), "scheduler")
+    assert asy.get_num_new_matched_tokens(r, 0) == (64, True)
+    assert [e["event"] for e in get_connector_events()].count("match") == 4
 
 
 def test_connector_save_waits_then_collects_from_scheduler_output():
@@ -258,7 +260,7 @@ def test_connector_save_waits_then_collects_from_scheduler_output():
         req_ids=["s1"], new_block_ids=[([7, 8, 9, 10],)]))
     md = c.build_connector_meta(out)
     assert [(m.request_id, m.block_ids, m.matched_tokens) for m in md.save_requests] == [("s1", (7, 8, 9, 10), 64)]
-    assert c.request_finished(r, [7, 8, 9, 10]) == (True, {"turbobus.prefix_key": "p",
+    assert c.request_finished(r, [7, 8, 9, 10]) == (False, {"turbobus.prefix_key": "p",
                                                            "turbobus.matched_tokens": 64})
     assert c.request_finished(Req("x"), []) == (False, None)
 
@@ -311,12 +313,12 @@ def test_connector_intent_path_save_then_restore_permuted(node):
 
     load = Req("l", {"turbobus.do_restore": True, "turbobus.prefix_key": "pfx"}, num_tokens=100)
     n, async_ = sched.get_num_new_matched_tokens(load, 0)
-    assert (n, async_) == (48, True)
+    assert (n, async_) == (48, False)
     sched.update_state_after_alloc(load, blocks([0, 11, 4, 13]), n)
     work.bind_connector_metadata(sched.build_connector_meta(None))
     work.start_load_kv(None)
     assert torch.equal(kv[:, [0, 11, 4]], expect)
-    assert work.get_finished(set()) == (None, {"l"})
+    assert work.get_finished(set()) == (None, None)  # synchronous load: nothing pending
     evs = [e["event"] for e in get_connector_events()]
     assert "save" in evs and "restore" in evs
 

@@ -1,0 +1,83 @@
+"""Intent benchmark CLIs against an in-process daemon whose executor moves
+bytes through the mock lanes (CPU)."""
+
+import json
+
+import numpy as np
+import pytest
+
+from pcie_pool_b200 import TurboBusClient
+from pcie_pool_b200.benchmarks import model_loading, summarize_result, training_offload
+from pcie_pool_b200.benchmarks.daemon_support import receipt_trace_line
+from pcie_pool_b200.daemon import InProcessDaemonClient, IntentExecutor, TurboBusDaemon
+from pcie_pool_b200.mock import MockDataPlane, MockWorld
+from pcie_pool_b200.topology import StaticTopologyProvider
+
+MiB = 1 << 20
+
+
+@pytest.fixture
+def node():
+    world = MockWorld(gpu_count=4)
+    d = TurboBusDaemon(relay_gpus=[1, 2, 3], max_inflight_chunks_per_relay=4096,
+                       topology_provider=StaticTopologyProvider(gpu_count=4),
+                       executor=IntentExecutor(MockDataPlane(world)))
+    d.put_profile(0, [1, 2, 3], world.profile(0))
+    dc = InProcessDaemonClient(d)
+    sid = dc.register_session(0, [1, 2, 3], max_inflight_chunks=4096).payload["session"]["session_id"]
+    host = np.random.default_rng(0).integers(0, 256, 16 * MiB, dtype=np.uint8)
+    gpu = world.alloc(0, 16 * MiB)
+    return dc, sid, host, gpu
+
+
+def _register(dc, job, sid, host, gpu):
+    assert dc.register_job(job, session_id=sid).ok
+    assert dc.register_buffer("host", job, "cpu_pinned", host.nbytes, address=host.ctypes.data, pinned=True).ok
+    assert dc.register_buffer("gpu", job, "gpu", gpu.nbytes, device_index=0, address=gpu.ctypes.data).ok
+
+
+def test_model_loading_cli(node, tmp_path, capsys):
+    dc, sid, host, gpu = node
+    _register(dc, "ml", sid, host, gpu)
+    args = model_loading.build_parser().parse_args([
+        "--session-id", sid, "--job-id", "ml", "--source-buffer-id", "host", "--destination-buffer-id", "gpu",
+        "--bucket-count", "4", "--bucket-bytes", str(4 * MiB), "--chunk-bytes", str(MiB), "--iterations", "2",
+        "--warmup", "1", "--wait-timeout-seconds", "60", "--daemon-socket-path", "unused",
+        "--json-output", str(tmp_path / "ml.json")])
+    res = model_loading.run_benchmark(args, client=TurboBusClient(daemon=dc))
+    assert np.array_equal(gpu, host)
+    s = res["summary"]
+    assert s["iterations"] == 2 and s["bytes_completed"] == 16 * MiB and s["relay_bytes"] > 0
+    text = model_loading.compact_summary(res)
+    assert text.startswith("MODEL_LOAD_SUMMARY_BEGIN") and "model_load_receipt" in text
+    model_loading.write_outputs(args, res, text)
+    assert summarize_result.compact_summary_for_result(json.loads((tmp_path / "ml.json").read_text())) == text
+
+
+def test_training_offload_cli_rotates_buckets(node):
+    dc, sid, host, gpu = node
+    _register(dc, "tr", sid, host, gpu)
+    args = training_offload.build_parser().parse_args([
+        "--session-id", sid, "--job-id", "tr", "--cpu-buffer-id", "host", "--gpu-buffer-id", "gpu",
+        "--bucket-count", "4", "--active-buckets", "2", "--bucket-bytes", str(4 * MiB), "--chunk-bytes", str(MiB),
+        "--iterations", "2", "--wait-timeout-seconds", "60", "--daemon-socket-path", "unused"])
+    assert training_offload.bucket_indices(4, 2, 0) == (0, 1)
+    assert training_offload.bucket_indices(4, 2, 1) == (2, 3)
+    res = training_offload.run_benchmark(args, client=TurboBusClient(daemon=dc))
+    assert np.array_equal(gpu, host), "prefetch of iterations 0 and 1 covered every bucket"
+    s = res["summary"]
+    assert s["prefetch"]["bytes"] == 8 * MiB and s["offload"]["bytes"] == 8 * MiB
+    text = training_offload.compact_summary(res)
+    assert "training_offload_prefetch_receipt" in text and text.endswith("TRAINING_OFFLOAD_SUMMARY_END")
+
+
+def test_receipt_trace_line_format(node):
+    dc, sid, host, gpu = node
+    _register(dc, "tl", sid, host, gpu)
+    args = model_loading.build_parser().parse_args([
+        "--session-id", sid, "--job-id", "tl", "--source-buffer-id", "host", "--destination-buffer-id", "gpu",
+        "--bucket-count", "1", "--bucket-bytes", str(MiB), "--iterations", "1", "--wait-timeout-seconds", "30",
+        "--daemon-socket-path", "unused"])
+    res = model_loading.run_benchmark(args, client=TurboBusClient(daemon=dc))
+    line = receipt_trace_line(model_loading.receipt_from_trace(res["samples"][0]["receipt"]))
+    assert line.startswith("daemon_receipt intent_id=") and "state=complete" in line
