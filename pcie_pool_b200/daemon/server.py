@@ -1918,9 +1918,18 @@ def direct_only(decision: SchedulingDecision) -> bool:
 
 
 def busy_relays(state: Mapping[str, Any]) -> set[int]:
-    return {int(p["relay_device"]) for p in state.get("active_paths", ()) or ()
-            if isinstance(p, Mapping) and str(p.get("kind", "")).lower() == "relay"
-            and p.get("relay_device") is not None}
+    """GPUs whose PCIe link is in use: relays of active relay paths and the
+    targets of active direct paths."""
+    out: set[int] = set()
+    for p in state.get("active_paths", ()) or ():
+        if not isinstance(p, Mapping):
+            continue
+        kind = str(p.get("kind", "")).lower()
+        if kind == "relay" and p.get("relay_device") is not None:
+            out.add(int(p["relay_device"]))
+        elif kind == "direct" and p.get("target_device") is not None:
+            out.add(int(p["target_device"]))
+    return out
 
 
 def job_runtime_state(weights: Mapping[str, float], records) -> dict[str, dict[str, Any]]:

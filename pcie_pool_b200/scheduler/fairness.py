@@ -85,9 +85,16 @@ def load_view(runtime_state: Mapping[str, object] | None, *, job_id: str | None,
     active = queued = 0
     if isinstance(runtime_state, Mapping):
         for rec in runtime_state.get("active_paths", ()) or ():
-            if isinstance(rec, Mapping) and str(rec.get("kind", "")).lower() == "relay" \
-                    and rec.get("relay_device") is not None:
+            if not isinstance(rec, Mapping):
+                continue
+            kind = str(rec.get("kind", "")).lower()
+            if kind == "relay" and rec.get("relay_device") is not None:
                 busy.add(int(rec["relay_device"]))
+            elif kind == "direct" and rec.get("target_device") is not None:
+                # A GPU whose own PCIe link is moving its own data has no link
+                # bandwidth to lend: relaying through it would only split the
+                # link between two transfers.
+                busy.add(int(rec["target_device"]))
         summary = runtime_state.get("summary", {})
         if isinstance(summary, Mapping):
             active = int(summary.get("active_transfer_count", 0) or 0)
