@@ -71,6 +71,7 @@ struct PoolEngine::Pending {
   int direction = 0;
   size_t total_chunks = 0;  // chunks in spec order (for the checksum vector)
   std::vector<int> spec_chunk_to_kernel;  // spec-order chunk -> kernel chunk (-1: none)
+  std::vector<int> kernel_lane_to_spec;   // kernel lane index -> spec lane index
   std::vector<LaneRec> lanes;
   std::vector<Ring*> rings;
   std::vector<int> ring_devices;
@@ -455,6 +456,7 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     const auto& L = s.lanes[li];
     if (R.ring) R.seq0 = R.ring->issued;
     if (R.kernel) {
+      P.kernel_lane_to_spec.push_back(static_cast<int>(li));
       LaneDesc d{};
       d.ring = R.staged ? R.ring->base : nullptr;
       d.ready = R.ring ? R.ring->ready : nullptr;
@@ -767,8 +769,17 @@ TransferResult PoolEngine::wait(uint64_t id, double host_timeout_s) {
       }
     }
     code = st[0];
+    // the kernel reports its own lane / chunk indices: map them to spec order
     res.error_lane = st[1];
+    if (st[1] >= 0 && static_cast<size_t>(st[1]) < P.kernel_lane_to_spec.size())
+      res.error_lane = P.kernel_lane_to_spec[st[1]];
     res.error_chunk = st[2];
+    for (size_t i = 0; st[2] >= 0 && i < P.spec_chunk_to_kernel.size(); ++i) {
+      if (P.spec_chunk_to_kernel[i] == st[2]) {
+        res.error_chunk = static_cast<int>(i);
+        break;
+      }
+    }
     res.error_detail = st[3];
   }
   if (!done) {

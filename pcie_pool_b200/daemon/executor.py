@@ -22,6 +22,8 @@ from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 from typing import Any, Protocol
 
+import numpy as np
+
 from ..schema import BufferRegistration, ExecutionTicket, TransferIntent
 
 
@@ -87,7 +89,13 @@ class IntentExecutor:
 class EngineDataPlane:
     """Runs tickets on the native PoolEngine (all GPUs of the node)."""
 
-    def __init__(self, engine=None, devices=None, *, checksum: bool = True, **engine_kw) -> None:
+    def __init__(self, engine=None, devices=None, *, checksum: bool = True, failover: bool = True,
+                 **engine_kw) -> None:
+        self.failover = failover
+        # tests: the next transfer drops the "ready" publications of this lane
+        # (so its landing wait runs out) and runs with this device timeout
+        self.debug_drop_publish = -1
+        self.failover_timeout_s = 0.0
         self._engine = engine
         self._devices = devices
         self._engine_kw = engine_kw
@@ -147,7 +155,7 @@ class EngineDataPlane:
     # -- execution ------------------------------------------------------------------------------
     def execute(self, ticket: ExecutionTicket, src: BufferRegistration, dst: BufferRegistration,
                 intent: TransferIntent | None) -> ExecutionResult:
-        from ..parallel.engine import D2H, H2D, lanes_from_plan
+        from ..parallel.engine import D2H, H2D, Lane, lanes_from_plan
 
         h2d = ticket.direction == "h2d"
         host_buf, dev_buf = (src, dst) if h2d else (dst, src)
@@ -156,8 +164,41 @@ class EngineDataPlane:
         dev_ptr = self.device_pointer(dev_buf)
         lanes = lanes_from_plan(ticket.plan, target)
         eng = self.engine
-        r = eng.run(H2D if h2d else D2H, target, host_ptr, host_buf.size_bytes, dev_ptr, dev_buf.size_bytes,
-                    lanes, checksum=self.checksum)
+        direction = H2D if h2d else D2H
+
+        def run(ls, drop=-1):
+            kw = {"debug_drop_publish": drop} if drop >= 0 else {}
+            if drop >= 0 and self.failover_timeout_s:
+                kw["timeout_s"] = self.failover_timeout_s
+            return eng.run(direction, target, host_ptr, host_buf.size_bytes, dev_ptr, dev_buf.size_bytes, ls,
+                           checksum=self.checksum, **kw)
+
+        drop, self.debug_drop_publish = self.debug_drop_publish, -1
+        r = run(lanes, drop)
+        failover = None
+        lane_stats = list(r.lanes)
+        checksums = None if r.checksums is None else np.array(r.checksums, dtype=np.uint64, copy=True)
+        if not r.ok and self.failover and len(lanes) > 1 and 0 <= r.error_lane < len(lanes):
+            # Lane failover: the chunks of the lane that failed are moved again
+            # over a surviving lane (the direct lane when it survived).  Every
+            # op here is a pure data movement, so chunks of the failed lane
+            # that did land are simply written again with the same bytes.
+            bad = lanes[r.error_lane]
+            survivors = [l for i, l in enumerate(lanes) if i != r.error_lane]
+            host = next((l for l in survivors if l.device == target), survivors[0])
+            redo = Lane(host.device, bad.src_off, bad.dst_off, bad.bytes, unit0=bad.unit0, tensor=bad.tensor,
+                        count=bad.count)
+            r2 = run([redo])
+            failover = {"failed_lane_device": int(bad.device), "rerun_on_device": int(host.device),
+                        "rerun_bytes": int(bad.total_bytes), "first_error": r.error, "rerun_ok": bool(r2.ok)}
+            if r2.ok:
+                first = sum(len(l.bytes) for l in lanes[:r.error_lane])
+                if checksums is not None and r2.checksums is not None and len(r2.checksums):
+                    checksums[first:first + len(bad.bytes)] = np.asarray(r2.checksums, dtype=np.uint64)
+                lane_stats = [l for i, l in enumerate(r.lanes) if i != r.error_lane] + list(r2.lanes)
+                r = type(r)(id=r.id, ok=True, status_code=0, error="", bytes=sum(l.total_bytes for l in lanes),
+                            cuda_ms=r.cuda_ms + r2.cuda_ms, submit_to_complete_ms=r.submit_to_complete_ms,
+                            gib_per_s=r.gib_per_s, lanes=lane_stats, checksums=checksums)
         measured = {
             "cuda_ms": r.cuda_ms, "gib_per_s": r.gib_per_s, "gb_per_s": r.gb_per_s,
             "submit_to_complete_ms": r.submit_to_complete_ms,
@@ -166,9 +207,13 @@ class EngineDataPlane:
                             "bytes": int(l.bytes), "chunk_count": int(l.chunks),
                             "cuda_ms": float(l.cuda_ms),
                             "gib_per_second": (l.bytes / (1 << 30)) / (l.cuda_ms / 1e3) if l.cuda_ms > 0 else 0.0}
-                           for l in r.lanes],
+                           for l in lane_stats],
         }
-        if self.checksum and r.checksums is not None and r.checksums.size:
+        if failover is not None:
+            measured["failover"] = failover
+            measured["fallback_reason"] = (f"lane failover: relay {failover['failed_lane_device']} failed, "
+                                           f"re-ran on {failover['rerun_on_device']}")
+        if self.checksum and r.checksums is not None and len(r.checksums):
             measured["chunk_checksums"] = [[int(a), int(b)] for a, b in r.checksums]
         return ExecutionResult(ok=r.ok, bytes_completed=r.bytes if r.ok else 0,
                                error=None if r.ok else r.error, measured=measured)

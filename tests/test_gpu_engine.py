@@ -302,3 +302,40 @@ def test_relay_scatter_units(need_two_gpus):
     src = host.numpy().reshape(64, unit)
     for i, b in enumerate(perm):
         assert np.array_equal(got[b], src[i])
+
+
+@pytest.mark.multigpu
+def test_daemon_lane_failover_reruns_failed_relay(need_two_gpus):
+    """A relay lane whose chunks are never published (the landing wait runs
+    out after 1 s) is re-run over the direct lane; the intent completes and
+    the bytes are exact."""
+    from pcie_pool_b200 import TransferIntent, TransferStatusState, TurboBusClient
+    from pcie_pool_b200.daemon import EngineDataPlane, InProcessDaemonClient, IntentExecutor, TurboBusDaemon
+    from pcie_pool_b200.topology import StaticTopologyProvider, synthetic_inventory
+
+    n = 64 << 20
+    host = _host(n, seed=21)
+    dev = torch.zeros(n, dtype=torch.uint8, device="cuda:0")
+    plane = EngineDataPlane(engine=_engine([0, 1], slot_bytes=4 << 20), checksum=True)
+    d = TurboBusDaemon([1], max_inflight_chunks_per_relay=4096,
+                       topology_provider=StaticTopologyProvider(synthetic_inventory(2, source="declared")),
+                       executor=IntentExecutor(plane))
+    link = {"h2d_bw_gbps": 50.0, "d2h_bw_gbps": 50.0, "p2p_bw_gbps": 700.0, "effective_bw_gbps": 50.0,
+            "effective_d2h_bw_gbps": 50.0, "p2p_enabled": True}
+    d.put_profile(0, [1], {"target_device": 0, "direct_h2d_bw_gbps": 50.0, "direct_d2h_bw_gbps": 50.0,
+                           "relays": [{"relay_device": 1, "target_device": 0, **link}]})
+    dc = InProcessDaemonClient(d)
+    sid = dc.register_session(0, [1], max_inflight_chunks=4096).payload["session"]["session_id"]
+    dc.register_job("fo", session_id=sid)
+    dc.register_buffer("h", "fo", "cpu_pinned", n, address=host.ptr, pinned=True)
+    dc.register_buffer("g", "fo", "gpu", n, device_index=0, address=dev.data_ptr())
+    plane.debug_drop_publish = 1  # the relay lane (spec lane 1) never publishes
+    plane.failover_timeout_s = 1.0
+    it = TransferIntent("fo-0", "fo", sid, "h", "g", "h2d", n, ({"src_offset": 0, "dst_offset": 0, "bytes": n},),
+                        metadata={"chunk_bytes": 4 << 20})
+    r = TurboBusClient(daemon=dc).transfer(it, timeout_seconds=120)
+    assert r.state is TransferStatusState.COMPLETE, r.error
+    assert torch.equal(dev.cpu(), torch.from_numpy(host.numpy()))
+    meas = r.metadata.get("measured", {})
+    assert meas.get("failover", {}).get("failed_lane_device") == 1
+    host.release()

@@ -259,3 +259,61 @@ def test_verification_pattern_and_daemon_seed():
     d = build_verification_daemon(0, 1, 8, 1 << 20)
     prof = d.get_profile(0, [1])
     assert prof.ok
+
+
+def test_engine_data_plane_lane_failover_logic():
+    """EngineDataPlane re-runs the chunks of a failed lane over a surviving
+    lane (CPU: a fake engine that fails lane 1 once, then moves bytes)."""
+    import ctypes
+
+    from pcie_pool_b200.daemon.executor import EngineDataPlane
+    from pcie_pool_b200.parallel.engine import LaneResult, TransferResult
+    from pcie_pool_b200.schema import BufferRegistration, ExecutionTicket
+
+    n = 8 * MiB
+    host = np.random.default_rng(4).integers(0, 256, n, dtype=np.uint8)
+    dev = np.zeros(n, dtype=np.uint8)
+
+    class FakeEngine:
+        def __init__(self):
+            self.calls = []
+
+        def run(self, direction, target, hp, hb, dp, db, lanes, checksum=False, **kw):
+            self.calls.append(([l.device for l in lanes], kw))
+            first = len(self.calls) == 1
+            stats = []
+            for i, l in enumerate(lanes):
+                if first and i == 1:
+                    continue
+                for s, d, b in zip(l.src_off, l.dst_off, l.bytes):
+                    ctypes.memmove(dp + int(d), hp + int(s), int(b))
+                stats.append(LaneResult(l.device, l.device == target, l.total_bytes, len(l.bytes), 1.0))
+            if first:
+                return TransferResult(1, False, 1, "timeout waiting for a staged chunk", 0, 1000.0, 0.0, 0.0,
+                                      stats, np.zeros((sum(len(l.bytes) for l in lanes), 2), np.uint64),
+                                      error_lane=1, error_chunk=3)
+            return TransferResult(2, True, 0, "", sum(l.total_bytes for l in lanes), 5.0, 0.0, 0.0, stats,
+                                  np.ones((sum(len(l.bytes) for l in lanes), 2), np.uint64))
+
+    eng = FakeEngine()
+    plane = EngineDataPlane(engine=eng, checksum=True)
+    plan = {"total_bytes": n, "assignments": [
+        {"path": {"kind": "direct", "direction": "h2d", "target_device": 0},
+         "chunks": [{"src_offset": o, "dst_offset": o, "bytes": MiB} for o in range(0, 4 * MiB, MiB)]},
+        {"path": {"kind": "relay", "direction": "h2d", "target_device": 0, "relay_device": 1},
+         "chunks": [{"src_offset": o, "dst_offset": o, "bytes": MiB} for o in range(4 * MiB, n, MiB)]}]}
+    t = ExecutionTicket(ticket_id="t", decision_id="d", intent_id="i", topology_snapshot_id="s", job_id="j",
+                        session_id="x", source_buffer_id="h", destination_buffer_id="g", direction="h2d",
+                        total_bytes=n, ranges=({"src_offset": 0, "dst_offset": 0, "bytes": n},), plan=plan,
+                        issued_at=0.0, expires_at=1.0)
+    src = BufferRegistration("h", "j", "cpu_pinned", n, address=host.ctypes.data, pinned=True)
+    dst = BufferRegistration("g", "j", "gpu", n, device_index=0, address=dev.ctypes.data)
+    res = plane.execute(t, src, dst, None)
+    assert res.ok and res.bytes_completed == n
+    assert np.array_equal(dev, host)
+    assert eng.calls[1][0] == [0], "failed relay chunks re-ran on the direct lane"
+    fo = res.measured["failover"]
+    assert fo["failed_lane_device"] == 1 and fo["rerun_on_device"] == 0 and fo["rerun_bytes"] == 4 * MiB
+    assert "lane failover" in res.measured["fallback_reason"]
+    # the re-run's checksums replaced the failed lane's entries (chunks 4..7)
+    assert res.measured["chunk_checksums"][4:] == [[1, 1]] * 4 and res.measured["chunk_checksums"][0] == [0, 0]
