@@ -171,6 +171,7 @@ PYBIND11_MODULE(_C, m) {
       .def_readwrite("checksum", &TransferSpec::checksum)
       .def_readwrite("stage_direct", &TransferSpec::stage_direct)
       .def_readwrite("debug_drop_publish", &TransferSpec::debug_drop_publish)
+      .def_readwrite("trace", &TransferSpec::trace)
       .def_readwrite("ctas_per_lane", &TransferSpec::ctas_per_lane)
       .def_readwrite("timeout_s", &TransferSpec::timeout_s)
       .def_readwrite("unit_bytes", &TransferSpec::unit_bytes)
@@ -209,7 +210,8 @@ PYBIND11_MODULE(_C, m) {
       .def_readonly("submit_to_complete_ms", &TransferResult::submit_to_complete_ms)
       .def_readonly("gib_per_s", &TransferResult::gib_per_s)
       .def_readonly("lanes", &TransferResult::lanes)
-      .def_readonly("checksums", &TransferResult::checksums);
+      .def_readonly("checksums", &TransferResult::checksums)
+      .def_readonly("trace", &TransferResult::trace);
 
   py::class_<PoolEngine>(m, "PoolEngine")
       .def(py::init<const std::vector<int>&, const EngineOptions&>(), py::arg("devices"),

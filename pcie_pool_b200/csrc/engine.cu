@@ -72,6 +72,7 @@ struct PoolEngine::Pending {
   size_t total_chunks = 0;  // chunks in spec order (for the checksum vector)
   std::vector<int> spec_chunk_to_kernel;  // spec-order chunk -> kernel chunk (-1: none)
   std::vector<int> kernel_lane_to_spec;   // kernel lane index -> spec lane index
+  bool trace = false;
   std::vector<LaneRec> lanes;
   std::vector<Ring*> rings;
   std::vector<int> ring_devices;
@@ -510,9 +511,11 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
   const size_t upload_bytes = off;
   const size_t o_csum = off; off = align_up(off + nk * 16, 256);
   const size_t o_status = off; off = align_up(off + 16, 256);
+  const size_t o_trace = off; off = align_up(off + (s.trace ? nk * kTraceWords * 8 : 0), 256);
   const size_t o_done = off; off = align_up(off + nk * 4, 256);
   const size_t scratch_bytes = off;
-  const size_t result_bytes = o_done - o_csum;  // csum + status
+  const size_t result_bytes = o_done - o_csum;  // csum + status (+ trace)
+  P.trace = s.trace;
 
   DeviceGuard tg(s.target);
   P.start = take_event(T);
@@ -571,6 +574,7 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     kp.csum = reinterpret_cast<unsigned long long*>(dsc + o_csum);
     kp.status = reinterpret_cast<int*>(dsc + o_status);
     kp.timeout_ns = static_cast<uint64_t>(P.timeout_s * 1e9);
+    kp.trace = s.trace ? reinterpret_cast<unsigned long long*>(dsc + o_trace) : nullptr;
     // Launch before any copy-engine work is queued: if the launch fails no
     // relay stream is left waiting for a kernel that never runs.
     const cudaError_t lrc = h2d ? launch_land(kp, static_cast<int>(cta), T.kern)
@@ -766,6 +770,15 @@ TransferResult PoolEngine::wait(uint64_t id, double host_timeout_s) {
       if (kc >= 0) {
         res.checksums[2 * i] = cs[2 * kc];
         res.checksums[2 * i + 1] = cs[2 * kc + 1];
+      }
+    }
+    if (P.trace) {
+      const uint64_t* tr = reinterpret_cast<const uint64_t*>(rh + align_up(nk * 16, 256) + 256);
+      res.trace.assign(P.total_chunks * kTraceWords, 0);
+      for (size_t i = 0; i < P.spec_chunk_to_kernel.size(); ++i) {
+        const int kc = P.spec_chunk_to_kernel[i];
+        if (kc >= 0)
+          for (int w = 0; w < kTraceWords; ++w) res.trace[kTraceWords * i + w] = tr[kTraceWords * kc + w];
       }
     }
     code = st[0];

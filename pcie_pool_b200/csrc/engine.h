@@ -76,6 +76,7 @@ struct TransferSpec {
   bool checksum = false;
   bool stage_direct = false;  // route a plain-copy direct lane through the landing ring
   int debug_drop_publish = -1;  // tests: lane whose "ready" publications are skipped
+  bool trace = false;        // record per-chunk %globaltimer stamps (TransferResult::trace)
   int ctas_per_lane = 0;     // 0: engine default
   double timeout_s = 0.0;    // 0: engine default
   uint32_t unit_bytes = 0;
@@ -108,6 +109,9 @@ struct TransferResult {
   double gib_per_s = 0.0;
   std::vector<LaneStats> lanes;
   std::vector<uint64_t> checksums;  // 2 per chunk, lanes in spec order
+  // 4 per chunk when TransferSpec::trace: {wait begin, ready, done, CTAs} in
+  // device nanoseconds (%globaltimer), zeros for chunks no kernel touched
+  std::vector<uint64_t> trace;
 };
 
 class PoolEngine {

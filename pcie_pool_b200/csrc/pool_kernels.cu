@@ -315,8 +315,11 @@ __global__ void __launch_bounds__(kLaneThreads, 1) land_kernel(const LaneKernelP
     const uint32_t cidx = L.chunk_begin + ci;
     const ChunkDesc c = p.chunks[cidx];
     if (threadIdx.x == 0) {
+      unsigned long long* tr = p.trace ? p.trace + uint64_t(kTraceWords) * cidx : nullptr;
+      if (tr && j == 0) tr[0] = globaltimer_ns();
       const bool ok = wait_flag_geq(L.ready, c.seq, globaltimer_ns() + p.timeout_ns);
       if (ok) fence_proxy_async_global();
+      if (tr && j == 0) tr[1] = globaltimer_ns();
       s_ok = ok ? 1 : 0;
     }
     __syncthreads();
@@ -368,7 +371,13 @@ __global__ void __launch_bounds__(kLaneThreads, 1) land_kernel(const LaneKernelP
     __syncthreads();
     if (threadIdx.x == 0) {
       const uint32_t old = G > 1 ? atom_add_acq_rel_gpu(p.done + cidx, 1u) : 0u;
-      if (old == G - 1 && L.freec) st_release_sys(L.freec, c.seq);
+      if (old == G - 1) {
+        if (p.trace) {
+          p.trace[uint64_t(kTraceWords) * cidx + 2] = globaltimer_ns();
+          p.trace[uint64_t(kTraceWords) * cidx + 3] = G;
+        }
+        if (L.freec) st_release_sys(L.freec, c.seq);
+      }
     }
   }
   if (threadIdx.x == 0) bulk_wait_all<0>();
@@ -400,7 +409,10 @@ __global__ void __launch_bounds__(kLaneThreads, 1) push_kernel(const LaneKernelP
     const ChunkDesc c = p.chunks[cidx];
     if (!L.in_place) {
       if (threadIdx.x == 0) {
+        unsigned long long* tr = p.trace ? p.trace + uint64_t(kTraceWords) * cidx : nullptr;
+        if (tr && j == 0) tr[0] = globaltimer_ns();
         s_ok = wait_flag_geq(L.freec, c.seq - L.slots, globaltimer_ns() + p.timeout_ns) ? 1 : 0;
+        if (tr && j == 0) tr[1] = globaltimer_ns();
       }
       __syncthreads();
       if (!s_ok) {
@@ -456,7 +468,13 @@ __global__ void __launch_bounds__(kLaneThreads, 1) push_kernel(const LaneKernelP
     __syncthreads();
     if (threadIdx.x == 0) {
       const uint32_t old = G > 1 ? atom_add_acq_rel_gpu(p.done + cidx, 1u) : 0u;
-      if (old == G - 1 && !L.in_place) st_release_sys(L.ready, c.seq);
+      if (old == G - 1) {
+        if (p.trace) {
+          p.trace[uint64_t(kTraceWords) * cidx + 2] = globaltimer_ns();
+          p.trace[uint64_t(kTraceWords) * cidx + 3] = G;
+        }
+        if (!L.in_place) st_release_sys(L.ready, c.seq);
+      }
     }
   }
   if (threadIdx.x == 0) bulk_wait_all<0>();

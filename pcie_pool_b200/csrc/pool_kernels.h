@@ -89,7 +89,14 @@ struct LaneKernelParams {
   unsigned long long* csum;     // per-chunk {sum, weighted} (zeroed per transfer)
   int* status;                  // {code, lane, chunk, detail} (first error wins)
   uint64_t timeout_ns;
+  // Optional per-chunk device trace (nullptr: off), kTraceWords words per
+  // kernel chunk of %globaltimer nanoseconds: {wait begin, ready (land: chunk
+  // published / push: slot free), chunk done (last CTA of the lane group),
+  // CTAs that finished the chunk}.
+  unsigned long long* trace;
 };
+
+constexpr int kTraceWords = 4;
 
 constexpr int kLaneThreads = 256;
 constexpr uint32_t kTileBytes = 32768;

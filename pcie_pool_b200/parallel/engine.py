@@ -89,6 +89,7 @@ class TransferResult:
     checksums: np.ndarray | None = None  # shape [chunks, 2] in lane order
     error_lane: int = -1
     error_chunk: int = -1
+    trace: np.ndarray | None = None  # [chunks, 4] device ns: wait begin, ready, done, CTAs (lane order)
 
     @property
     def gb_per_s(self) -> float:
@@ -128,7 +129,7 @@ class PoolEngine:
                unit_bytes: int = 0, unit_addrs: np.ndarray | None = None,
                ranges: tuple[np.ndarray, np.ndarray, np.ndarray] | None = None,
                tensors: Sequence[tuple[int, int, int, int]] = (),
-               debug_drop_publish: int = -1) -> int:
+               debug_drop_publish: int = -1, trace: bool = False) -> int:
         C = self._C
         spec = C.TransferSpec()
         spec.direction = int(direction)
@@ -141,6 +142,7 @@ class PoolEngine:
         spec.checksum = bool(checksum)
         spec.stage_direct = bool(stage_direct)
         spec.debug_drop_publish = int(debug_drop_publish)
+        spec.trace = bool(trace)
         spec.ctas_per_lane = int(ctas_per_lane)
         spec.timeout_s = float(timeout_s)
         spec.unit_bytes = int(unit_bytes)
@@ -171,12 +173,13 @@ class PoolEngine:
     def wait(self, tid: int, host_timeout_s: float = 0.0) -> TransferResult:
         r = self._eng.wait(tid, host_timeout_s)
         cs = np.array(r.checksums, dtype=np.uint64).reshape(-1, 2)
+        tr = np.array(r.trace, dtype=np.uint64).reshape(-1, 4) if len(r.trace) else None
         return TransferResult(
             id=r.id, ok=r.ok, status_code=r.status_code, error=r.error, bytes=r.bytes,
             cuda_ms=r.cuda_ms, submit_to_complete_ms=r.submit_to_complete_ms,
             gib_per_s=r.gib_per_s,
             lanes=[LaneResult(l.device, l.direct, l.bytes, l.chunks, l.cuda_ms) for l in r.lanes],
-            checksums=cs, error_lane=r.error_lane, error_chunk=r.error_chunk)
+            checksums=cs, error_lane=r.error_lane, error_chunk=r.error_chunk, trace=tr)
 
     def query(self, tid: int) -> bool:
         return self._eng.query(tid)

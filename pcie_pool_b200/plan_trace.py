@@ -127,5 +127,35 @@ def chrome_trace(record: Mapping[str, Any], t0_us: float = 0.0) -> dict:
     return {"traceEvents": events, "displayTimeUnit": "ms"}
 
 
-__all__ = ["TRACE_FORMAT", "chrome_trace", "plan_from_dict", "read_trace", "trace_record",
+
+def device_trace_events(result, lanes, *, name: str = "transfer", pid: int = 0) -> list[dict]:
+    """Chrome-trace events from a transfer run with ``trace=True``: per lane
+    (one track per lane device) and chunk, a ``wait`` span (until the chunk
+    was published -- H2D -- or its staging slot was free -- D2H) and a
+    ``move`` span (until the last CTA finished it).  Times are the device's
+    %globaltimer in microseconds relative to the earliest stamp."""
+    tr = getattr(result, "trace", None)
+    if tr is None or not len(tr):
+        return []
+    stamps = [int(x) for x in tr[:, 0] if int(x)]
+    if not stamps:
+        return []
+    t0 = min(stamps)
+    out, i = [], 0
+    for lane in lanes:
+        for k in range(len(lane.bytes)):
+            a, b, c, ctas = (int(x) for x in tr[i])
+            i += 1
+            if not a:
+                continue
+            args = {"chunk": k, "bytes": int(lane.bytes[k]), "ctas": ctas}
+            out.append({"name": f"{name}:wait", "ph": "X", "pid": pid, "tid": int(lane.device),
+                        "ts": (a - t0) / 1e3, "dur": max(0, b - a) / 1e3, "args": args})
+            if c:
+                out.append({"name": f"{name}:move", "ph": "X", "pid": pid, "tid": int(lane.device),
+                            "ts": (b - t0) / 1e3, "dur": max(0, c - b) / 1e3, "args": args})
+    return out
+
+
+__all__ = ["TRACE_FORMAT", "chrome_trace", "device_trace_events", "plan_from_dict", "read_trace", "trace_record",
            "transfer_plan_to_dict", "validate_plan_dict", "write_trace"]

@@ -339,3 +339,24 @@ def test_daemon_lane_failover_reruns_failed_relay(need_two_gpus):
     meas = r.metadata.get("measured", {})
     assert meas.get("failover", {}).get("failed_lane_device") == 1
     host.release()
+
+
+def test_device_trace_stamps_are_ordered(need_gpu):
+    """trace=True records per-chunk %globaltimer stamps: wait begin <= ready
+    <= done for every staged chunk, exported as Chrome-trace spans."""
+    from pcie_pool_b200.parallel.engine import H2D, split_even
+    from pcie_pool_b200.plan_trace import device_trace_events
+
+    n = 24 << 20
+    host = _host(n, seed=31)
+    dev = torch.zeros(n, dtype=torch.uint8, device="cuda:0")
+    lanes = split_even(n, 4 << 20, [0])
+    r = _engine([0], slot_bytes=4 << 20).run(H2D, 0, host.ptr, n, dev.data_ptr(), n, lanes, checksum=True,
+                                             stage_direct=True, trace=True)
+    assert r.ok, r.error
+    assert r.trace is not None and r.trace.shape == (6, 4)
+    for a, b, c, ctas in r.trace.astype(np.int64):
+        assert 0 < a <= b <= c and ctas >= 1
+    ev = device_trace_events(r, lanes)
+    assert len(ev) == 12 and {e["name"] for e in ev} == {"transfer:wait", "transfer:move"}
+    host.release()
