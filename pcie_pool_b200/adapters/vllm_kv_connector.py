@@ -652,13 +652,13 @@ class TurboBusConnector(KVConnectorBase_V1, SupportsHMA):
 
     # ---- completion ----------------------------------------------------------------------------
     def get_finished(self, finished_req_ids: set[str]):
-        sending = set(self.state.finished_sending)
+        # Saves complete inside wait_for_save and request_finished never
+        # delays the free, so there is nothing "sending" to report (vLLM has
+        # already dropped finished requests); only asynchronous loads report.
         if finished_req_ids:
-            sending |= self.state.saved_request_ids & set(finished_req_ids)
-            self.state.saved_request_ids -= sending
-        self.state.finished_sending -= sending
+            self.state.saved_request_ids -= set(finished_req_ids)
         recving, self.state.finished_recving = self.state.finished_recving, set()
-        return sending or None, recving or None
+        return None, recving or None
 
     def request_finished(self, request, block_ids: list[int]):
         p = _params(request)

@@ -27,10 +27,11 @@ import os
 import threading
 import time
 import uuid
-from dataclasses import asdict, dataclass, field
+from dataclasses import dataclass, field
 from typing import Any, Callable, Iterable, Mapping
 
 from ..scheduler import DaemonScheduler, scheduling_decision_leases, scheduling_decision_stats
+from ..schema import contract_asdict as asdict
 from ..schema import (BufferRegistration, CleanupRequest, DaemonRequest, DaemonResponse,
                       ExecutionTicket, JobIdentity, LeaseToken, PeerIdentity, RelayQuota, RequestType,
                       SchedulingDecision, Session, TERMINAL_STATES, TransferIntent, TransferReceipt,

@@ -13,7 +13,7 @@ Bandwidth fields named ``*_gbps`` carry GiB/s, as in the reference
 
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, fields, is_dataclass
 from enum import Enum
 from typing import Any, Callable, Mapping
 
@@ -84,6 +84,27 @@ class SchedulingDecisionState(str, Enum):
     PLANNED = "planned"
     FALLBACK = "fallback"
     REJECTED = "rejected"
+
+
+# ---- record conversion ----------------------------------------------------------------
+
+def contract_asdict(obj: Any) -> dict[str, Any]:
+    """Dict of a contract for responses: nested contracts are converted, the
+    top-level containers are copied, but their contents (plan chunk lists,
+    ranges) are shared rather than deep-copied.  Contracts are immutable once
+    issued, and a plan of N chunks would otherwise be copied N-deep on every
+    response (``dataclasses.asdict`` dominated the per-intent control cost)."""
+    out: dict[str, Any] = {}
+    for f in fields(obj):
+        v = getattr(obj, f.name)
+        if is_dataclass(v) and not isinstance(v, type):
+            v = contract_asdict(v)
+        elif isinstance(v, dict):
+            v = dict(v)
+        elif isinstance(v, list):
+            v = list(v)
+        out[f.name] = v
+    return out
 
 
 # ---- field coercers ------------------------------------------------------------------
