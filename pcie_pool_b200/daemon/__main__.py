@@ -45,6 +45,9 @@ def startup_config_from_args(args) -> DaemonStartupConfig:
 
 
 def main(argv=None) -> None:
+    from ..utils.log import configure_from_env
+
+    configure_from_env()
     parser = build_parser()
     args = parser.parse_args(argv)
     try:

@@ -32,6 +32,7 @@ from typing import Any, Callable, Iterable, Mapping
 
 from ..scheduler import DaemonScheduler, scheduling_decision_leases, scheduling_decision_stats
 from ..schema import contract_asdict as asdict
+from ..utils.log import logger
 from ..schema import (BufferRegistration, CleanupRequest, DaemonRequest, DaemonResponse,
                       ExecutionTicket, JobIdentity, LeaseToken, PeerIdentity, RelayQuota, RequestType,
                       SchedulingDecision, Session, TERMINAL_STATES, TransferIntent, TransferReceipt,
@@ -45,6 +46,7 @@ DELAYED = "delayed"
 EXPIRED = "expired"
 PLAN_TTL_SECONDS = 30.0
 TICKET_ISSUER = "turbobus-daemon"
+_LOG = logger("daemon")
 TOPOLOGY_UNAVAILABLE = "topology provider is required; synthetic topology is test fixture only"
 PROFILE_STORE_FORMAT = "pcie_pool_b200.profile_cache.v1"
 
@@ -886,6 +888,13 @@ class TurboBusDaemon:
     def executor_finished(self, transfer_id: str, *, ok_: bool, bytes_completed: int,
                           error: str | None = None, measured: dict | None = None) -> None:
         """Record the data plane's outcome: status, measured stats, leases."""
+        m = measured or {}
+        if ok_:
+            _LOG.info("transfer_complete", transfer_id=transfer_id, bytes=int(bytes_completed),
+                      cuda_ms=float(m.get("cuda_ms", 0.0) or 0.0), gb_per_s=float(m.get("gb_per_s", 0.0) or 0.0),
+                      lanes=len(m.get("path_stats", ()) or ()), fallback=m.get("fallback_reason", ""))
+        else:
+            _LOG.warning("transfer_failed", transfer_id=transfer_id, bytes=int(bytes_completed), error=error or "")
         with self._lock:
             if measured:
                 self._st.measured[transfer_id] = dict(measured)
