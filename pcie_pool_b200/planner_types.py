@@ -82,9 +82,12 @@ class PlannerPathAssignment:
         return sum(c.bytes for c in self.chunks)
 
     def as_dict(self) -> dict[str, object]:
-        chunks = [c.as_dict() for c in self.chunks]
+        # flat records: built directly (dataclasses.asdict per chunk dominated
+        # the cost of converting plans with thousands of chunks)
+        chunks = [{"src_offset": c.src_offset, "dst_offset": c.dst_offset, "bytes": c.bytes,
+                   "relay_device": c.relay_device} for c in self.chunks]
         return {"path": self.path.as_dict(), "chunks": chunks,
-                "bytes": sum(c["bytes"] for c in chunks), "chunk_count": len(chunks)}
+                "bytes": sum(c.bytes for c in self.chunks), "chunk_count": len(chunks)}
 
 
 @dataclass(frozen=True)
