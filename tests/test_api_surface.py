@@ -1,0 +1,222 @@
+"""Public surface on the CPU: package boundaries, runtime-engine
+marshalling, the backend's IPC-handle checks, the offload-store state
+machine, phase-7 and paper-validation tooling on synthetic reports, and the
+examples' import-level entry points.  Mirrors test_package_boundaries,
+test_runtime_engine, test_backend_cuda, test_offload_store,
+test_phase7_* and test_paper_validation of the reference."""
+
+import json
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+
+def test_control_plane_imports_without_vllm():
+    code = ("import sys, pcie_pool_b200, pcie_pool_b200.daemon, pcie_pool_b200.worker, pcie_pool_b200.scheduler; "
+            "print(','.join(m for m in ('vllm', 'pcie_pool_b200.adapters') if m in sys.modules))")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True).stdout.strip()
+    assert out == ""
+
+
+def test_daemon_requires_a_topology_provider():
+    from pcie_pool_b200.daemon import TurboBusDaemon
+
+    d = TurboBusDaemon(relay_gpus=[1])
+    inv, disc = d.get_inventory(), d.discover_relays(target_gpu=0, requested_relays=[1])
+    assert not inv.ok and not disc.ok
+    assert "topology provider is required" in inv.error and "topology provider is required" in disc.error
+
+
+def test_runtime_options_from_json(tmp_path):
+    from pcie_pool_b200.runtime_engine import RuntimeOptions
+
+    (tmp_path / "t.json").write_text(json.dumps({"best": {"chunk_bytes": 8 << 20, "staging_slots": 4}}))
+    o = RuntimeOptions.from_tuning_json(tmp_path / "t.json")
+    assert (o.chunk_bytes, o.staging_slots) == (8 << 20, 4)
+    (tmp_path / "p.json").write_text(json.dumps({"config": {"chunk_bytes": 4 << 20, "profile_bytes": 1 << 20}}))
+    o = RuntimeOptions.from_profile_json(tmp_path / "p.json")
+    assert (o.chunk_bytes, o.profile_bytes) == (4 << 20, 1 << 20)
+    (tmp_path / "bad.json").write_text(json.dumps({"best": 3}))
+    with pytest.raises(ValueError):
+        RuntimeOptions.from_tuning_json(tmp_path / "bad.json")
+    assert o.planner_options().min_chunks_for_relay == 2
+
+
+def test_plan_to_lanes_validation():
+    from pcie_pool_b200.runtime_engine import plan_to_lanes
+
+    plan = {"total_bytes": 3 << 20, "chunk_bytes": 1 << 20, "assignments": [
+        {"path": {"kind": "direct", "enabled": True}, "chunks": [{"src_offset": 0, "dst_offset": 0, "bytes": 1 << 20}]},
+        {"path": {"kind": "relay", "relay_device": 2, "enabled": True},
+         "chunks": [{"src_offset": 1 << 20, "dst_offset": 1 << 20, "bytes": 2 << 20}]}]}
+    lanes = plan_to_lanes(plan, 0, source_bytes=3 << 20, destination_bytes=3 << 20)
+    assert [l.device for l in lanes] == [0, 2] and lanes[1].total_bytes == 2 << 20
+    with pytest.raises(ValueError, match="past"):
+        plan_to_lanes(plan, 0, source_bytes=2 << 20)
+    bad = json.loads(json.dumps(plan))
+    bad["assignments"][1]["path"]["enabled"] = False
+    with pytest.raises(ValueError, match="disabled"):
+        plan_to_lanes(bad, 0)
+    bad = dict(plan, total_bytes=5)
+    with pytest.raises(ValueError, match="total_bytes"):
+        plan_to_lanes(bad, 0)
+
+
+def test_profile_daemon_roundtrip():
+    from pcie_pool_b200.runtime_engine import profile_from_daemon_entry, profile_to_daemon_dict
+
+    d = {"target_device": 0, "direct_h2d_bw_gbps": 50.0, "direct_d2h_bw_gbps": 52.0,
+         "relays": [{"relay_device": 3, "target_device": 0, "h2d_bw_gbps": 40.0, "d2h_bw_gbps": 41.0,
+                     "p2p_bw_gbps": 700.0, "effective_bw_gbps": 40.0, "effective_d2h_bw_gbps": 41.0,
+                     "p2p_enabled": True}]}
+    p = profile_from_daemon_entry({"profile": d}, 0)
+    assert p.relays[0].relay_device == 3 and p.direct_d2h_bw_gbps == 52.0
+    assert profile_to_daemon_dict(p) == d
+    with pytest.raises(ValueError):
+        profile_from_daemon_entry({"profile": {"direct_h2d_bw_gbps": 0}}, 0)
+
+
+def test_backend_ipc_handle_checks():
+    from pcie_pool_b200.backends.cuda import coerce_ipc_handle
+
+    h = bytes(range(64))
+    assert coerce_ipc_handle(h) == h and coerce_ipc_handle(h.hex()) == h
+    with pytest.raises(ValueError):
+        coerce_ipc_handle(b"short")
+
+
+def test_offload_store_state_machine():
+    from pcie_pool_b200.offload_store import AdapterTransferContext, BlockState, OffloadStore
+    from pcie_pool_b200.schema import TransferReceipt, TransferStatusState
+
+    class Client:
+        def __init__(self):
+            self.intents = []
+
+        def submit_transfer_intent(self, intent):
+            self.intents.append(intent)
+            return self._receipt(intent, TransferStatusState.RUNNING)
+
+        def wait_transfer_receipt(self, intent_id, timeout_seconds=None):
+            it = next(i for i in self.intents if i.intent_id == intent_id)
+            return self._receipt(it, TransferStatusState.COMPLETE)
+
+        @staticmethod
+        def _receipt(it, state):
+            return TransferReceipt(receipt_id="r-" + it.intent_id, ticket_id="t", intent_id=it.intent_id,
+                                   decision_id="d", topology_snapshot_id="s", job_id=it.job_id,
+                                   session_id=it.session_id, state=state, bytes_total=it.total_bytes,
+                                   bytes_completed=it.total_bytes if state is TransferStatusState.COMPLETE else 0,
+                                   started_at=0.0, path_stats=({"kind": "direct", "bytes": it.total_bytes,
+                                                                "chunk_count": 1},))
+
+    class T:
+        def __init__(self, n):
+            self.n = n
+
+        def numel(self):
+            return self.n
+
+        def element_size(self):
+            return 1
+
+    c = Client()
+    store = OffloadStore(c, AdapterTransferContext("j", "s", "cpu", "gpu", intent_prefix="st"))
+    cpu, gpu = T(4096), T(4096)
+    for i in range(4):
+        store.add(f"b{i}", cpu, gpu, cpu_offset=i * 1024, gpu_offset=i * 1024, byte_count=1024)
+    with pytest.raises(ValueError):
+        store.add("b0", cpu, gpu)
+    store.prefetch_many(["b0", "b1", "b2"])
+    assert len(c.intents) == 1 and len(c.intents[0].ranges) == 3  # one batched multi-range intent
+    assert c.intents[0].intent_id == "st-prefetch-1"
+    assert store.block("b0").state is BlockState.PREFETCHING
+    store.wait_many(["b0", "b1", "b2"])
+    assert store.block("b1").state is BlockState.GPU and store.block("b3").state is BlockState.CPU
+    store.evict("b1")
+    store.wait("b1")
+    assert store.block("b1").state is BlockState.CPU
+    assert store.transfer_stats_many(["b0"]).bytes == 3072
+
+
+def _report(policy, ms):
+    return {"config": {"policy": policy}, "workloads": [{"workload": "model-loading", "status": "passed",
+                                                         "returncode": 0, "data_path": "", "metrics": [{
+        "workload": "model-loading", "report_schema": "x", "policy": policy, "job_id": "j", "session_id": "s",
+        "workload_kind": "model_weights", "transfer_ms": ms, "performance_ms": ms, "throughput_gib_s": 1000 / ms,
+        "transfer_bytes": 10, "bytes_completed": 10, "direct_bytes": 10, "relay_bytes": 0,
+        "correctness_status": "complete", "decision_ids": "d1"}]}]}
+
+
+def test_phase7_compare_check_gate_inventory(tmp_path):
+    from pcie_pool_b200.benchmarks import phase7
+
+    base, pooled = _report("paper-baseline", 20.0), _report("turbobus-daemon", 10.0)
+    cmp_ = phase7.compare_reports(base, pooled)
+    row = cmp_["workloads"][0]
+    assert row["p50_speedup"] == pytest.approx(2.0) and row["throughput_ratio"] == pytest.approx(2.0)
+    assert phase7.check_report(pooled)["ok"]
+    broken = json.loads(json.dumps(pooled))
+    broken["workloads"][0]["metrics"][0]["bytes_completed"] = 3
+    assert "model-loading:bytes_incomplete" in phase7.check_report(broken)["errors"]
+    ev = phase7.evidence_report(pooled, {"audit_records": [{"job_id": "j", "event_type": "worker_completion"}],
+                                         "relay_quotas": {"1": {"active_chunks": 0}}, "reservations": {}})
+    assert ev["ok"] and ev["metrics"][0]["audit_records"] == 1
+    gate = phase7.gate_bundle("8gpu", base, pooled, cmp_, [ev], required=("model-loading",))
+    assert gate["status"] == "accepted", gate["reasons"]
+    gp = tmp_path / "gate.json"
+    gp.write_text(json.dumps(gate))
+    manifest = phase7.ingest(tmp_path / "manifest.json", gp)
+    inv = phase7.inventory(manifest)
+    assert inv["accepted"] == ["8gpu"] and not inv["complete"]
+    plan = phase7.server_run_plan(phase7.build_parser().parse_args(["server-run", "--server-class", "2gpu",
+                                                                    "--output-root", str(tmp_path)]))
+    assert [s["name"] for s in plan["steps"]][:2] == ["paper-validation-baseline", "paper-validation-pooled"]
+
+
+def test_paper_validation_dry_run_and_metric_line(tmp_path):
+    from pcie_pool_b200.benchmarks import paper_validation as pv
+
+    args = pv.build_parser().parse_args(["--session-id", "s", "--cpu-buffer-id", "c", "--gpu-buffer-id", "g",
+                                         "--dry-run", "--output-dir", str(tmp_path)])
+    rep = pv.run_validation(args)
+    assert [w["status"] for w in rep["workloads"]] == ["dry_run"] * 4
+    assert "PAPER_VALIDATION_SUMMARY_BEGIN" in pv.compact_summary(rep)
+    m = pv.collect_model_metrics({"config": {"job_id": "j", "session_id": "s", "source_buffer_id": "c",
+                                             "destination_buffer_id": "g", "workload_kind": "model_weights"},
+                                  "summary": {"iterations": 2, "median_load_ms": 5.0, "median_gib_per_second": 2.0,
+                                              "bytes": 100, "bytes_completed": 100, "decision_ids": ["d"]}},
+                                 "turbobus-daemon")[0]
+    assert not pv.metric_errors(m)
+    assert pv.metric_line(m).startswith("paper_metric workload=model-loading report_schema=")
+
+
+def test_examples_entry_points():
+    from pcie_pool_b200.examples.framework_kv_slot_adapter import make_contiguous_slots
+    from pcie_pool_b200.examples.torch_tensor_fetch import build_intent, main
+    from pcie_pool_b200.examples.vllm_kv_connector import SHAPES, write_model_dir
+
+    assert len(make_contiguous_slots("x", 3, 4096)) == 3
+    cfg = json.loads(open(write_model_dir("tiny", 2048) + "/config.json").read())
+    assert cfg["num_hidden_layers"] == SHAPES["tiny"]["num_hidden_layers"] and cfg["head_dim"] == 128
+    args = type("A", (), dict(intent_id="i", job_id="j", session_id="s", source_buffer_id="a",
+                              destination_buffer_id="b", direction="h2d", bytes=16, src_offset=0, dst_offset=0,
+                              policy="p"))()
+    assert build_intent(args).total_bytes == 16
+    with pytest.raises(SystemExit):
+        main(["--bytes", "16"])  # needs a daemon socket unless --self-contained
+
+
+def test_checksum_rebase_matches_whole_buffer():
+    from pcie_pool_b200.parallel.engine import Lane
+    from pcie_pool_b200.utils.checksum import checksum_bytes, combine, rebase_chunk_sums
+
+    data = np.random.default_rng(1).integers(0, 256, 4096 + 12, dtype=np.uint8)
+    offs = [0, 1024, 2048, 3072, 4096]
+    sizes = [1024, 1024, 1024, 1024, 12]
+    lanes = [Lane(0, np.array(offs[:3], np.uint64), np.zeros(3, np.uint64), np.array(sizes[:3], np.uint64)),
+             Lane(1, np.array(offs[3:], np.uint64), np.zeros(2, np.uint64), np.array(sizes[3:], np.uint64))]
+    sums = [checksum_bytes(data[o:o + n]) for o, n in zip(offs, sizes)]
+    assert combine(rebase_chunk_sums(sums, lanes)) == checksum_bytes(data)
