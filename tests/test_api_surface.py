@@ -220,3 +220,19 @@ def test_checksum_rebase_matches_whole_buffer():
              Lane(1, np.array(offs[3:], np.uint64), np.zeros(2, np.uint64), np.array(sizes[3:], np.uint64))]
     sums = [checksum_bytes(data[o:o + n]) for o, n in zip(offs, sizes)]
     assert combine(rebase_chunk_sums(sums, lanes)) == checksum_bytes(data)
+
+
+def test_device_trace_events_from_stamps():
+    from types import SimpleNamespace
+
+    from pcie_pool_b200.parallel.engine import Lane
+    from pcie_pool_b200.plan_trace import device_trace_events
+
+    lanes = [Lane(0, np.array([0, 10], np.uint64), np.zeros(2, np.uint64), np.array([10, 10], np.uint64)),
+             Lane(3, np.array([20], np.uint64), np.zeros(1, np.uint64), np.array([10], np.uint64))]
+    tr = np.array([[1000, 1500, 4000, 4], [4000, 4000, 6000, 4], [1200, 3000, 5000, 4]], np.uint64)
+    ev = device_trace_events(SimpleNamespace(trace=tr), lanes, name="x")
+    assert [(e["name"], e["tid"], e["ts"], e["dur"]) for e in ev][:2] == [("x:wait", 0, 0.0, 0.5),
+                                                                          ("x:move", 0, 0.5, 2.5)]
+    assert {e["tid"] for e in ev} == {0, 3} and len(ev) == 6
+    assert device_trace_events(SimpleNamespace(trace=None), lanes) == []
