@@ -102,6 +102,46 @@ class Tenants:
                 h.release()
 
 
+TRANSFER_TIMEOUT_S = 180.0
+LINK_GIBPS = 51.6  # one Gen5 x16 link alone (measured 55.4 GB/s)
+
+
+def shard_job(job: int, gpu: int) -> str:
+    """Daemon job of one GPU shard: a daemon job is bound to one session and a
+    session to one target GPU, so every shard is its own job; the tenant's
+    weight is split between its shards."""
+    return f"job{job}-gpu{gpu}"
+
+
+def setup_tenants(daemon, dc, gpus, job_of, gpus_per_job: int, n: int, addrs) -> dict:
+    """Profile, session, job and the four buffers of every GPU shard;
+    ``addrs[g] = (host params, host grads, device params, device grads)``."""
+    sessions = {}
+    for g in gpus:
+        relays = [r for r in gpus if r != g]
+        daemon.put_profile(g, relays, {
+            "target_device": g, "direct_h2d_bw_gbps": LINK_GIBPS, "direct_d2h_bw_gbps": LINK_GIBPS,
+            "relays": [{"relay_device": r, "target_device": g, "h2d_bw_gbps": LINK_GIBPS, "d2h_bw_gbps": LINK_GIBPS,
+                        "p2p_bw_gbps": 700.0, "effective_bw_gbps": LINK_GIBPS, "effective_d2h_bw_gbps": LINK_GIBPS,
+                        "p2p_enabled": True} for r in relays]})
+        r = dc.register_session(g, relays, max_inflight_chunks=1 << 16)
+        if not r.ok:
+            raise RuntimeError(r.error)
+        sid = r.payload["session"]["session_id"]
+        job = shard_job(job_of[g], g)
+        r = dc.register_job(job, user_id=f"tenant{job_of[g]}", session_id=sid, weight=1.0 / gpus_per_job)
+        if not r.ok:
+            raise RuntimeError(r.error)
+        hp, hg, dp, dg = addrs[g]
+        for name, kind, dev, addr in ((f"hp{g}", "cpu_pinned", None, hp), (f"hg{g}", "cpu_pinned", None, hg),
+                                      (f"dp{g}", "gpu", g, dp), (f"dg{g}", "gpu", g, dg)):
+            r = dc.register_buffer(name, job, kind, n, device_index=dev, address=addr, pinned=kind == "cpu_pinned")
+            if not r.ok:
+                raise RuntimeError(r.error)
+        sessions[g] = sid
+    return sessions
+
+
 def run_ours(a) -> dict:
     import torch
 
@@ -124,23 +164,9 @@ def run_ours(a) -> dict:
                             executor=IntentExecutor(EngineDataPlane(engine=eng, checksum=True),
                                                     max_workers=4 * len(gpus)))
     dc = InProcessDaemonClient(daemon)
-    link = 51.6  # GiB/s, one Gen5 x16 link alone (measured 55.4 GB/s)
-    sessions = {}
-    for g in gpus:
-        relays = [r for r in gpus if r != g]
-        daemon.put_profile(g, relays, {"target_device": g, "direct_h2d_bw_gbps": link, "direct_d2h_bw_gbps": link,
-                                       "relays": [{"relay_device": r, "target_device": g, "h2d_bw_gbps": link,
-                                                   "d2h_bw_gbps": link, "p2p_bw_gbps": 700.0,
-                                                   "effective_bw_gbps": link, "effective_d2h_bw_gbps": link,
-                                                   "p2p_enabled": True} for r in relays]})
-        sid = dc.register_session(g, relays, max_inflight_chunks=1 << 16).payload["session"]["session_id"]
-        job = f"job{T.job_of[g]}"
-        dc.register_job(job, session_id=sid)
-        dc.register_buffer(f"hp{g}", job, "cpu_pinned", T.n, address=T.host_params[g].ptr, pinned=True)
-        dc.register_buffer(f"hg{g}", job, "cpu_pinned", T.n, address=T.host_grads[g].ptr, pinned=True)
-        dc.register_buffer(f"dp{g}", job, "gpu", T.n, device_index=g, address=T.dev_params[g].data_ptr())
-        dc.register_buffer(f"dg{g}", job, "gpu", T.n, device_index=g, address=T.dev_grads[g].data_ptr())
-        sessions[g] = sid
+    sessions = setup_tenants(daemon, dc, gpus, T.job_of, a.gpus_per_job, T.n,
+                             {g: (T.host_params[g].ptr, T.host_grads[g].ptr, T.dev_params[g].data_ptr(),
+                                  T.dev_grads[g].data_ptr()) for g in gpus})
     client = TurboBusClient(daemon=dc)
     active = gpus[:(a.active_jobs or a.jobs) * a.gpus_per_job]
     rng = ({"src_offset": 0, "dst_offset": 0, "bytes": T.n},)
@@ -148,7 +174,7 @@ def run_ours(a) -> dict:
     pool = ThreadPoolExecutor(max_workers=2 * len(active))
 
     def one(g, kind):
-        job = f"job{T.job_of[g]}"
+        job = shard_job(T.job_of[g], g)
         i = next(counter)
         if kind == "grads":
             it = TransferIntent(f"{job}-g{g}-grads-{i}", job, sessions[g], f"dg{g}", f"hg{g}", "d2h", T.n, rng,
@@ -157,7 +183,7 @@ def run_ours(a) -> dict:
             it = TransferIntent(f"{job}-g{g}-params-{i}", job, sessions[g], f"hp{g}", f"dp{g}", "h2d", T.n, rng,
                                 workload_kind="training_state", metadata={"chunk_bytes": a.chunk})
         t0 = time.perf_counter()
-        r = client.transfer(it, timeout_seconds=600)
+        r = client.transfer(it, timeout_seconds=TRANSFER_TIMEOUT_S)
         if r.state is not TransferStatusState.COMPLETE:
             raise RuntimeError(f"{it.intent_id}: {r.error}")
         return g, kind, time.perf_counter() - t0, r
@@ -165,7 +191,13 @@ def run_ours(a) -> dict:
     def step():
         t0 = time.perf_counter()
         futs = [pool.submit(one, g, k) for g in active for k in ("grads", "params")]
-        res = [f.result() for f in futs]
+        try:
+            res = [f.result() for f in futs]
+        except Exception:
+            for f in futs:
+                f.cancel()
+            pool.shutdown(wait=False, cancel_futures=True)
+            raise
         return time.perf_counter() - t0, res
 
     for _ in range(a.warmup):
@@ -263,7 +295,15 @@ def run_reference(a) -> dict:
 
 def main(argv=None) -> int:
     a = parse_args(argv)
-    res = run_reference(a) if a.impl == "reference" else run_ours(a)
+    try:
+        res = run_reference(a) if a.impl == "reference" else run_ours(a)
+    except Exception as exc:  # noqa: BLE001 - report and leave without waiting on worker threads
+        import os
+        import traceback
+
+        traceback.print_exc()
+        emit({"impl": a.impl, "error": f"{type(exc).__name__}: {exc}"}, a.json_out)
+        os._exit(1)
     if "unavailable" in res:
         emit({"impl": a.impl, "unavailable": res["unavailable"]}, a.json_out)
         return 0

@@ -81,3 +81,48 @@ def test_receipt_trace_line_format(node):
     res = model_loading.run_benchmark(args, client=TurboBusClient(daemon=dc))
     line = receipt_trace_line(model_loading.receipt_from_trace(res["samples"][0]["receipt"]))
     assert line.startswith("daemon_receipt intent_id=") and "state=complete" in line
+
+
+def test_multi_tenant_setup_and_concurrent_steps_on_mock_world():
+    """The config-5 benchmark's daemon layout (one job per GPU shard, tenant
+    weight split between its shards) with concurrent grads-D2H / params-H2D
+    intents of two tenants on the mock world: all complete, bytes exact,
+    nothing leaks."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from pcie_pool_b200 import TransferIntent
+    from pcie_pool_b200.benchmarks.multi_tenant_offload import setup_tenants, shard_job
+
+    world = MockWorld(gpu_count=4)
+    d = TurboBusDaemon(relay_gpus=[0, 1, 2, 3], max_sessions_per_relay=4, max_inflight_chunks_per_relay=1 << 16,
+                       topology_provider=StaticTopologyProvider(gpu_count=4),
+                       executor=IntentExecutor(MockDataPlane(world), max_workers=8))
+    dc = InProcessDaemonClient(d)
+    n = 2 * MiB
+    gpus, job_of = [0, 1, 2, 3], {0: 0, 1: 0, 2: 1, 3: 1}
+    rng = np.random.default_rng(5)
+    bufs = {g: (rng.integers(0, 256, n, dtype=np.uint8), np.zeros(n, np.uint8), world.alloc(g, n),
+                rng.integers(0, 256, n, dtype=np.uint8)) for g in gpus}
+    sessions = setup_tenants(d, dc, gpus, job_of, 2, n, {g: tuple(b.ctypes.data for b in bufs[g]) for g in gpus})
+    client = TurboBusClient(daemon=dc)
+    rr = ({"src_offset": 0, "dst_offset": 0, "bytes": n},)
+
+    def one(g, kind):
+        job = shard_job(job_of[g], g)
+        if kind == "grads":
+            it = TransferIntent(f"{job}-grads", job, sessions[g], f"dg{g}", f"hg{g}", "d2h", n, rr,
+                                workload_kind="training_state", metadata={"chunk_bytes": 256 << 10})
+        else:
+            it = TransferIntent(f"{job}-params", job, sessions[g], f"hp{g}", f"dp{g}", "h2d", n, rr,
+                                workload_kind="training_state", metadata={"chunk_bytes": 256 << 10})
+        return client.transfer(it, timeout_seconds=60)
+
+    with ThreadPoolExecutor(8) as pool:
+        res = list(pool.map(lambda a: one(*a), [(g, k) for g in gpus for k in ("grads", "params")]))
+    assert all(r.state.value == "complete" for r in res), [r.error for r in res]
+    for g in gpus:
+        hp, hg, dp, dg = bufs[g]
+        assert np.array_equal(dp, hp) and np.array_equal(hg, dg)
+    desc = d.describe().payload
+    assert desc["reservations"] == {} and all(q["active_chunks"] == 0 for q in desc["relay_quotas"].values())
+    assert desc["jobs"]["job0-gpu1"]["weight"] == 0.5 and desc["jobs"]["job1-gpu2"]["user_id"] == "tenant1"
