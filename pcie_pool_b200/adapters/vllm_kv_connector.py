@@ -354,7 +354,7 @@ class TurboBusConnector(KVConnectorBase_V1, SupportsHMA):
     def requires_piecewise_for_cudagraph(cls, extra_config: dict[str, Any]) -> bool:
         return True
 
-    def __init__(self, vllm_config, role, kv_cache_config=None) -> None:
+    def __init__(self, vllm_config, role: "KVConnectorRole", kv_cache_config=None) -> None:
         try:
             super().__init__(vllm_config=vllm_config, role=role, kv_cache_config=kv_cache_config)
         except TypeError:
@@ -692,6 +692,6 @@ def _scheduled(scheduler_output) -> list[Any]:
     return out
 
 
-__all__ = ["TurboBusCPUBackingPool", "TurboBusConnector", "TurboBusConnectorConfig", "TurboBusConnectorMetadata",
+__all__ = ["KVConnectorRole", "TurboBusCPUBackingPool", "TurboBusConnector", "TurboBusConnectorConfig", "TurboBusConnectorMetadata",
            "TurboBusKVConnectorState", "TurboBusPrefixStore", "TurboBusRequestMetadata", "TurboBusSavedPrefix",
            "clear_connector_events", "clear_saved_prefixes", "get_connector_events", "get_saved_prefix"]

@@ -20,7 +20,6 @@ import argparse
 import json
 import statistics
 
-import numpy as np
 
 UNITS = {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30}
 

@@ -14,8 +14,6 @@ from __future__ import annotations
 import time
 from typing import Any
 
-import numpy as np
-
 
 def build_inprocess_node(engine, devices, target: int = 0, profile: dict | None = None,
                          max_chunks: int = 1 << 16):

@@ -24,8 +24,6 @@ import statistics
 import time
 from typing import Sequence
 
-import numpy as np
-
 from .balance import LaneBalancer
 from .engine import D2H, H2D, PoolEngine
 from .planning import plan_lanes

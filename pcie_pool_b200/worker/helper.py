@@ -21,7 +21,7 @@ from typing import Any, Iterable, Mapping
 from ..schema import (BufferRegistration, DaemonResponse, ExecutionTicket, SchedulingDecision,
                       TransferStatusState, WorkerDataPlaneCompletion, WorkerDataPlaneRequest,
                       WorkerTransferAuthorization, WorkerTransferAuthorizationRequest)
-from .resources import WorkerDataPlaneResourceBinder, WorkerDataPlaneResourceError, WorkerDataPlaneResources
+from .resources import WorkerDataPlaneResourceBinder, WorkerDataPlaneResourceError
 from .staging_pool import WorkerStagingPool, WorkerStagingSlot
 
 TICKET_ISSUER = "turbobus-daemon"
