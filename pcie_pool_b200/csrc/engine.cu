@@ -11,12 +11,24 @@ namespace ppb {
 
 namespace {
 
-// Mailbox layout: four 32-bit counters, each on its own 128-byte line.
+// Mailbox layout: per direction four 32-bit counters (relay ready, relay
+// free, landing ready, landing free), each on its own 128-byte line.
+constexpr int kCounterStride = 128 / 4;
 constexpr int kRelayReady = 0;
-constexpr int kRelayFree = 32;
-constexpr int kLandReady = 64;
-constexpr int kLandFree = 96;
-constexpr size_t kMailboxBytes = 128 * 4;
+constexpr int kRelayFree = 1;
+constexpr int kLandReady = 2;
+constexpr int kLandFree = 3;
+constexpr size_t kMailboxBytes = 128 * 8;
+uint32_t* counter(uint32_t* mbox, int dir, int which) { return mbox + (dir * 4 + which) * kCounterStride; }
+
+// Of the lane-kernel CTAs that can be resident on one GPU, landing kernels
+// (H2D; fp8 quantisation wants many CTAs) get two thirds and push kernels
+// (D2H) one third, so one transfer of each direction always fits side by side
+// and no CTA of either waits for the other to leave the GPU.
+int direction_cta_budget(int max_ctas, bool h2d) {
+  const int d2h = std::max(1, max_ctas / 3);
+  return h2d ? std::max(1, max_ctas - d2h) : d2h;
+}
 constexpr uint32_t kRescueStride = 0x40000000u;
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -84,6 +96,9 @@ struct PoolEngine::Pending {
   uint64_t bytes = 0;
   double timeout_s = 0.0;
   std::chrono::steady_clock::time_point t_submit;
+  // bytes the transfer touches, for ordering against the other direction
+  uint64_t host_lo = 0, host_hi = 0, dev_lo = 0, dev_hi = 0;
+  bool dev_known = false;  // false: scattered device addresses (treated as overlapping)
 };
 
 PoolEngine::PoolEngine(const std::vector<int>& devices, const EngineOptions& options)
@@ -108,18 +123,21 @@ PoolEngine::PoolEngine(const std::vector<int>& devices, const EngineOptions& opt
     PPB_CUDA(cudaSetDevice(d));
     int lo = 0, hi = 0;
     PPB_CUDA(cudaDeviceGetStreamPriorityRange(&lo, &hi));
-    PPB_CUDA(cudaStreamCreateWithFlags(&D->main, cudaStreamNonBlocking));
-    PPB_CUDA(cudaStreamCreateWithPriority(&D->kern, cudaStreamNonBlocking, hi));
-    PPB_CUDA(cudaStreamCreateWithFlags(&D->cin, cudaStreamNonBlocking));
-    PPB_CUDA(cudaStreamCreateWithFlags(&D->cout, cudaStreamNonBlocking));
+    for (int dir = 0; dir < 2; ++dir) {
+      PPB_CUDA(cudaStreamCreateWithFlags(&D->main[dir], cudaStreamNonBlocking));
+      PPB_CUDA(cudaStreamCreateWithPriority(&D->kern[dir], cudaStreamNonBlocking, hi));
+      PPB_CUDA(cudaStreamCreateWithFlags(&D->copy[dir], cudaStreamNonBlocking));
+    }
     void* mb = nullptr;
     PPB_CUDA(cudaMalloc(&mb, kMailboxBytes));
     PPB_CUDA(cudaMemset(mb, 0, kMailboxBytes));
     D->mbox = static_cast<uint32_t*>(mb);
-    D->relay.ready = D->mbox + kRelayReady;
-    D->relay.freec = D->mbox + kRelayFree;
-    D->land.ready = D->mbox + kLandReady;
-    D->land.freec = D->mbox + kLandFree;
+    for (int dir = 0; dir < 2; ++dir) {
+      D->relay[dir].ready = counter(D->mbox, dir, kRelayReady);
+      D->relay[dir].freec = counter(D->mbox, dir, kRelayFree);
+      D->land[dir].ready = counter(D->mbox, dir, kLandReady);
+      D->land[dir].freec = counter(D->mbox, dir, kLandFree);
+    }
     // Keep freed stream-ordered allocations cached in the pool.
     cudaMemPool_t pool;
     if (cudaDeviceGetDefaultMemPool(&pool, d) == cudaSuccess) {
@@ -164,11 +182,12 @@ PoolEngine::~PoolEngine() {
   for (auto& kv : devs_) {
     Dev& D = *kv.second;
     cudaSetDevice(D.device);
-    cudaStreamSynchronize(D.main);
-    cudaStreamSynchronize(D.kern);
-    cudaStreamSynchronize(D.cin);
-    cudaStreamSynchronize(D.cout);
-    for (Ring* r : {&D.relay, &D.land}) {
+    for (int dir = 0; dir < 2; ++dir) {
+      cudaStreamSynchronize(D.main[dir]);
+      cudaStreamSynchronize(D.kern[dir]);
+      cudaStreamSynchronize(D.copy[dir]);
+    }
+    for (Ring* r : {&D.relay[0], &D.land[0], &D.relay[1], &D.land[1]}) {
       if (r->base) {
         cudaMemset(r->base, 0, options_.slot_bytes * options_.slots);
         cudaFree(r->base);
@@ -176,10 +195,11 @@ PoolEngine::~PoolEngine() {
     }
     if (D.mbox) cudaFree(D.mbox);
     for (auto e : D.free_events) cudaEventDestroy(e);
-    cudaStreamDestroy(D.main);
-    cudaStreamDestroy(D.kern);
-    cudaStreamDestroy(D.cin);
-    cudaStreamDestroy(D.cout);
+    for (int dir = 0; dir < 2; ++dir) {
+      cudaStreamDestroy(D.main[dir]);
+      cudaStreamDestroy(D.kern[dir]);
+      cudaStreamDestroy(D.copy[dir]);
+    }
   }
   for (auto& kv : pending_) {
     if (kv.second->desc_host) cudaFreeHost(kv.second->desc_host);
@@ -248,8 +268,8 @@ void PoolEngine::give_pinned(void* p) {
 uint64_t PoolEngine::relay_ring(int device) {
   std::lock_guard<std::mutex> g(mu_);
   Dev& d = dev(device);
-  ensure_ring(d, d.relay, true);
-  return reinterpret_cast<uint64_t>(d.relay.base);
+  ensure_ring(d, d.relay[0], true);
+  return reinterpret_cast<uint64_t>(d.relay[0].base);
 }
 
 uint64_t PoolEngine::mailbox(int device) {
@@ -260,7 +280,7 @@ uint64_t PoolEngine::mailbox(int device) {
 std::vector<uint64_t> PoolEngine::issued(int device) {
   std::lock_guard<std::mutex> g(mu_);
   Dev& d = dev(device);
-  return {d.relay.issued, d.land.issued};
+  return {d.relay[0].issued, d.land[0].issued, d.relay[1].issued, d.land[1].issued};
 }
 
 int PoolEngine::max_lane_ctas(int device) {
@@ -394,19 +414,26 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     R.in_place = R.direct && !R.staged && s.checksum;
     R.kernel = R.staged || R.in_place;
     if (R.staged) {
-      R.ring = R.direct ? &T.land : &R.d->relay;
+      R.ring = R.direct ? &T.land[s.direction] : &R.d->relay[s.direction];
       ensure_ring(*R.d, *R.ring, !R.direct);
     } else if (R.in_place && h2d) {
-      R.ring = &T.land;  // counters only: CE publishes, the kernel verifies in place
+      R.ring = &T.land[0];  // counters only: CE publishes, the kernel verifies in place
     }
-    R.stream = h2d ? R.d->cin : R.d->cout;
+    R.stream = R.d->copy[s.direction];
     for (const auto& c : L.chunks) R.bytes += c.bytes;
     R.chunks = L.chunks.size();
     P.bytes += R.bytes;
     P.lanes.push_back(R);
   }
 
-  // ---- ring hand-over: a ring whose direction or target changes must be idle --
+  // ---- footprint, for ordering against the other direction ---------------------
+  P.host_lo = s.host_ptr;
+  P.host_hi = s.host_ptr + s.host_bytes;
+  P.dev_known = s.op == kOpCopy;
+  P.dev_lo = s.dev_ptr;
+  P.dev_hi = s.dev_ptr + s.dev_bytes;
+
+  // ---- ring hand-over: a ring whose target changes must be idle -----------------
   for (auto& R : P.lanes) {
     if (!R.ring) continue;
     if (std::find(P.rings.begin(), P.rings.end(), R.ring) != P.rings.end()) {
@@ -419,9 +446,11 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     Ring* r = P.rings[i];
     const bool switching = r->last_dir != -1 && (r->last_dir != s.direction || r->last_target != s.target);
     if (switching || r->poisoned) {
-      // Drain every pending transfer (bounded) so no other producer/consumer
-      // still advances this ring's counters.
+      // Drain the pending transfers that use this ring (bounded) so no other
+      // producer/consumer still advances its counters.
       for (auto& kv : pending_) {
+        const auto& kr = kv.second->rings;
+        if (std::find(kr.begin(), kr.end(), r) == kr.end()) continue;
         const auto deadline = std::chrono::steady_clock::now() +
                               std::chrono::duration<double>(kv.second->timeout_s * 2 + 5);
         while (cudaEventQuery(kv.second->stop) == cudaErrorNotReady) {
@@ -448,8 +477,9 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
   int cpl = s.ctas_per_lane > 0 ? s.ctas_per_lane : options_.ctas_per_lane;
   if (kernel_lanes > 0) {
     if (T.max_ctas <= 0) throw std::runtime_error("lane kernel cannot be resident on target");
-    if (kernel_lanes > T.max_ctas) throw std::invalid_argument("more kernel lanes than resident CTAs");
-    cpl = std::max(1, std::min(cpl, T.max_ctas / kernel_lanes));
+    const int budget = direction_cta_budget(T.max_ctas, h2d);
+    if (kernel_lanes > budget) throw std::invalid_argument("more kernel lanes than resident CTAs");
+    cpl = std::max(1, std::min(cpl, budget / kernel_lanes));
   }
   uint32_t cta = 0;
   for (size_t li = 0; li < s.lanes.size(); ++li) {
@@ -526,7 +556,18 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     R.t1 = take_event(*R.d);
   }
 
-  PPB_CUDA(cudaEventRecord(P.start, T.main));
+  cudaStream_t tmain = T.main[s.direction];
+  cudaStream_t tkern = T.kern[s.direction];
+  // Order after pending transfers of the other direction on this target that
+  // touch the same host or device bytes (save-then-restore of one region).
+  for (auto& kv : pending_) {
+    const Pending& Q = *kv.second;
+    if (Q.target != s.target || Q.direction == s.direction) continue;
+    const bool host_overlap = Q.host_lo < P.host_hi && P.host_lo < Q.host_hi;
+    const bool dev_overlap = !Q.dev_known || !P.dev_known || (Q.dev_lo < P.dev_hi && P.dev_lo < Q.dev_hi);
+    if (host_overlap || dev_overlap) PPB_CUDA(cudaStreamWaitEvent(tmain, Q.stop, 0));
+  }
+  PPB_CUDA(cudaEventRecord(P.start, tmain));
   for (auto& R : P.lanes) {
     DeviceGuard lg(R.device);
     PPB_CUDA(cudaStreamWaitEvent(R.stream, P.start, 0));
@@ -551,11 +592,11 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
       qt.push_back(QuantTensor{reinterpret_cast<uint8_t*>(t.q), reinterpret_cast<float*>(t.scales), t.rows, t.cols});
     put(o_tensors, qt.data(), qt.size() * sizeof(QuantTensor));
 
-    PPB_CUDA(cudaStreamWaitEvent(T.kern, P.start, 0));
-    PPB_CUDA(cudaMallocAsync(&scratch, scratch_bytes, T.kern));
+    PPB_CUDA(cudaStreamWaitEvent(tkern, P.start, 0));
+    PPB_CUDA(cudaMallocAsync(&scratch, scratch_bytes, tkern));
     uint8_t* dsc = static_cast<uint8_t*>(scratch);
-    PPB_CUDA(cudaMemcpyAsync(dsc, h, upload_bytes, cudaMemcpyHostToDevice, T.kern));
-    PPB_CUDA(cudaMemsetAsync(dsc + o_csum, 0, scratch_bytes - o_csum, T.kern));
+    PPB_CUDA(cudaMemcpyAsync(dsc, h, upload_bytes, cudaMemcpyHostToDevice, tkern));
+    PPB_CUDA(cudaMemsetAsync(dsc + o_csum, 0, scratch_bytes - o_csum, tkern));
 
     LaneKernelParams kp{};
     kp.lanes = reinterpret_cast<const LaneDesc*>(dsc + o_lanes);
@@ -577,19 +618,19 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     kp.trace = s.trace ? reinterpret_cast<unsigned long long*>(dsc + o_trace) : nullptr;
     // Launch before any copy-engine work is queued: if the launch fails no
     // relay stream is left waiting for a kernel that never runs.
-    const cudaError_t lrc = h2d ? launch_land(kp, static_cast<int>(cta), T.kern)
-                                : launch_push(kp, static_cast<int>(cta), T.kern);
+    const cudaError_t lrc = h2d ? launch_land(kp, static_cast<int>(cta), tkern)
+                                : launch_push(kp, static_cast<int>(cta), tkern);
     if (lrc != cudaSuccess) {
-      cudaFreeAsync(scratch, T.kern);
+      cudaFreeAsync(scratch, tkern);
       for (auto& R : P.lanes)
         if (R.ring) R.ring->issued = R.seq0;
       give_pinned(P.desc_host);
       give_pinned(P.result_host);
       check_cuda(lrc, "lane kernel launch");
     }
-    PPB_CUDA(cudaMemcpyAsync(P.result_host, dsc + o_csum, result_bytes, cudaMemcpyDeviceToHost, T.kern));
-    PPB_CUDA(cudaFreeAsync(scratch, T.kern));
-    PPB_CUDA(cudaEventRecord(P.kern_done, T.kern));
+    PPB_CUDA(cudaMemcpyAsync(P.result_host, dsc + o_csum, result_bytes, cudaMemcpyDeviceToHost, tkern));
+    PPB_CUDA(cudaFreeAsync(scratch, tkern));
+    PPB_CUDA(cudaEventRecord(P.kern_done, tkern));
   }
 
   // ---- copy-engine side, chunks interleaved round-robin across lanes ------------
@@ -665,9 +706,9 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     PPB_CUDA(cudaEventRecord(R.t1, R.stream));
   }
   PPB_CUDA(cudaSetDevice(s.target));
-  for (auto& R : P.lanes) PPB_CUDA(cudaStreamWaitEvent(T.main, R.t1, 0));
-  if (P.has_kernel) PPB_CUDA(cudaStreamWaitEvent(T.main, P.kern_done, 0));
-  PPB_CUDA(cudaEventRecord(P.stop, T.main));
+  for (auto& R : P.lanes) PPB_CUDA(cudaStreamWaitEvent(tmain, R.t1, 0));
+  if (P.has_kernel) PPB_CUDA(cudaStreamWaitEvent(tmain, P.kern_done, 0));
+  PPB_CUDA(cudaEventRecord(P.stop, tmain));
 
   for (size_t i = 0; i < P.rings.size(); ++i) {
     P.rings[i]->last_dir = s.direction;

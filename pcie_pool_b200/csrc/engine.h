@@ -1,15 +1,19 @@
 // PoolEngine: the persistent data plane of pcie_pool_b200.
 //
 // One engine lives in the data-plane process and holds contexts on every GPU
-// it may use.  Per device it owns
-//   * four streams (main/join, lane-kernel, copy-in, copy-out),
+// it may use.  Per device and per direction (H2D, D2H) it owns
+//   * a main/join stream, a lane-kernel stream and a copy-engine stream, so
+//     one GPU's H2D and D2H transfers run at the same time on the full-duplex
+//     PCIe link (same-direction transfers on one target run in submit order),
 //   * a relay staging ring (`slots` x `slot_bytes`) used while the device
 //     lends its PCIe link to another GPU, plus a landing ring used for staged
 //     ops on its own direct lane,
-//   * a mailbox of 32-bit lane counters (ready / free for each ring),
+//   * 32-bit lane counters (ready / free for each ring) in one mailbox,
 // all allocated once and reused by every transfer (the reference re-creates
 // its runtime, staging slots and peer mappings per transfer:
-// turbobus/worker/cuda_executor.py:67-75).
+// turbobus/worker/cuda_executor.py:67-75).  A transfer that overlaps (host or
+// device bytes) a pending transfer of the other direction on the same target
+// is ordered after it.
 //
 // A transfer is a set of lanes (the target's direct PCIe lane plus relay
 // lanes), each with an ordered chunk list.  For H2D each relay lane runs
@@ -131,7 +135,8 @@ class PoolEngine {
   // Raw pointers for tests / probes.
   uint64_t relay_ring(int device);
   uint64_t mailbox(int device);
-  // Counter values as the host believes them (relay ring, landing ring).
+  // Counter values as the host believes them: H2D relay ring, H2D landing
+  // ring, D2H relay ring, D2H landing ring.
   std::vector<uint64_t> issued(int device);
   int max_lane_ctas(int device);
 
@@ -148,9 +153,13 @@ class PoolEngine {
   };
   struct Dev {
     int device = -1;
-    cudaStream_t main = nullptr, kern = nullptr, cin = nullptr, cout = nullptr;
-    uint32_t* mbox = nullptr;  // 4 counters, each on its own 128-byte line
-    Ring relay, land;
+    // indexed by direction (0 = H2D, 1 = D2H); copy[0] carries host->device
+    // copies, copy[1] device->host copies, whichever GPU is the target
+    cudaStream_t main[2] = {nullptr, nullptr};
+    cudaStream_t kern[2] = {nullptr, nullptr};
+    cudaStream_t copy[2] = {nullptr, nullptr};
+    uint32_t* mbox = nullptr;  // 8 counters, each on its own 128-byte line
+    Ring relay[2], land[2];
     std::vector<cudaEvent_t> free_events;
     int max_ctas = 0;
   };

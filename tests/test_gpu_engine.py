@@ -360,3 +360,58 @@ def test_device_trace_stamps_are_ordered(need_gpu):
     ev = device_trace_events(r, lanes)
     assert len(ev) == 12 and {e["name"] for e in ev} == {"transfer:wait", "transfer:move"}
     host.release()
+
+
+def test_h2d_and_d2h_on_one_target_run_concurrently(need_gpu):
+    """A GPU's H2D and D2H transfers overlap on the full-duplex link: both in
+    flight together take clearly less than one after the other."""
+    import time
+
+    from pcie_pool_b200.parallel.engine import D2H, H2D, split_even
+
+    n = 1 << 30
+    up = _host(n, seed=11)
+    down = _host(n, seed=12)
+    dst = torch.empty(n, dtype=torch.uint8, device="cuda:0")
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda:0")
+    eng = _engine([0], slot_bytes=16 << 20)
+    lanes = split_even(n, 16 << 20, [0])
+
+    def both(serial: bool) -> float:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        a = eng.submit(H2D, 0, up.ptr, n, dst.data_ptr(), n, lanes)
+        if serial:
+            assert eng.wait(a).ok
+        b = eng.submit(D2H, 0, down.ptr, n, src.data_ptr(), n, lanes)
+        rb = eng.wait(b)
+        if not serial:
+            assert eng.wait(a).ok
+        assert rb.ok, rb.error
+        return time.perf_counter() - t0
+
+    both(True)
+    serial = min(both(True) for _ in range(2))
+    duplex = min(both(False) for _ in range(2))
+    assert torch.equal(dst[:1 << 20].cpu(), torch.from_numpy(up.numpy()[:1 << 20].copy()))
+    assert np.array_equal(down.numpy()[-(1 << 20):], src[-(1 << 20):].cpu().numpy())
+    assert duplex < 0.8 * serial, (duplex, serial)
+
+
+def test_overlapping_opposite_transfers_stay_ordered(need_gpu):
+    """D2H of a device region into host memory followed at once by H2D of that
+    host memory into another region: the H2D sees the D2H's bytes."""
+    from pcie_pool_b200.parallel.engine import D2H, H2D, split_even
+
+    n = 64 << 20
+    host = _host(n, seed=13)
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda:0")
+    dst = torch.zeros(n, dtype=torch.uint8, device="cuda:0")
+    eng = _engine([0], slot_bytes=4 << 20)
+    lanes = split_even(n, 4 << 20, [0])
+    for _ in range(3):
+        src.random_(0, 256)
+        a = eng.submit(D2H, 0, host.ptr, n, src.data_ptr(), n, lanes)
+        b = eng.submit(H2D, 0, host.ptr, n, dst.data_ptr(), n, lanes, checksum=True)
+        assert eng.wait(b).ok and eng.wait(a).ok
+        assert torch.equal(dst, src)
