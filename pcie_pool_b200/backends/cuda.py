@@ -81,6 +81,13 @@ class CudaNativeBackend:
             raise ValueError("device_ptr must be positive")
         return ipc_handle_bytes(bytes(self._native().export_ipc_handle(int(device_ptr))))
 
+    def device_allocation_offset(self, device_ptr: int) -> int:
+        """Offset of ``device_ptr`` inside its CUDA allocation (an IPC handle
+        names the allocation; the receiver adds this offset to the mapping)."""
+        if int(device_ptr) <= 0:
+            raise ValueError("device_ptr must be positive")
+        return int(device_ptr) - int(self._native().allocation_base(int(device_ptr)))
+
     def open_device_ipc_handle(self, cuda_ipc_handle: bytes | bytearray | str, device_index: int = 0) -> int:
         ptr = int(self._native().open_ipc_handle(coerce_ipc_handle(cuda_ipc_handle), int(device_index)))
         if ptr <= 0:

@@ -237,6 +237,7 @@ class CudaIpcDeviceBuffer:
     size_bytes: int
     cuda_ipc_handle: bytes
     device_ptr: int | None = None
+    ipc_offset: int = 0  # device_ptr - base of its allocation (the handle maps the base)
 
     @classmethod
     def from_device_pointer(cls, buffer_id: str, job_id: str, device_index: int, size_bytes: int,
@@ -249,9 +250,10 @@ class CudaIpcDeviceBuffer:
         setter = getattr(backend, "set_device", None)
         if callable(setter):
             setter(int(device_index))
+        off = getattr(backend, "device_allocation_offset", None)
         return cls(buffer_id=str(buffer_id), job_id=str(job_id), device_index=int(device_index),
                    size_bytes=int(size_bytes), cuda_ipc_handle=backend.export_device_ipc_handle(int(device_ptr)),
-                   device_ptr=int(device_ptr))
+                   device_ptr=int(device_ptr), ipc_offset=int(off(int(device_ptr))) if callable(off) else 0)
 
     @classmethod
     def from_tensor(cls, buffer_id: str, job_id: str, tensor, *, backend=None) -> "CudaIpcDeviceBuffer":
@@ -260,7 +262,10 @@ class CudaIpcDeviceBuffer:
 
     @property
     def metadata(self) -> dict[str, object]:
-        return {"cuda_ipc_handle": self.cuda_ipc_handle.hex()}
+        md: dict[str, object] = {"cuda_ipc_handle": self.cuda_ipc_handle.hex()}
+        if self.ipc_offset:
+            md["cuda_ipc_offset"] = int(self.ipc_offset)
+        return md
 
     def buffer_registration(self) -> BufferRegistration:
         return BufferRegistration(buffer_id=self.buffer_id, job_id=self.job_id, kind="gpu",

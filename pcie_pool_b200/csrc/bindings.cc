@@ -76,6 +76,27 @@ PYBIND11_MODULE(_C, m) {
     PPB_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(dptr)));
     return py::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
   });
+  // Base of the device allocation holding `dptr`: an IPC handle names a whole
+  // allocation, so a pointer inside a caching-allocator segment travels as
+  // handle + (dptr - base) and the receiver adds the offset back.
+  m.def("allocation_base", [](uint64_t dptr) {
+    using Fn = int (*)(unsigned long long*, size_t*, unsigned long long);
+    static Fn fn = [] {
+      void* f = nullptr;
+      cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+      if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &f, 12000, cudaEnableDefault, &q) !=
+              cudaSuccess ||
+          q != cudaDriverEntryPointSuccess)
+        f = nullptr;
+      return reinterpret_cast<Fn>(f);
+    }();
+    if (fn == nullptr) throw std::runtime_error("CUDA driver does not provide cuMemGetAddressRange");
+    unsigned long long base = 0;
+    size_t size = 0;
+    const int rc = fn(&base, &size, static_cast<unsigned long long>(dptr));
+    if (rc != 0) throw std::runtime_error("cuMemGetAddressRange failed with CUresult " + std::to_string(rc));
+    return static_cast<uint64_t>(base);
+  });
   m.def("open_ipc_handle", [](py::bytes raw, int device) {
     std::string s = raw;
     if (s.size() != sizeof(cudaIpcMemHandle_t)) throw std::invalid_argument("IPC handle must be 64 bytes");

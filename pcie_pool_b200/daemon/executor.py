@@ -147,7 +147,8 @@ class EngineDataPlane:
                     from .._native import native
 
                     self._ipc[h] = native().open_ipc_handle(bytes.fromhex(h), int(buf.device_index or 0))
-                return self._ipc[h]
+                # the handle maps its allocation's base; the buffer may start inside it
+                return self._ipc[h] + int(buf.metadata.get("cuda_ipc_offset", 0) or 0)
         if buf.address is None:
             raise ValueError(f"buffer {buf.buffer_id} has no device address")
         return int(buf.address)

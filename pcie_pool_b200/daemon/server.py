@@ -105,6 +105,7 @@ class DaemonState:
     profiles: dict[str, dict[str, Any]] = field(default_factory=dict)
     measured: dict[str, dict[str, Any]] = field(default_factory=dict)
     completed_at: dict[str, float] = field(default_factory=dict)
+    target_seen: dict[int, float] = field(default_factory=dict)  # device -> last time it was a target
 
 
 class TurboBusDaemon:
@@ -116,7 +117,7 @@ class TurboBusDaemon:
                  topology_provider: TopologyProvider | None = None, *,
                  scheduler: DaemonScheduler | None = None, executor=None,
                  profile_store_path: str | None = None,
-                 clock: Callable[[], float] = time.time) -> None:
+                 clock: Callable[[], float] = time.time, link_hold_seconds: float = 1.0) -> None:
         self._lock = threading.RLock()
         self._changed = threading.Condition(self._lock)
         self._st = DaemonState()
@@ -124,6 +125,11 @@ class TurboBusDaemon:
         self._topology = topology_provider
         self._session_timeout = max(0.0, float(session_timeout_seconds))
         self._profile_max_age = max(0.0, float(profile_max_age_seconds))
+        # A GPU that was the target of a transfer within this window is not
+        # lent as a relay: in multi-tenant training every GPU moves its own
+        # shard each step, and relaying through it only queues another job's
+        # chunks in front of that GPU's own on its link.  0 disables.
+        self._link_hold = max(0.0, float(link_hold_seconds))
         self._clock = clock
         self._quotas = {g: RelayQuota(relay_gpu=g, max_sessions=int(max_sessions_per_relay),
                                       max_inflight_chunks=int(max_inflight_chunks_per_relay))
@@ -1602,7 +1608,10 @@ class TurboBusDaemon:
             "workload_kind": None, "priority": 0, "queued_at": float(now), "planned_at": decision.issued_at,
             "admission_state": adm.get("state", ADMITTED), "admission_reason": adm.get("reason"),
             "plan_generation": S.generations.get(tid, 0), "plan_expires_at": S.plan_expiry.get(tid),
-            "started_at": None, "completed_at": None, "fallback_reason": decision.fallback_reason}
+            "started_at": None, "completed_at": None, "fallback_reason": decision.fallback_reason,
+            "target_devices": plan_targets(decision.plan)}
+        for g in S.queue_records[tid]["target_devices"]:
+            S.target_seen[g] = float(now)
         self._refresh_record(tid, now)
         S.version += 1
 
@@ -1637,6 +1646,8 @@ class TurboBusDaemon:
             rec["started_at"] = at
         if st.state in TERMINAL_STATES and rec.get("completed_at") is None:
             rec["completed_at"] = at
+            for g in rec.get("target_devices", ()) or ():
+                S.target_seen[int(g)] = max(at, S.target_seen.get(int(g), at))
         it = S.intents.get(str(rec.get("intent_id"))) if rec.get("intent_id") is not None else None
         if it is not None:
             rec.update(intent_id=it.intent_id, source_buffer_id=it.source_buffer_id,
@@ -1692,8 +1703,10 @@ class TurboBusDaemon:
                  "relay_staging": {"count": len(staging), "active_reservation_count": len(reservations),
                                    "active_lease_count": len(leases)}}
         terminal = {s.value for s in TERMINAL_STATES}
+        recent = sorted(g for g, t in S.target_seen.items() if self._link_hold > 0 and at - t <= self._link_hold)
         return {
             "version": S.version, "captured_at": at, "transfer_order": tuple(S.queue), "transfers": recs,
+            "recent_targets": recent, "link_hold_seconds": self._link_hold,
             "queued_transfers": queued, "running_transfers": running, "active_transfers": active,
             "active_paths": paths, "active_resource_usage": usage, "job_runtime_state": jobs,
             "active_reservations": reservations, "active_leases": leases, "relay_staging": staging,
@@ -1927,10 +1940,21 @@ def direct_only(decision: SchedulingDecision) -> bool:
                              and str(a["path"].get("kind", "")).lower() == "direct" for a in asg)
 
 
-def busy_relays(state: Mapping[str, Any]) -> set[int]:
-    """GPUs whose PCIe link is in use: relays of active relay paths and the
-    targets of active direct paths."""
+def plan_targets(plan: Mapping[str, Any]) -> tuple[int, ...]:
+    """Target devices named by a plan's paths."""
     out: set[int] = set()
+    for a in plan.get("assignments", ()) or ():
+        p = a.get("path") if isinstance(a, Mapping) else None
+        if isinstance(p, Mapping) and p.get("target_device") is not None:
+            out.add(int(p["target_device"]))
+    return tuple(sorted(out))
+
+
+def busy_relays(state: Mapping[str, Any]) -> set[int]:
+    """GPUs whose PCIe link is in use: relays of active relay paths, the
+    targets of active direct paths and GPUs that were a transfer's target
+    within the daemon's link-hold window."""
+    out: set[int] = {int(g) for g in state.get("recent_targets", ()) or ()}
     for p in state.get("active_paths", ()) or ():
         if not isinstance(p, Mapping):
             continue

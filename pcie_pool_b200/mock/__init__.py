@@ -167,22 +167,34 @@ def chunk_lane_map(trace: list[dict[str, Any]]) -> dict[int, int]:
 class MockCudaBackend:
     """Stand-in for the CUDA backend in worker tests: IPC handles are 64
     random bytes mapped to in-process addresses; host registration is
-    recorded, not performed."""
+    recorded, not performed.  Like CUDA, a handle names a whole allocation:
+    ``allocations`` (base -> bytes) declares them, and a pointer inside one
+    exports the allocation's handle (mapped at its base)."""
 
     def __init__(self) -> None:
         self.handles: dict[bytes, int] = {}
         self.open: dict[int, bytes] = {}
         self.registered: dict[int, int] = {}
+        self.allocations: dict[int, int] = {}
         self.device = 0
 
     def set_device(self, device_index: int) -> None:
         self.device = int(device_index)
 
+    def _base(self, device_ptr: int) -> int:
+        for base, size in self.allocations.items():
+            if base <= int(device_ptr) < base + size:
+                return base
+        return int(device_ptr)
+
+    def device_allocation_offset(self, device_ptr: int) -> int:
+        return int(device_ptr) - self._base(device_ptr)
+
     def export_device_ipc_handle(self, device_ptr: int) -> bytes:
         import os
 
         h = os.urandom(64)
-        self.handles[h] = int(device_ptr)
+        self.handles[h] = self._base(device_ptr)
         return h
 
     def open_device_ipc_handle(self, handle, device_index: int = 0) -> int:

@@ -84,6 +84,9 @@ def load_view(runtime_state: Mapping[str, object] | None, *, job_id: str | None,
     jobs: Mapping[str, object] = {}
     active = queued = 0
     if isinstance(runtime_state, Mapping):
+        # GPUs that were a transfer's target within the daemon's link-hold
+        # window keep their link for their own traffic.
+        busy.update(int(g) for g in runtime_state.get("recent_targets", ()) or ())
         for rec in runtime_state.get("active_paths", ()) or ():
             if not isinstance(rec, Mapping):
                 continue

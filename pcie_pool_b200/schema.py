@@ -258,6 +258,10 @@ def buffer_handle_metadata(*, kind: str, pinned: bool, device_index: int | None,
         if "cuda_ipc_handle" not in md:
             raise ValueError("cuda_ipc_device metadata requires cuda_ipc_handle")
         md["cuda_ipc_handle"] = cuda_ipc_handle(md["cuda_ipc_handle"])
+        if "cuda_ipc_offset" in md:
+            off = md["cuda_ipc_offset"]
+            if isinstance(off, bool) or not isinstance(off, int) or off < 0:
+                raise ValueError("cuda_ipc_offset must be a non-negative integer")
     return md
 
 

@@ -223,11 +223,16 @@ def verify(direction: str = "h2d", *, target_gpu: int = 0, relay_gpu: int = 1, b
                 want = np.zeros(dst_size, dtype=np.uint8)
                 want[dst_offset:dst_offset + n] = pattern
             secs = time.perf_counter() - t0
+            if res.state != "complete" or res.bytes_completed != n:
+                raise RuntimeError(f"daemon status {res.state} with {res.bytes_completed} of {n} bytes: "
+                                   f"{getattr(res, 'final_status', '')}")
             if not np.array_equal(got, want):
                 bad = int(np.flatnonzero(got != want)[0])
-                raise RuntimeError(f"verification bytes differ first at offset {bad}")
-            if res.state != "complete" or res.bytes_completed != n:
-                raise RuntimeError(f"daemon status {res.state} with {res.bytes_completed} of {n} bytes")
+                raise RuntimeError(f"verification bytes differ first at offset {bad} "
+                                   f"({int((got != want).sum())} bytes differ, {int((got == 0).sum())} zero; "
+                                   f"got {got[bad:bad + 8].tolist()} want {want[bad:bad + 8].tolist()}; "
+                                   f"status {res.state}, path {getattr(res, 'path', None)}, "
+                                   f"measured {getattr(res, 'measured', None)})")
             d_b, d_c = _plan_split(res.plan["plan"], "direct")
             r_b, r_c = _plan_split(res.plan["plan"], "relay")
             wres = ((res.worker_completion or {}).get("worker_result") or {}).get("metadata") or {}

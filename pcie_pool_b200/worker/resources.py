@@ -85,7 +85,9 @@ class WorkerDataPlaneResourceBinding:
                 be.set_device(int(dev_h.device_index))
             self._dev_ptr = int(be.open_device_ipc_handle(str(dev_h.metadata["cuda_ipc_handle"]),
                                                           int(dev_h.device_index or 0)))
-            self._resources = WorkerDataPlaneResources(req, self._cpu, self._dev_ptr, dev_h.size_bytes,
+            # the handle maps its allocation's base; the buffer may start inside it
+            dev_ptr = self._dev_ptr + int(dev_h.metadata.get("cuda_ipc_offset", 0) or 0)
+            self._resources = WorkerDataPlaneResources(req, self._cpu, dev_ptr, dev_h.size_bytes,
                                                        int(dev_h.device_index or 0), self.register_cuda_host)
             return self._resources
         except WorkerDataPlaneResourceError:

@@ -374,6 +374,7 @@ def test_h2d_and_d2h_on_one_target_run_concurrently(need_gpu):
     down = _host(n, seed=12)
     dst = torch.empty(n, dtype=torch.uint8, device="cuda:0")
     src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda:0")
+    torch.cuda.synchronize()
     eng = _engine([0], slot_bytes=16 << 20)
     lanes = split_even(n, 16 << 20, [0])
 
@@ -411,6 +412,7 @@ def test_overlapping_opposite_transfers_stay_ordered(need_gpu):
     lanes = split_even(n, 4 << 20, [0])
     for _ in range(3):
         src.random_(0, 256)
+        torch.cuda.synchronize()  # the engine's streams do not wait for torch's stream
         a = eng.submit(D2H, 0, host.ptr, n, src.data_ptr(), n, lanes)
         b = eng.submit(H2D, 0, host.ptr, n, dst.data_ptr(), n, lanes, checksum=True)
         assert eng.wait(b).ok and eng.wait(a).ok

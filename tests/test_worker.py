@@ -317,3 +317,23 @@ def test_engine_data_plane_lane_failover_logic():
     assert "lane failover" in res.measured["fallback_reason"]
     # the re-run's checksums replaced the failed lane's entries (chunks 4..7)
     assert res.measured["chunk_checksums"][4:] == [[1, 1]] * 4 and res.measured["chunk_checksums"][0] == [0, 0]
+
+
+def test_ipc_buffer_inside_an_allocation_lands_at_its_offset(node):
+    """A device buffer that starts inside a larger allocation (a caching
+    allocator's segment) travels as the allocation's handle plus an offset;
+    the worker writes at the buffer, not at the allocation base."""
+    n, off = 8 * MiB, 3 * MiB + 4096
+    host = SharedPinnedCpuBuffer.allocate("host", "job", n)
+    host.numpy()[:] = np.random.default_rng(5).integers(0, 256, n, dtype=np.uint8)
+    seg = node.world.alloc(0, off + n)
+    node.backend.allocations[seg.ctypes.data] = seg.nbytes
+    dev = CudaIpcDeviceBuffer.from_device_pointer("dev", "job", 0, n, seg.ctypes.data + off, backend=node.backend)
+    assert dev.ipc_offset == off and dev.metadata["cuda_ipc_offset"] == off
+    try:
+        r = node.client().fetch_shared_cpu_to_cuda_ipc(host, dev, chunk_bytes=2 * MiB, mode="pool")
+        assert r.state == "complete"
+        assert not seg[:off].any(), "nothing written below the buffer"
+        assert np.array_equal(seg[off:], host.numpy())
+    finally:
+        host.release()
