@@ -41,6 +41,8 @@ def parse_args(argv=None):
     p.add_argument("--chunk", type=int, default=16 << 20)
     p.add_argument("--slots", type=int, default=3)
     p.add_argument("--ctas", type=int, default=4, help="lane-kernel CTAs per lane")
+    p.add_argument("--coalesce", type=int, default=64 << 20,
+                   help="largest merged copy-engine transfer on the direct lane (bytes)")
     p.add_argument("--direction", choices=["h2d", "d2h"], default="h2d")
     p.add_argument("--no-checksum", action="store_true", help="skip the fused per-chunk checksum")
     p.add_argument("--no-e2e", action="store_true")
@@ -116,7 +118,7 @@ def run_ours(args, dist: Dist) -> dict:
         if args.direction == "d2h":
             dev.copy_(torch.from_numpy(host.numpy()).to("cuda:0"))
         eng = PoolEngine(devices, slot_bytes=max(args.chunk, 1 << 20), slots=args.slots,
-                         ctas_per_lane=args.ctas, timeout_s=20.0)
+                         ctas_per_lane=args.ctas, timeout_s=20.0, coalesce_bytes=args.coalesce)
         direction = H2D if args.direction == "h2d" else D2H
         dname = args.direction
         checksum = not args.no_checksum
@@ -310,7 +312,7 @@ def main(argv=None) -> int:
                     "model": "pooled-transfer sweep point (BASELINE config 2)",
                     "direction": args.direction,
                     "transfer_bytes": args.bytes,
-                    "chunk_bytes": args.chunk,
+                    "chunk_bytes": args.chunk, "coalesce_bytes": args.coalesce,
                     "target_gpu": 0,
                     "relay_gpus": list(range(1, N)),
                     "parallelism": f"direct+{N - 1}relay",

@@ -1951,10 +1951,10 @@ def plan_targets(plan: Mapping[str, Any]) -> tuple[int, ...]:
 
 
 def busy_relays(state: Mapping[str, Any]) -> set[int]:
-    """GPUs whose PCIe link is in use: relays of active relay paths, the
-    targets of active direct paths and GPUs that were a transfer's target
-    within the daemon's link-hold window."""
-    out: set[int] = {int(g) for g in state.get("recent_targets", ()) or ()}
+    """GPUs whose PCIe link is in use: relays of active relay paths and the
+    targets of active direct paths.  (GPUs inside the link-hold window are
+    only kept out of new plans; admission never waits on them.)"""
+    out: set[int] = set()
     for p in state.get("active_paths", ()) or ():
         if not isinstance(p, Mapping):
             continue

@@ -144,6 +144,8 @@ class DaemonScheduler:
             dev = int(r["relay_device"])
             if dev not in allowed:
                 continue
+            if dev in view.held_relays:
+                continue
             if not defer and (not _has_capacity(session, quotas.get(dev)) or dev in view.busy_relays):
                 continue
             relays.append(RelayProfileView(

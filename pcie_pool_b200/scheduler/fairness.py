@@ -53,6 +53,10 @@ class LoadView:
     fairness_threshold_bytes: float
     active_transfer_count: int
     queued_transfer_count: int
+    # GPUs that were a transfer's target within the daemon's link-hold window:
+    # never planned as relays (a planning preference, unlike busy_relays,
+    # which delayed admission waits out)
+    held_relays: frozenset[int] = frozenset()
 
     def policy_metadata(self) -> dict[str, object]:
         return {
@@ -66,6 +70,7 @@ class LoadView:
             "average_weighted_active_bytes": self.average_weighted_active_bytes,
             "fairness_threshold_bytes": self.fairness_threshold_bytes,
             "busy_relays": tuple(sorted(self.busy_relays)),
+            "held_relays": tuple(sorted(self.held_relays)),
             "active_transfer_count": self.active_transfer_count,
             "queued_transfer_count": self.queued_transfer_count,
         }
@@ -83,10 +88,11 @@ def load_view(runtime_state: Mapping[str, object] | None, *, job_id: str | None,
     busy: set[int] = set()
     jobs: Mapping[str, object] = {}
     active = queued = 0
+    held: frozenset[int] = frozenset()
     if isinstance(runtime_state, Mapping):
         # GPUs that were a transfer's target within the daemon's link-hold
         # window keep their link for their own traffic.
-        busy.update(int(g) for g in runtime_state.get("recent_targets", ()) or ())
+        held = frozenset(int(g) for g in runtime_state.get("recent_targets", ()) or ())
         for rec in runtime_state.get("active_paths", ()) or ():
             if not isinstance(rec, Mapping):
                 continue
@@ -127,6 +133,7 @@ def load_view(runtime_state: Mapping[str, object] | None, *, job_id: str | None,
     avg = (total_active + charge) / max(total_w, 1e-12)
     return LoadView(
         job_id=job, workload_kind=workload, priority=int(priority), busy_relays=frozenset(busy),
+        held_relays=held,
         job_weight=my_w, total_weight=total_w, current_job_active_bytes=mine,
         total_active_bytes=total_active, request_charge_bytes=charge,
         average_weighted_active_bytes=avg,

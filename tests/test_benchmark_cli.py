@@ -107,22 +107,81 @@ def test_multi_tenant_setup_and_concurrent_steps_on_mock_world():
     client = TurboBusClient(daemon=dc)
     rr = ({"src_offset": 0, "dst_offset": 0, "bytes": n},)
 
-    def one(g, kind):
+    def one(g, kind, step=0):
         job = shard_job(job_of[g], g)
         if kind == "grads":
-            it = TransferIntent(f"{job}-grads", job, sessions[g], f"dg{g}", f"hg{g}", "d2h", n, rr,
+            it = TransferIntent(f"{job}-grads-{step}", job, sessions[g], f"dg{g}", f"hg{g}", "d2h", n, rr,
                                 workload_kind="training_state", metadata={"chunk_bytes": 256 << 10})
         else:
-            it = TransferIntent(f"{job}-params", job, sessions[g], f"hp{g}", f"dp{g}", "h2d", n, rr,
+            it = TransferIntent(f"{job}-params-{step}", job, sessions[g], f"hp{g}", f"dp{g}", "h2d", n, rr,
                                 workload_kind="training_state", metadata={"chunk_bytes": 256 << 10})
         return client.transfer(it, timeout_seconds=60)
 
+    relay_bytes = []
     with ThreadPoolExecutor(8) as pool:
-        res = list(pool.map(lambda a: one(*a), [(g, k) for g in gpus for k in ("grads", "params")]))
-    assert all(r.state.value == "complete" for r in res), [r.error for r in res]
+        for step in range(3):  # every GPU is a target each step: after the first, none is lent
+            res = list(pool.map(lambda a: one(*a), [(g, k, step) for g in gpus for k in ("grads", "params")]))
+            assert all(r.state.value == "complete" for r in res), [r.error for r in res]
+            relay_bytes.append(sum(int(p.get("bytes", 0)) for r in res for p in r.path_stats
+                                   if p.get("kind") == "relay"))
+    assert relay_bytes[1:] == [0, 0], relay_bytes
     for g in gpus:
         hp, hg, dp, dg = bufs[g]
         assert np.array_equal(dp, hp) and np.array_equal(hg, dg)
     desc = d.describe().payload
     assert desc["reservations"] == {} and all(q["active_chunks"] == 0 for q in desc["relay_quotas"].values())
     assert desc["jobs"]["job0-gpu1"]["weight"] == 0.5 and desc["jobs"]["job1-gpu2"]["user_id"] == "tenant1"
+
+
+def test_multi_tenant_slow_transfers_never_wait_on_the_link_hold():
+    """Two single-GPU tenants whose transfers overlap in time (each takes
+    tens of ms): every intent completes well inside its timeout in every
+    step (a relay kept out by the link-hold window is left out of the plan,
+    never parked in delayed admission), and once both GPUs are targets
+    neither is lent to the other."""
+    import time
+    from concurrent.futures import ThreadPoolExecutor
+
+    from pcie_pool_b200 import TransferIntent
+    from pcie_pool_b200.benchmarks.multi_tenant_offload import setup_tenants, shard_job
+
+    class SlowPlane(MockDataPlane):
+        def execute(self, *a, **k):
+            time.sleep(0.04)
+            return super().execute(*a, **k)
+
+    world = MockWorld(gpu_count=2)
+    d = TurboBusDaemon(relay_gpus=[0, 1], max_sessions_per_relay=2, max_inflight_chunks_per_relay=1 << 16,
+                       topology_provider=StaticTopologyProvider(gpu_count=2),
+                       executor=IntentExecutor(SlowPlane(world), max_workers=8))
+    dc = InProcessDaemonClient(d)
+    n = 4 * MiB
+    gpus, job_of = [0, 1], {0: 0, 1: 1}
+    rng = np.random.default_rng(9)
+    bufs = {g: (rng.integers(0, 256, n, dtype=np.uint8), np.zeros(n, np.uint8), world.alloc(g, n),
+                rng.integers(0, 256, n, dtype=np.uint8)) for g in gpus}
+    sessions = setup_tenants(d, dc, gpus, job_of, 1, n, {g: tuple(b.ctypes.data for b in bufs[g]) for g in gpus})
+    client = TurboBusClient(daemon=dc)
+    rr = ({"src_offset": 0, "dst_offset": 0, "bytes": n},)
+
+    def one(g, kind, step):
+        job = shard_job(job_of[g], g)
+        src, dst, direction = (f"dg{g}", f"hg{g}", "d2h") if kind == "grads" else (f"hp{g}", f"dp{g}", "h2d")
+        it = TransferIntent(f"{job}-{kind}-{step}", job, sessions[g], src, dst, direction, n, rr,
+                            workload_kind="training_state", metadata={"chunk_bytes": 512 << 10})
+        t0 = time.perf_counter()
+        r = client.transfer(it, timeout_seconds=10)
+        return r, time.perf_counter() - t0
+
+    relay_bytes = []
+    with ThreadPoolExecutor(4) as pool:
+        for step in range(4):
+            out = list(pool.map(lambda a: one(*a), [(g, k, step) for g in gpus for k in ("grads", "params")]))
+            assert all(r.state.value == "complete" for r, _ in out), [r.error for r, _ in out]
+            assert max(t for _, t in out) < 5.0
+            relay_bytes.append(sum(int(p.get("bytes", 0)) for r, _ in out for p in r.path_stats
+                                   if p.get("kind") == "relay"))
+    assert relay_bytes[1:] == [0, 0, 0], relay_bytes
+    for g in gpus:
+        hp, hg, dp, dg = bufs[g]
+        assert np.array_equal(dp, hp) and np.array_equal(hg, dg)
