@@ -170,6 +170,10 @@ class TurboBusCPUBackingPool:
     def release(self, block_count: int, kv_caches: list[Any], backing) -> None:
         self._free.setdefault(_signature(block_count, kv_caches), []).append(backing)
 
+    def release_prefix(self, prefix: "TurboBusSavedPrefix", kv_caches: list[Any]) -> None:
+        """Return a saved prefix's CPU backings to the pool."""
+        self.release(prefix.block_count, kv_caches, prefix.cpu_backings)
+
     @staticmethod
     def _allocate(block_count: int, kv_caches: list[Any]):
         import torch

@@ -25,6 +25,12 @@ class CudaNativeBackend:
 
         return native()
 
+    def bind_runtime(self, native_module: Any, torch_module: Any = None) -> None:
+        """Use ``native_module`` as the native core (tests inject a stand-in;
+        turbobus/backends/cuda.py:15-17).  ``torch_module`` is accepted for the
+        same signature; this backend imports torch itself where it needs it."""
+        self._loader = (lambda: native_module) if native_module is not None else None
+
     def require_available(self) -> None:
         self._native()
 

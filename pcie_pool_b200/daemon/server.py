@@ -40,6 +40,7 @@ from ..schema import (BufferRegistration, CleanupRequest, DaemonRequest, DaemonR
                       WorkerTransferAuthorization, WorkerTransferAuthorizationRequest)
 from ..topology import TopologyProvider
 from .audit import build_audit_record
+from .wire import reserve_socket
 
 ADMITTED = "admitted"
 DELAYED = "delayed"
@@ -2078,4 +2079,4 @@ def socket_path_for_user(base_dir: str = "/tmp") -> str:
 
 PoolDaemon = TurboBusDaemon
 
-__all__ = ["PoolDaemon", "TurboBusDaemon", "profile_key", "socket_path_for_user"]
+__all__ = ["PoolDaemon", "TurboBusDaemon", "profile_key", "reserve_socket", "socket_path_for_user"]

@@ -70,14 +70,40 @@ def _json_default(o):
     raise TypeError(f"not JSON serialisable: {type(o).__name__}")
 
 
+def reserve_socket(path: str, backlog: int = 128) -> socket.socket:
+    """Bind and listen on the AF_UNIX socket ``path`` (turbobus/daemon/server.py:3680).
+
+    A leftover socket file nobody listens on is removed first; a path that a
+    live server still answers on is refused, so a second daemon cannot take
+    over the first one's socket.
+    """
+    if os.path.exists(path):
+        probe = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        probe.settimeout(0.5)
+        try:
+            probe.connect(path)
+        except OSError:
+            os.unlink(path)  # stale: no listener behind it
+        else:
+            raise RuntimeError(f"socket {path} is served by a running process")
+        finally:
+            probe.close()
+    sock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+    try:
+        sock.bind(path)
+        sock.listen(int(backlog))
+    except BaseException:
+        sock.close()
+        raise
+    return sock
+
+
 def serve_unix(daemon, socket_path: str, *, stop_event: threading.Event | None = None,
-               ready_event: threading.Event | None = None, poll_seconds: float = 0.1) -> None:
-    """Accept connections until ``stop_event`` is set (forever if None)."""
-    if os.path.exists(socket_path):
-        os.unlink(socket_path)
-    server = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
-    server.bind(socket_path)
-    server.listen(128)
+               ready_event: threading.Event | None = None, poll_seconds: float = 0.1,
+               sock: socket.socket | None = None) -> None:
+    """Accept connections until ``stop_event`` is set (forever if None).
+    ``sock``: a socket already bound to ``socket_path`` by :func:`reserve_socket`."""
+    server = sock if sock is not None else reserve_socket(socket_path)
     server.settimeout(poll_seconds)
     if ready_event is not None:
         ready_event.set()

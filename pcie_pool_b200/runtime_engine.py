@@ -69,6 +69,22 @@ class RuntimeOptions:
                                     relay_min_effective_bw_gbps=self.relay_min_effective_bw_gbps,
                                     relay_min_direct_ratio=self.relay_min_direct_ratio)
 
+    def to_native(self):
+        """The native engine's options for these settings (``_C.EngineOptions``;
+        the reference returns its ``_turbobus.RuntimeOptions``,
+        turbobus/runtime_engine.py:87-107).  Planning fields stay on the
+        Python side (``planner_options``); the engine takes the staging ring
+        geometry, lane-kernel width, device timeout and peer setting."""
+        from ._native import native
+
+        o = native().EngineOptions()
+        o.slot_bytes = max(int(self.chunk_bytes), 1 << 20)
+        o.slots = int(self.staging_slots)
+        o.ctas_per_lane = int(self.ctas_per_lane)
+        o.timeout_s = float(self.timeout_s)
+        o.enable_peer_access = bool(self.enable_peer_access)
+        return o
+
 
 def read_json(path: str | Path) -> dict:
     with Path(path).open("r", encoding="utf-8") as fh:

@@ -42,6 +42,10 @@ class WorkerDataPlaneResources:
     target_device_ptr = property(lambda self: self.device_ptr)
     target_device_bytes = property(lambda self: self.device_bytes)
 
+    def close(self) -> None:
+        """Close this process's mapping of the shared CPU buffer."""
+        self.cpu_buffer.close()
+
     def as_dict(self) -> dict[str, object]:
         return {"transfer_id": self.request.transfer_id, "direction": self.request.direction,
                 "cpu_buffer_id": self.cpu_buffer.buffer_id, "host_bytes": self.host_bytes,

@@ -236,3 +236,41 @@ def test_device_trace_events_from_stamps():
                                                                           ("x:move", 0, 0.5, 2.5)]
     assert {e["tid"] for e in ev} == {0, 3} and len(ev) == 6
     assert device_trace_events(SimpleNamespace(trace=None), lanes) == []
+
+
+def test_native_options_backend_binding_and_prefix_release():
+    """RuntimeOptions.to_native fills the engine options; bind_runtime swaps
+    the native core under the CUDA backend; a saved prefix's CPU backings go
+    back to the connector's pool."""
+    from pcie_pool_b200.adapters.vllm_kv_connector import TurboBusCPUBackingPool, TurboBusSavedPrefix
+    from pcie_pool_b200.backends.cuda import CudaNativeBackend
+    from pcie_pool_b200.runtime_engine import RuntimeOptions
+
+    o = RuntimeOptions(chunk_bytes=8 << 20, staging_slots=4, ctas_per_lane=6, timeout_s=3.0).to_native()
+    assert (o.slot_bytes, o.slots, o.ctas_per_lane, o.timeout_s) == (8 << 20, 4, 6, 3.0)
+
+    class FakeNative:
+        def __init__(self):
+            self.devices = []
+
+        def set_device(self, d):
+            self.devices.append(d)
+
+    fake = FakeNative()
+    be = CudaNativeBackend()
+    be.bind_runtime(fake, None)
+    be.set_device(3)
+    assert fake.devices == [3]
+
+    import dataclasses
+
+    pool = TurboBusCPUBackingPool()
+    fields = {f.name for f in dataclasses.fields(TurboBusSavedPrefix)}
+    backing = ["layer0-backing"]
+    kw = {name: None for name in fields}
+    kw.update(cpu_backings=backing, block_count=2)
+    prefix = TurboBusSavedPrefix(**kw)
+    kv = []
+    pool.release_prefix(prefix, kv)
+    got, reused = pool.acquire(2, kv)
+    assert reused and got is backing

@@ -330,3 +330,18 @@ def test_socket_wire_roundtrip_with_peer_identity():
     finally:
         stop.set()
         t.join(5)
+
+
+def test_reserve_socket_refuses_a_live_socket_and_reclaims_a_stale_one(tmp_path):
+    from pcie_pool_b200.daemon.server import reserve_socket
+
+    path = str(tmp_path / "d.sock")
+    live = reserve_socket(path)
+    try:
+        with pytest.raises(RuntimeError, match="running process"):
+            reserve_socket(path)
+    finally:
+        live.close()
+    assert os.path.exists(path)  # closed listener leaves a stale file behind
+    again = reserve_socket(path)
+    again.close()

@@ -20,7 +20,7 @@ from pcie_pool_b200.daemon import InProcessDaemonClient, TurboBusDaemon
 from pcie_pool_b200.mock import FaultPlan, MockCudaBackend, MockDataPlane, MockWorkerExecutor, MockWorld
 from pcie_pool_b200.schema import ExecutionTicket, WorkerTransferAuthorizationRequest
 from pcie_pool_b200.topology import StaticTopologyProvider
-from pcie_pool_b200.worker import (WorkerDataPlaneResourceBinder, WorkerMessageCodecError,
+from pcie_pool_b200.worker import (WorkerDataPlaneCompletionEnvelope, WorkerDataPlaneResourceBinder, WorkerMessageCodecError,
                                    WorkerServiceRequestEnvelope, WorkerServiceSocketClient,
                                    WorkerServiceUnixSocketTransport, WorkerStagingPool, WorkerStagingPoolError,
                                    WorkerTransferClient, WorkerTransferService, build_worker_helper_transport,
@@ -226,6 +226,10 @@ def test_worker_over_unix_sockets_with_threaded_daemon():
         # a malformed line gets an error envelope, not a dropped connection
         bad = decode_worker_response_envelope(WorkerServiceSocketClient(wsock, 10.0).send_message("{not json"))
         assert not bad.ok and bad.error
+        # submit_envelope folds the response into a completion envelope
+        env = WorkerServiceSocketClient(wsock, 10.0).submit_envelope(
+            WorkerServiceRequestEnvelope(payload={"authorization": {"bogus": True}}))
+        assert isinstance(env, WorkerDataPlaneCompletionEnvelope) and not env.ok and env.error
     finally:
         stop.set()
         wthread.join(5)
