@@ -167,8 +167,8 @@ class TurboBusCPUBackingPool:
             return self._free[sig].pop(), True
         return self._allocate(block_count, kv_caches), False
 
-    def release(self, block_count: int, kv_caches: list[Any], backing) -> None:
-        self._free.setdefault(_signature(block_count, kv_caches), []).append(backing)
+    def release(self, block_count: int, kv_caches: list[Any], cpu_backings) -> None:
+        self._free.setdefault(_signature(block_count, kv_caches), []).append(cpu_backings)
 
     def release_prefix(self, prefix: "TurboBusSavedPrefix", kv_caches: list[Any]) -> None:
         """Return a saved prefix's CPU backings to the pool."""
@@ -193,11 +193,11 @@ class TurboBusConnectorMetadata(KVConnectorMetadata):
         self.requests: list[TurboBusRequestMetadata] = []
         self.save_requests: list[TurboBusRequestMetadata] = []
 
-    def add_request(self, r: TurboBusRequestMetadata) -> None:
-        self.requests.append(r)
+    def add_request(self, request: TurboBusRequestMetadata) -> None:
+        self.requests.append(request)
 
-    def add_save_request(self, r: TurboBusRequestMetadata) -> None:
-        self.save_requests.append(r)
+    def add_save_request(self, request: TurboBusRequestMetadata) -> None:
+        self.save_requests.append(request)
 
     def __len__(self) -> int:
         return len(self.requests) + len(self.save_requests)

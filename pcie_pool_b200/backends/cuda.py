@@ -15,8 +15,16 @@ IPC_HANDLE_BYTES = 64
 
 
 class CudaNativeBackend:
-    def __init__(self, native_loader=None) -> None:
+    """``runtime_engine_module``: a module whose ``_turbobus`` attribute is the
+    native core to use (the reference's constructor argument,
+    turbobus/backends/cuda.py:12); ``native_loader``: a callable returning it.
+    Neither: the in-tree ``pcie_pool_b200._C``."""
+
+    def __init__(self, runtime_engine_module=None, native_loader=None) -> None:
         self._loader = native_loader
+        native_core = getattr(runtime_engine_module, "_turbobus", None)
+        if native_core is not None:
+            self._loader = lambda: native_core
 
     def _native(self):
         if self._loader is not None:

@@ -523,7 +523,8 @@ class WorkerDataPlaneCompletionEnvelope:
             raise ValueError("lease_id must be included in lease_ids")
 
     @classmethod
-    def from_lifecycle(cls, lc: WorkerTransferLifecycleRecord) -> "WorkerDataPlaneCompletionEnvelope":
+    def from_lifecycle(cls, lifecycle: WorkerTransferLifecycleRecord) -> "WorkerDataPlaneCompletionEnvelope":
+        lc = lifecycle
         if not isinstance(lc, WorkerTransferLifecycleRecord):
             raise TypeError("lifecycle must be a WorkerTransferLifecycleRecord")
         d = lc.as_dict()
@@ -578,9 +579,9 @@ class WorkerServiceResponseEnvelope:
                 object.__setattr__(self, name, str(getattr(self, name)))
 
     @classmethod
-    def from_lifecycle(cls, lc: WorkerTransferLifecycleRecord) -> "WorkerServiceResponseEnvelope":
-        return cls(ok=True, completion=lc.completion_envelope().as_dict(), final_state=lc.final_state,
-                   error=lc.error)
+    def from_lifecycle(cls, lifecycle: WorkerTransferLifecycleRecord) -> "WorkerServiceResponseEnvelope":
+        return cls(ok=True, completion=lifecycle.completion_envelope().as_dict(), final_state=lifecycle.final_state,
+                   error=lifecycle.error)
 
     @classmethod
     def from_error(cls, error: str) -> "WorkerServiceResponseEnvelope":
@@ -849,8 +850,8 @@ class WorkerTransferService:
         except Exception as exc:  # noqa: BLE001 - every failure becomes an error envelope
             return WorkerServiceResponseEnvelope.from_error(str(exc))
 
-    def handle_envelope_payload(self, payload: Mapping[str, object]) -> dict[str, object]:
-        return self.handle_envelope(payload).as_dict()
+    def handle_envelope_payload(self, envelope: Mapping[str, object]) -> dict[str, object]:
+        return self.handle_envelope(envelope).as_dict()
 
 
 def parse_worker_authorization_request_payload(payload: Mapping[str, object]) -> WorkerTransferAuthorizationRequest:

@@ -27,7 +27,7 @@ def build_worker_helper_transport(daemon_socket_path: str, socket_path: str, *, 
     if staging_pool is not None:
         kw["staging_pool"] = staging_pool
     service = WorkerTransferService(transfer_client=WorkerTransferClient(daemon_client, **kw))
-    return WorkerServiceUnixSocketTransport(WorkerServiceEndpoint(service), socket_path)
+    return WorkerServiceUnixSocketTransport(WorkerServiceEndpoint(service=service), socket_path)
 
 
 def run_worker_helper_process(daemon_socket_path: str, socket_path: str, max_requests: int | None = None,
