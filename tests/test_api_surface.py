@@ -274,3 +274,31 @@ def test_native_options_backend_binding_and_prefix_release():
     pool.release_prefix(prefix, kv)
     got, reused = pool.acquire(2, kv)
     assert reused and got is backing
+
+
+def test_vllm_example_prompts_and_summary_lines():
+    """The vLLM example's prompt builder (random ids, byte-level text, second
+    save) and its COPY_SUMMARY lines, without an engine."""
+    from pcie_pool_b200.examples.vllm_kv_connector import (build_prompts, byte_token_ids, parse_args,
+                                                            prompt_text, summary_lines)
+
+    a = parse_args(["--prompt-tokens", "100", "--suffix-tokens", "5"])
+    p = build_prompts(a, 32000)
+    assert len(p["first"]) == 96 and p["restore"][:96] == p["first"] and len(p["restore"]) == 101
+    assert a.data_path == "engine" and a.restore_enabled and a.save_enabled
+
+    a = parse_args(["--prompt", "ab", "--prompt-repeat", "3", "--second-prompt-suffix", "!",
+                    "--second-save-prefix-key", "k2", "--second-save-prompt", "cd",
+                    "--daemon-socket-path", "/tmp/x.sock", "--no-restore"])
+    assert prompt_text("ab", 3) == "ab ab ab" and byte_token_ids("a", 32000) == [256 + 97]
+    p = build_prompts(a, 32000)
+    assert p["first"] == byte_token_ids("ab ab ab", 32000)
+    assert p["restore"] == byte_token_ids("cd cd cd", 32000) + byte_token_ids("!", 32000)
+    assert a.data_path == "intent" and not a.restore_enabled
+
+    summary = {"restore_prefix_key": "k2", "matched_tokens": 0, "prompt_tokens": 8, "restore_verified": None,
+               "restored_tokens": [5, 6]}
+    lines = summary_lines(a, summary, {"request_id": "r1", "block_count": 1, "bytes": 10}, {})
+    assert lines[0] == "COPY_SUMMARY_BEGIN" and lines[-1] == "COPY_SUMMARY_END"
+    assert any(l.startswith("vllm_kv_connector_save source_request=r1") for l in lines)
+    assert "generated_tokens=5,6" in lines[-2]
