@@ -302,3 +302,67 @@ def test_vllm_example_prompts_and_summary_lines():
     assert lines[0] == "COPY_SUMMARY_BEGIN" and lines[-1] == "COPY_SUMMARY_END"
     assert any(l.startswith("vllm_kv_connector_save source_request=r1") for l in lines)
     assert "generated_tokens=5,6" in lines[-2]
+
+
+def test_vllm_sweep_rows_commands_and_outputs(tmp_path):
+    import json
+
+    from pcie_pool_b200.examples import vllm_kv_connector_sweep as S
+
+    a = S.parse_args(["--restore-blocks-list", "0,4", "--case-ids", "engine,daemon",
+                      "--summary-output", str(tmp_path / "s.txt"), "--cases-json-output", str(tmp_path / "c.json"),
+                      "--cases-csv-output", str(tmp_path / "c.csv")])
+    cmd = S.case_command(a, "daemon", 1024, 4, tmp_path / "x.log")
+    assert cmd[cmd.index("--data-path") + 1] == "intent" and cmd[cmd.index("--matched-tokens") + 1] == "64"
+    assert "--log-output" in cmd
+    summary = {"data_path": "engine", "job_id": "j", "session_id": "s", "save_ms": 2.0, "save_cuda_ms": 1.0,
+               "restore_ms": 1.0, "restore_cuda_ms": 0.5, "bytes_completed": 1 << 30, "save_blocks": 64,
+               "restore_blocks": 64, "restore_verified": True, "prompt_tokens": 1024}
+    row = S.case_row("engine", 1024, 0, 16, 0, "noise\nVLLM_KV_SUMMARY " + json.dumps(summary), None)
+    assert row["restore_gib_s"] == "1000.000" and row["restore_verified"] is True
+    bad = S.case_row("engine", 1024, 0, 16, 1, "", None)
+    assert bad["save_ms"] == "NA" and bad["returncode"] == 1
+    lines = S.summary_lines(a, [row, bad])
+    assert lines[0] == "SWEEP_SUMMARY_BEGIN" and lines[-1] == "SWEEP_SUMMARY_END" and len(lines) == 5
+    S.write_outputs(a, [row, bad], lines)
+    assert json.loads((tmp_path / "c.json").read_text())[0]["case_id"] == "engine"
+    assert (tmp_path / "c.csv").read_text().splitlines()[0].startswith("case_id,prompt_tokens")
+
+
+def test_vllm_probe_describers_and_observer_wrapping():
+    """The probe's text forms and its wrapper install/remove, on stand-in
+    classes (no engine)."""
+    import types
+
+    from pcie_pool_b200.examples import vllm_probe as P
+
+    class Blocks:
+        def get_block_ids(self, allow_none=False):
+            return ([3, 4],)
+
+    assert P.describe_blocks(Blocks()) == "([3, 4],)" and P.describe_blocks(None) == "None"
+    assert P.describe_value({"a": [1, 2]}) == "dict{a:list[int,int]}"
+    cfg = types.SimpleNamespace(num_blocks=7, kv_cache_tensors=[1, 2], kv_cache_groups=[
+        types.SimpleNamespace(layer_names=["l0", "l1"], kv_cache_spec=types.SimpleNamespace(block_size=16))])
+    assert P.describe_cache_config(cfg).startswith("num_blocks=7 tensor_count=2 group_count=1 groups=[g0:layers=2")
+    a = P.parse_args(["--model", "/m", "--max-tokens", "3"])
+    assert a.model == "/m" and a.max_tokens == 3 and not a.run
+
+
+def test_vllm_probe_observers_wrap_and_restore_vllm_methods():
+    pytest.importorskip("vllm")
+    from vllm.v1.core import kv_cache_manager as km
+    from vllm.v1.worker import gpu_model_runner as gm
+
+    from pcie_pool_b200.examples import vllm_probe as P
+
+    before = (gm.GPUModelRunner.initialize_kv_cache, km.KVCacheManager.allocate_slots,
+              km.KVCacheManager.get_computed_blocks)
+    saved = P.install_observers(emit=lambda line: None)
+    try:
+        assert len(saved) == 3 and km.KVCacheManager.allocate_slots is not before[1]
+        assert km.KVCacheManager.allocate_slots.__wrapped__ is before[1]
+    finally:
+        P.remove_observers(saved)
+    assert (gm.GPUModelRunner.initialize_kv_cache, km.KVCacheManager.allocate_slots,
+            km.KVCacheManager.get_computed_blocks) == before
