@@ -69,21 +69,37 @@ def build_workload_commands(args, workload: str, paths: dict[str, Path]) -> list
         return [py + ["pcie_pool_b200.benchmarks.model_loading", *_common(args), "--job-id", f"{args.job_id}-model",
                       "--source-buffer-id", args.cpu_buffer_id, "--destination-buffer-id", args.gpu_buffer_id,
                       "--bucket-count", str(args.bucket_count), "--bucket-bytes", str(args.bucket_bytes),
-                      "--run-id", args.run_id, *outs]]
+                      "--storage-layout", args.storage_layout, "--run-id", args.run_id, *outs]]
     if workload in ("training-offload", "optimizer-offload"):
         cmd = py + ["pcie_pool_b200.benchmarks.training_offload", *_common(args), "--job-id",
                     f"{args.job_id}-{workload.split('-')[0]}", "--cpu-buffer-id", args.cpu_buffer_id,
                     "--gpu-buffer-id", args.gpu_buffer_id, "--workload-kind", KIND[workload],
                     "--bucket-count", str(args.bucket_count), "--bucket-bytes", str(args.bucket_bytes),
-                    "--compute-delay-ms", str(args.compute_delay_ms), "--run-id", args.run_id, *outs]
+                    "--compute-delay-ms", str(args.compute_delay_ms), "--storage-layout", args.storage_layout,
+                    "--run-id", args.run_id, *outs]
         if args.active_buckets:
             cmd += ["--active-buckets", str(args.active_buckets)]
         return [cmd]
     cmds = []
     for j in range(max(1, int(args.jobs))):
-        cmds.append(py + ["pcie_pool_b200.examples.vllm_kv_connector", "--json-output",
-                          str(paths["json"].with_suffix(f".job{j}.json")), "--session-id", f"{args.session_id}-kv{j}",
-                          "--job-id", f"{args.job_id}-kv{j}", "--prompt-tokens", str(args.vllm_prompt_tokens)])
+        cmd = py + ["pcie_pool_b200.examples.vllm_kv_connector", "--json-output",
+                    str(paths["json"].with_suffix(f".job{j}.json")), "--session-id", f"{args.session_id}-kv{j}",
+                    "--job-id", f"{args.job_id}-kv{j}", "--prompt-tokens", str(args.vllm_prompt_tokens),
+                    "--prefix-key", f"{args.vllm_prefix_key}-{j}", "--prompt-repeat", str(args.vllm_prompt_repeat),
+                    "--second-prompt-suffix", args.vllm_second_prompt_suffix,
+                    "--restore-blocks", str(args.vllm_restore_blocks),
+                    "--matched-tokens", str(args.vllm_matched_tokens), "--chunk-bytes", str(args.chunk_bytes)]
+        if args.vllm_model:
+            cmd += ["--model", args.vllm_model]
+        if args.vllm_prompt:
+            cmd += ["--prompt", args.vllm_prompt]
+        if args.vllm_wait_timeout_seconds is not None:
+            cmd += ["--wait-timeout-seconds", str(args.vllm_wait_timeout_seconds)]
+        if args.vllm_enable_multiproc_executor:
+            cmd.append("--enable-multiproc-executor")
+        if args.daemon_socket_path:
+            cmd += ["--daemon-socket-path", args.daemon_socket_path]
+        cmds.append(cmd)
     return cmds
 
 
@@ -269,8 +285,20 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--bucket-bytes", type=int, default=32 << 20)
     p.add_argument("--compute-delay-ms", type=float, default=0.0)
     p.add_argument("--wait-timeout-seconds", type=float, default=600.0)
-    p.add_argument("--jobs", type=int, default=1, help="concurrent vLLM KV jobs")
-    p.add_argument("--vllm-prompt-tokens", type=int, default=4096)
+    p.add_argument("--jobs", "--vllm-job-count", dest="jobs", type=int, default=1, help="concurrent vLLM KV jobs")
+    p.add_argument("--storage-layout", choices=["packed", "separate"], default="packed",
+                   help="host layout of the model-loading / training buckets")
+    p.add_argument("--vllm-prompt-tokens", type=int, default=4096, help="random-token prefix length")
+    p.add_argument("--vllm-model", default="", help="local checkpoint (default: random-init demo model)")
+    p.add_argument("--vllm-prompt", default="", help="text prompt (default: random token ids)")
+    p.add_argument("--vllm-prompt-repeat", type=int, default=64)
+    p.add_argument("--vllm-second-prompt-suffix", default=" Italy")
+    p.add_argument("--vllm-prefix-key", default="paper-validation-vllm-kv")
+    p.add_argument("--vllm-restore-blocks", type=int, default=0, help="restore cap in blocks (0 = all)")
+    p.add_argument("--vllm-matched-tokens", type=int, default=0, help="tokens to restore (0 = whole prefix)")
+    p.add_argument("--vllm-wait-timeout-seconds", type=float, default=None)
+    p.add_argument("--vllm-enforce-eager", action="store_true", help="accepted; the demo runs eager by default")
+    p.add_argument("--vllm-enable-multiproc-executor", action="store_true")
     p.add_argument("--dry-run", action="store_true")
     p.add_argument("--keep-going", action="store_true")
     p.add_argument("--output-dir", default="results/paper_validation")

@@ -191,6 +191,21 @@ def test_paper_validation_dry_run_and_metric_line(tmp_path):
                                  "turbobus-daemon")[0]
     assert not pv.metric_errors(m)
     assert pv.metric_line(m).startswith("paper_metric workload=model-loading report_schema=")
+    # reference flags reach the workload commands
+    args = pv.build_parser().parse_args(["--session-id", "s", "--cpu-buffer-id", "c", "--gpu-buffer-id", "g",
+                                         "--storage-layout", "separate", "--vllm-job-count", "2",
+                                         "--vllm-prompt", "hello", "--vllm-matched-tokens", "64",
+                                         "--vllm-enable-multiproc-executor"])
+    paths = {"json": tmp_path / "w.json", "summary": tmp_path / "w.txt"}
+    ml = pv.build_workload_commands(args, "model-loading", paths)[0]
+    assert ml[ml.index("--storage-layout") + 1] == "separate"
+    kv = pv.build_workload_commands(args, "vllm-kv", paths)
+    assert len(kv) == 2 and kv[1][kv[1].index("--prompt") + 1] == "hello"
+    assert kv[0][kv[0].index("--matched-tokens") + 1] == "64" and "--enable-multiproc-executor" in kv[0]
+    from pcie_pool_b200.examples.vllm_kv_connector import parse_args as kv_args
+
+    parsed = kv_args(kv[0][kv[0].index("pcie_pool_b200.examples.vllm_kv_connector") + 1:])
+    assert parsed.prompt == "hello" and parsed.disable_multiproc_executor is False
 
 
 def test_examples_entry_points():
