@@ -142,12 +142,17 @@ def test_offload_store_state_machine():
 
 
 def _report(policy, ms):
-    return {"config": {"policy": policy}, "workloads": [{"workload": "model-loading", "status": "passed",
-                                                         "returncode": 0, "data_path": "", "metrics": [{
-        "workload": "model-loading", "report_schema": "x", "policy": policy, "job_id": "j", "session_id": "s",
-        "workload_kind": "model_weights", "transfer_ms": ms, "performance_ms": ms, "throughput_gib_s": 1000 / ms,
-        "transfer_bytes": 10, "bytes_completed": 10, "direct_bytes": 10, "relay_bytes": 0,
-        "correctness_status": "complete", "decision_ids": "d1"}]}]}
+    def metric(workload, kind, job):
+        return {"workload": workload, "report_schema": "x", "policy": policy, "job_id": job, "session_id": "s",
+                "workload_kind": kind, "transfer_ms": ms, "performance_ms": ms, "throughput_gib_s": 1000 / ms,
+                "transfer_bytes": 10, "bytes_completed": 10, "direct_bytes": 10, "relay_bytes": 0,
+                "correctness_status": "complete", "decision_ids": "d1"}
+
+    return {"config": {"policy": policy}, "workloads": [
+        {"workload": "model-loading", "status": "passed", "returncode": 0, "data_path": "",
+         "metrics": [metric("model-loading", "model_weights", "j")]},
+        {"workload": "vllm-kv", "status": "passed", "returncode": 0, "data_path": "",
+         "metrics": [metric("vllm-kv", "kv_cache", "kv0")]}]}
 
 
 def test_phase7_compare_check_gate_inventory(tmp_path):
@@ -161,19 +166,48 @@ def test_phase7_compare_check_gate_inventory(tmp_path):
     broken = json.loads(json.dumps(pooled))
     broken["workloads"][0]["metrics"][0]["bytes_completed"] = 3
     assert "model-loading:bytes_incomplete" in phase7.check_report(broken)["errors"]
-    ev = phase7.evidence_report(pooled, {"audit_records": [{"job_id": "j", "event_type": "worker_completion"}],
-                                         "relay_quotas": {"1": {"active_chunks": 0}}, "reservations": {}})
-    assert ev["ok"] and ev["metrics"][0]["audit_records"] == 1
-    gate = phase7.gate_bundle("8gpu", base, pooled, cmp_, [ev], required=("model-loading",))
-    assert gate["status"] == "accepted", gate["reasons"]
+    ev = phase7.evidence_report(pooled, {"audit_records": [{"job_id": "j", "event_type": "worker_completion"},
+                                                           {"job_id": "kv0", "event_type": "worker_completion"}],
+                                         "relay_quotas": {"1": {"active_chunks": 0}}, "reservations": {}},
+                                cmp_)
+    assert ev["ok"] and ev["metrics"][0]["audit_records"] == 1 and ev["workloads"][0]["flags"]["has_audit_record"]
+    req = ("model-loading", "vllm-kv")
+    gate = phase7.gate_bundle("8gpu", base, pooled, cmp_, [ev], required=req)
+    assert gate["ok"] and gate["status"] == "accepted", gate["errors"]
+    assert gate["warnings"] == ["correctness:not_provided"]
+    # labels, provided checks and correctness artifacts can each block the bundle
+    assert "baseline:policy_mismatch:paper-baseline" in phase7.gate_bundle(
+        "8gpu", base, pooled, cmp_, [ev], required=req, baseline_label="other")["errors"]
+    assert "turbobus:provided_check_failed" in phase7.gate_bundle(
+        "8gpu", base, pooled, cmp_, [ev], required=req, turbobus_check={"ok": False})["errors"]
+    assert "correctness:0:failed" in phase7.gate_bundle(
+        "8gpu", base, pooled, cmp_, [ev], required=req, correctness=[{"commands": [{"returncode": 1}]}])["errors"]
+    assert phase7.correctness_state({"status": "passed"}) == (True, [])
     gp = tmp_path / "gate.json"
     gp.write_text(json.dumps(gate))
     manifest = phase7.ingest(tmp_path / "manifest.json", gp)
-    inv = phase7.inventory(manifest)
-    assert inv["accepted"] == ["8gpu"] and not inv["complete"]
-    plan = phase7.server_run_plan(phase7.build_parser().parse_args(["server-run", "--server-class", "2gpu",
-                                                                    "--output-root", str(tmp_path)]))
-    assert [s["name"] for s in plan["steps"]][:2] == ["paper-validation-baseline", "paper-validation-pooled"]
+    inv = phase7.inventory(manifest, base_dir=tmp_path)
+    assert inv["accepted"] == ["8gpu"] and not inv["complete"] and inv["real_workload_accepted"]
+    assert "2gpu:missing_manifest_entry" in inv["errors"]
+    # a blocked class needs its environment gap and next commands
+    res = phase7.ingest_entry(tmp_path / "manifest.json", phase7.build_entry("2gpu", "blocked", tmp_path / "m"))
+    assert not res["written"] and "2gpu:blocked_missing_environment_gap" in res["errors"]
+    res = phase7.ingest_entry(tmp_path / "manifest.json",
+                              phase7.build_entry("2gpu", "blocked", tmp_path / "m", block_reason="no 2-GPU host",
+                                                 next_commands=["phase7 server-run --server-class 2gpu"]),
+                              allow_incomplete_inventory=True)
+    assert res["written"] and res["ok"] and not res["inventory_ok"]
+    assert [e["server_class"] for e in json.loads((tmp_path / "manifest.json").read_text())["server_classes"]] == \
+        ["2gpu", "8gpu"]
+    plan = phase7.server_run_plan(phase7.build_parser().parse_args(
+        ["server-run", "--server-class", "2gpu", "--output-root", str(tmp_path), "--profile", "p.json",
+         "--correctness", "c.json", "--vllm-model", "/m", "--allow-incomplete-inventory"]))
+    names = [s["name"] for s in plan["steps"]]
+    assert names[:2] == ["paper-validation-baseline", "paper-validation-pooled"] and names[-1] == "ingest"
+    steps = {s["name"]: s["command"] for s in plan["steps"]}
+    assert "--profile" in steps["evidence"] and "--correctness" in steps["gate"]
+    assert "--baseline-check" in steps["gate"] and "--allow-incomplete-inventory" in steps["ingest"]
+    assert steps["paper-validation-pooled"][steps["paper-validation-pooled"].index("--vllm-model") + 1] == "/m"
 
 
 def test_paper_validation_dry_run_and_metric_line(tmp_path):
