@@ -809,9 +809,12 @@ class TurboBusDaemon:
                     profile_bytes: int = 0, updated_at: float | None = None) -> DaemonResponse:
         target = int(target_gpu)
         relays = norm_relays(relay_gpus)
+        try:
+            norm = normalize_profile(profile, target)
+        except (TypeError, ValueError) as exc:
+            return fail(str(exc))
         entry = {"target_gpu": target, "relay_gpus": relays, "profile_bytes": int(profile_bytes),
-                 "updated_at": float(self._now() if updated_at is None else updated_at),
-                 "profile": normalize_profile(profile, target)}
+                 "updated_at": float(self._now() if updated_at is None else updated_at), "profile": norm}
         with self._lock:
             self._purge_profiles(self._now())
             self._st.profiles[profile_key(target, relays)] = entry
