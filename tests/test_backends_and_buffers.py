@@ -9,7 +9,6 @@ from __future__ import annotations
 
 from types import SimpleNamespace
 
-import numpy as np
 import pytest
 
 from pcie_pool_b200.backends.cuda import CudaNativeBackend, coerce_ipc_handle
