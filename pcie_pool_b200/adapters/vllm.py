@@ -18,7 +18,8 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
-from typing import Iterable, Mapping
+from collections.abc import Mapping
+from typing import Iterable
 
 import numpy as np
 

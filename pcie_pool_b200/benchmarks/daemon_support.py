@@ -10,7 +10,8 @@ from __future__ import annotations
 import os
 from dataclasses import asdict
 from enum import Enum
-from typing import Iterable, Mapping
+from collections.abc import Mapping
+from typing import Iterable
 
 from ..schema import TransferIntent, TransferReceipt, WorkloadKind
 

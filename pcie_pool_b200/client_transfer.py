@@ -13,7 +13,8 @@ planning releases the planned relay leases.
 from __future__ import annotations
 
 from dataclasses import asdict, dataclass, field
-from typing import Iterable, Mapping
+from collections.abc import Mapping
+from typing import Iterable
 
 from .client import CudaIpcDeviceBuffer, SharedPinnedCpuBuffer
 from .schema import (BufferRegistration, DaemonResponse, ExecutionTicket, WorkerTransferAuthorizationRequest)

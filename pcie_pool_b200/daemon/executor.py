@@ -215,7 +215,7 @@ class EngineDataPlane:
             measured["fallback_reason"] = (f"lane failover: relay {failover['failed_lane_device']} failed, "
                                            f"re-ran on {failover['rerun_on_device']}")
         if self.checksum and r.checksums is not None and len(r.checksums):
-            measured["chunk_checksums"] = [[int(a), int(b)] for a, b in r.checksums]
+            measured["chunk_checksums"] = np.asarray(r.checksums, dtype=np.uint64).reshape(-1, 2).tolist()
         return ExecutionResult(ok=r.ok, bytes_completed=r.bytes if r.ok else 0,
                                error=None if r.ok else r.error, measured=measured)
 

@@ -25,10 +25,12 @@ from __future__ import annotations
 import json
 import os
 import threading
+from collections import deque
 import time
 import uuid
 from dataclasses import dataclass, field
-from typing import Any, Callable, Iterable, Mapping
+from collections.abc import Mapping
+from typing import Any, Callable, Iterable
 
 from ..scheduler import DaemonScheduler, scheduling_decision_leases, scheduling_decision_stats
 from ..schema import contract_asdict as asdict
@@ -83,7 +85,10 @@ class DaemonState:
     reservation_transfer: dict[str, str] = field(default_factory=dict)
     intents: dict[str, TransferIntent] = field(default_factory=dict)
     intent_transfer: dict[str, str] = field(default_factory=dict)
-    queue: list[str] = field(default_factory=list)
+    queue: dict[str, None] = field(default_factory=dict)    # transfer ids in submit order (ordered set)
+    live: dict[str, None] = field(default_factory=dict)     # the non-terminal ones among them
+    terminal_order: deque = field(default_factory=deque)    # terminal ids, oldest first (history trim)
+    ticket_ids: dict[str, list[str]] = field(default_factory=dict)  # transfer id -> every ticket issued
     queue_records: dict[str, dict[str, Any]] = field(default_factory=dict)
     version: int = 0
     plan_requests: dict[str, dict[str, Any]] = field(default_factory=dict)
@@ -118,7 +123,8 @@ class TurboBusDaemon:
                  topology_provider: TopologyProvider | None = None, *,
                  scheduler: DaemonScheduler | None = None, executor=None,
                  profile_store_path: str | None = None,
-                 clock: Callable[[], float] = time.time, link_hold_seconds: float = 1.0) -> None:
+                 clock: Callable[[], float] = time.time, link_hold_seconds: float = 1.0,
+                 history_limit: int = 10000, audit_limit: int = 100000) -> None:
         self._lock = threading.RLock()
         self._changed = threading.Condition(self._lock)
         self._st = DaemonState()
@@ -131,6 +137,12 @@ class TurboBusDaemon:
         # shard each step, and relaying through it only queues another job's
         # chunks in front of that GPU's own on its link.  0 disables.
         self._link_hold = max(0.0, float(link_hold_seconds))
+        # A long-running daemon keeps the records of the last ``history_limit``
+        # finished transfers (receipts, statuses, plans, tickets) and the last
+        # ``audit_limit`` audit records; older ones are dropped, so memory and
+        # the per-request bookkeeping stay bounded.
+        self._history_limit = max(1, int(history_limit))
+        self._audit_limit = max(1, int(audit_limit))
         self._clock = clock
         self._quotas = {g: RelayQuota(relay_gpu=g, max_sessions=int(max_sessions_per_relay),
                                       max_inflight_chunks=int(max_inflight_chunks_per_relay))
@@ -472,8 +484,7 @@ class TurboBusDaemon:
             ticket = None
             if self._st.admissions.get(tid, {}).get("state") == ADMITTED:
                 ticket = self._intent_ticket(intent, tid, decision, now)
-                self._st.tickets[ticket.ticket_id] = ticket
-                self._st.transfer_tickets[tid] = ticket.ticket_id
+                self._store_ticket(tid, ticket)
             self._refresh_record(tid, now)
             receipt = self._receipt(intent.intent_id)
             resp = ok(receipt=asdict(receipt), transfer_id=tid, decision=asdict(decision),
@@ -660,8 +671,7 @@ class TurboBusDaemon:
             return fail("lease expired")
         ticket = self._plan_ticket(req.transfer_id, decision, auth.src_buffer.buffer_id,
                                    auth.dst_buffer.buffer_id, now, exp, tuple(l.lease_id for l in related))
-        S.tickets[ticket.ticket_id] = ticket
-        S.transfer_tickets[req.transfer_id] = ticket.ticket_id
+        self._store_ticket(req.transfer_id, ticket)
         records = {}
         for l in related:
             rr = relay_ranges(plan, l.relay_gpu, req.direction)
@@ -735,8 +745,7 @@ class TurboBusDaemon:
             self._touch(session.session_id, now)
             if not reservations and len(bids) >= 2 and direct_only(decision):
                 tk = self._plan_ticket(tid, decision, bids[0], bids[1], now, None, ())
-                S.tickets[tk.ticket_id] = tk
-                S.transfer_tickets[tid] = tk.ticket_id
+                self._store_ticket(tid, tk)
             return DaemonResponse(ok=True, payload=self._planned_payload(tid, decision, status, session,
                                                                          relays, elig, reservations))
 
@@ -788,8 +797,7 @@ class TurboBusDaemon:
         ticket = None
         if intent is not None and adm["state"] == ADMITTED:
             ticket = self._intent_ticket(intent, tid, decision, at)
-            S.tickets[ticket.ticket_id] = ticket
-            S.transfer_tickets[tid] = ticket.ticket_id
+            self._store_ticket(tid, ticket)
         self._refresh_record(tid, at)
         self._touch(session.session_id, at)
         payload = self._planned_payload(tid, decision, st, session, relays, elig, reservations)
@@ -933,7 +941,7 @@ class TurboBusDaemon:
     def _readmit_delayed(self) -> None:
         """Re-plan delayed intents now that capacity may have been freed."""
         S = self._st
-        for tid in list(S.queue):
+        for tid in list(S.live):
             adm = S.admissions.get(tid, {})
             st = S.statuses.get(tid)
             if adm.get("state") != DELAYED or st is None or st.state in TERMINAL_STATES:
@@ -1202,7 +1210,7 @@ class TurboBusDaemon:
             max_inflight_chunks=session.max_inflight_chunks, active_chunks=session.active_chunks,
             active=session.active, created_at=session.created_at, last_seen=session.last_seen,
             closed_at=session.closed_at)
-        state = self._runtime_state(now)
+        state = self._runtime_state(now, active_only=True)
         if exclude is not None:
             state = state_without_transfer(state, str(exclude))
         decision = self._scheduler.plan_transfer(
@@ -1246,7 +1254,7 @@ class TurboBusDaemon:
     def _admission_block(self, session: Session, leases) -> str | None:
         if session.active_chunks + sum(l.chunk_limit for l in leases) > session.max_inflight_chunks:
             return "session relay admission is delayed by chunk quota"
-        busy = busy_relays(self._runtime_state())
+        busy = busy_relays(self._runtime_state(active_only=True))
         for l in leases:
             if l.relay_device not in session.relay_gpus:
                 return "relay admission is delayed by session relay ownership"
@@ -1599,7 +1607,8 @@ class TurboBusDaemon:
     def _record_planned(self, tid, status, intent_id, bids, total, chunk, ranges, direction, decision, now):
         S = self._st
         adm = S.admissions.get(tid, {})
-        S.queue.append(tid)
+        S.queue[tid] = None
+        S.live[tid] = None
         S.queue_records[tid] = {
             "transfer_id": tid, "intent_id": None if intent_id is None else str(intent_id),
             "decision_id": decision.decision_id, "topology_snapshot_id": decision.topology_snapshot_id,
@@ -1622,6 +1631,49 @@ class TurboBusDaemon:
     _SIG = ("state", "bytes_completed", "error", "intent_id", "source_buffer_id", "destination_buffer_id",
             "workload_kind", "priority", "admission_state", "plan_generation", "plan_expires_at",
             "started_at", "completed_at")
+
+    def _store_ticket(self, tid: str, ticket: ExecutionTicket) -> None:
+        S = self._st
+        S.tickets[ticket.ticket_id] = ticket
+        S.transfer_tickets[str(tid)] = ticket.ticket_id
+        S.ticket_ids.setdefault(str(tid), []).append(ticket.ticket_id)
+
+    def _trim_history(self) -> None:
+        """Forget the oldest finished transfers beyond ``history_limit`` (a
+        transfer whose leases are still held is kept until they are released)
+        and the oldest audit / cleanup records beyond ``audit_limit``."""
+        S = self._st
+        held = None
+        skipped = []
+        while len(S.terminal_order) > self._history_limit:
+            tid = S.terminal_order.popleft()
+            if tid in S.live:
+                continue
+            if held is None:
+                held = set(S.reservation_transfer.values())
+            if tid in held:
+                skipped.append(tid)
+                if len(skipped) > 64:
+                    break
+                continue
+            self._forget_transfer(tid)
+        S.terminal_order.extendleft(reversed(skipped))
+        for lst in (S.audit, S.cleanup_events, S.system_cleanup_events):
+            if len(lst) > self._audit_limit + self._audit_limit // 8:
+                del lst[:len(lst) - self._audit_limit]
+
+    def _forget_transfer(self, tid: str) -> None:
+        S = self._st
+        req = S.plan_requests.get(tid) or {}
+        iid = req.get("intent_id")
+        if iid is not None and S.intent_transfer.get(str(iid)) == tid:
+            S.intent_transfer.pop(str(iid), None)
+            S.intents.pop(str(iid), None)
+        for tk in S.ticket_ids.pop(tid, ()):
+            S.tickets.pop(tk, None)
+        for d in (S.queue, S.queue_records, S.statuses, S.plans, S.decisions, S.plan_requests, S.admissions,
+                  S.generations, S.plan_expiry, S.completed_at, S.measured, S.transfer_tickets):
+            d.pop(tid, None)
 
     def _refresh_record(self, tid: str, now: float | None = None) -> dict | None:
         S = self._st
@@ -1652,6 +1704,9 @@ class TurboBusDaemon:
             rec["completed_at"] = at
             for g in rec.get("target_devices", ()) or ():
                 S.target_seen[int(g)] = max(at, S.target_seen.get(int(g), at))
+        if st.state in TERMINAL_STATES and S.live.pop(str(tid), 0) is None:
+            S.terminal_order.append(str(tid))
+            self._trim_history()
         it = S.intents.get(str(rec.get("intent_id"))) if rec.get("intent_id") is not None else None
         if it is not None:
             rec.update(intent_id=it.intent_id, source_buffer_id=it.source_buffer_id,
@@ -1662,12 +1717,17 @@ class TurboBusDaemon:
             S.version += 1
         return rec
 
-    def _runtime_state(self, now: float | None = None) -> dict[str, Any]:
+    def _runtime_state(self, now: float | None = None, active_only: bool = False) -> dict[str, Any]:
+        """Resource state over the queued transfers.  ``active_only`` (what
+        planning and admission need) covers only non-terminal transfers, so its
+        cost does not grow with the daemon's history; ``describe`` reports the
+        retained history as well."""
         S = self._st
         at = float(self._now() if now is None else now)
-        for t in tuple(S.queue):
+        for t in tuple(S.live):
             self._refresh_record(t, at)
-        recs = [dict(S.queue_records[t]) for t in S.queue if t in S.queue_records]
+        ids = S.live if active_only else S.queue
+        recs = [dict(S.queue_records[t]) for t in ids if t in S.queue_records]
         sub, run = TransferStatusState.SUBMITTED.value, TransferStatusState.RUNNING.value
         queued = [r for r in recs if r.get("state") == sub]
         running = [r for r in recs if r.get("state") == run]

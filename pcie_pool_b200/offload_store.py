@@ -14,7 +14,8 @@ from __future__ import annotations
 import uuid
 from dataclasses import dataclass, field
 from enum import Enum
-from typing import Iterable, Mapping, Protocol
+from collections.abc import Mapping
+from typing import Iterable, Protocol
 
 from .schema import (FORBIDDEN_POLICY_KEYS, TERMINAL_STATES, TransferIntent, TransferReceipt, TransferStatusState,
                      WorkloadKind)

@@ -10,7 +10,8 @@ turbobus/plan_trace.py:43-47) convert with :func:`lanes_from_plan`.
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import Iterable, Mapping, Sequence
+from collections.abc import Mapping
+from typing import Iterable, Sequence
 
 import numpy as np
 
@@ -41,12 +42,8 @@ class Lane:
 
 def make_lane(device: int, chunks: Iterable, **extra) -> Lane:
     """Lane from (src_off, dst_off, bytes) tuples or dicts."""
-    rows = []
-    for c in chunks:
-        if isinstance(c, Mapping):
-            rows.append((int(c["src_offset"]), int(c["dst_offset"]), int(c["bytes"])))
-        else:
-            rows.append((int(c[0]), int(c[1]), int(c[2])))
+    rows = [(c["src_offset"], c["dst_offset"], c["bytes"]) if isinstance(c, Mapping) else (c[0], c[1], c[2])
+            for c in chunks]
     a = np.array(rows, dtype=np.uint64).reshape(-1, 3)
     return Lane(device, a[:, 0].copy(), a[:, 1].copy(), a[:, 2].copy(), **extra)
 

@@ -12,7 +12,8 @@ from __future__ import annotations
 import json
 import time
 from pathlib import Path
-from typing import Any, Mapping
+from collections.abc import Mapping
+from typing import Any
 
 from .planner_types import (PlannerChunk, PlannerPath, PlannerPathAssignment,
                             PlannerTransferPlan)

@@ -25,7 +25,8 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass, field
-from typing import Iterable, Mapping, Sequence
+from collections.abc import Mapping
+from typing import Iterable, Sequence
 
 from .planner_types import (PlannerChunk, PlannerPath, PlannerPathAssignment,
                             PlannerTransferPlan)

@@ -17,7 +17,8 @@ import json
 import time
 from dataclasses import dataclass, field
 from pathlib import Path
-from typing import Any, Iterable, Mapping, Sequence
+from collections.abc import Mapping
+from typing import Any, Iterable, Sequence
 
 from .plan_trace import transfer_plan_to_dict
 from .schema import TransferMode

@@ -16,7 +16,8 @@ from __future__ import annotations
 
 import uuid
 from dataclasses import dataclass
-from typing import Callable, Mapping
+from collections.abc import Mapping
+from typing import Callable
 
 from ..planner_engine import PlannerEngine
 from ..planner_types import PlannerLease, PlannerStats, PlannerTransferPlan

@@ -12,7 +12,7 @@ mixed fleets arbitrate identically.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Mapping
+from collections.abc import Mapping
 
 from ..schema import WorkloadKind
 

@@ -15,7 +15,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass, field, fields, is_dataclass
 from enum import Enum
-from typing import Any, Callable, Mapping
+from collections.abc import Mapping
+from typing import Any, Callable
 
 
 # ---- enums -------------------------------------------------------------------------
@@ -188,13 +189,16 @@ def coerce_direction(value: Any, name: str = "direction") -> str:
 
 def byte_ranges(value: Any, name: str = "ranges") -> tuple[dict[str, int], ...]:
     out = []
+    append = out.append
     for item in value:
-        src, dst, n = int(item["src_offset"]), int(item["dst_offset"]), int(item["bytes"])
+        src, dst, n = item["src_offset"], item["dst_offset"], item["bytes"]
+        if type(src) is not int or type(dst) is not int or type(n) is not int:  # noqa: E721 - exact ints pass as is
+            src, dst, n = int(src), int(dst), int(n)
         if src < 0 or dst < 0:
             raise ValueError("range offsets must be non-negative")
         if n <= 0:
             raise ValueError("range bytes must be positive")
-        out.append({"src_offset": src, "dst_offset": dst, "bytes": n})
+        append({"src_offset": src, "dst_offset": dst, "bytes": n})
     return tuple(out)
 
 

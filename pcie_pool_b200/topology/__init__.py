@@ -12,7 +12,8 @@ port share one uplink and are planned against its concurrent capacity.
 from __future__ import annotations
 
 from dataclasses import asdict, dataclass, field
-from typing import Iterable, Mapping
+from collections.abc import Mapping
+from typing import Iterable
 
 from ..schema import as_bool, as_float, nonempty, nonneg_float, nonneg_int, opt
 

@@ -21,7 +21,8 @@ import subprocess
 import time
 from dataclasses import dataclass
 from pathlib import Path
-from typing import Callable, Mapping, Protocol, Sequence
+from collections.abc import Mapping
+from typing import Callable, Protocol, Sequence
 
 from . import (PCIE_GTPS, DaemonResourceInventory, FabricLinkRecord, GpuInventoryRecord,
                PciePathRecord, TopologyProvider, pcie_gbps)

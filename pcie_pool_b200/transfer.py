@@ -6,7 +6,8 @@ from __future__ import annotations
 import math
 from dataclasses import asdict, dataclass, field
 from enum import Enum
-from typing import Iterable, Mapping
+from collections.abc import Mapping
+from typing import Iterable
 
 from .schema import TransferMode
 

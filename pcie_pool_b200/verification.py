@@ -20,7 +20,8 @@ import os
 import tempfile
 import time
 from dataclasses import asdict, dataclass
-from typing import Mapping, Sequence
+from collections.abc import Mapping
+from typing import Sequence
 
 PATTERN_MUL, PATTERN_ADD = 131, 17
 

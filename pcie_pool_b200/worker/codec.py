@@ -5,7 +5,7 @@ turbobus/worker/codec.py:74-78 so either side can talk to the other."""
 from __future__ import annotations
 
 import json
-from typing import Mapping
+from collections.abc import Mapping
 
 from .helper import WorkerServiceRequestEnvelope, WorkerServiceResponseEnvelope
 

@@ -16,7 +16,8 @@ from __future__ import annotations
 
 from dataclasses import asdict, dataclass, field
 from enum import Enum
-from typing import Any, Iterable, Mapping
+from collections.abc import Mapping
+from typing import Any, Iterable
 
 from ..schema import (BufferRegistration, DaemonResponse, ExecutionTicket, SchedulingDecision,
                       TransferStatusState, WorkerDataPlaneCompletion, WorkerDataPlaneRequest,

@@ -420,3 +420,33 @@ def test_audit_records_have_the_full_field_set():
     for k in ("audit_id", "event_type", "transfer_id", "lease_id", "session_id", "job_id", "relay_gpu",
               "direction", "state", "reason"):
         assert k in rec, k
+
+
+def test_history_is_bounded_and_recent_receipts_stay_available():
+    from pcie_pool_b200.daemon import IntentExecutor
+    from pcie_pool_b200.mock import MockDataPlane, MockWorld
+
+    world = MockWorld(gpu_count=4)
+    d = TurboBusDaemon(relay_gpus=[1, 2, 3], max_inflight_chunks_per_relay=4096,
+                       topology_provider=StaticTopologyProvider(gpu_count=4), executor=IntentExecutor(
+                           MockDataPlane(world)), history_limit=5, audit_limit=8)
+    d.put_profile(0, [1, 2, 3], world.profile(0))
+    c = InProcessDaemonClient(d)
+    sid = d.register_session(0, [1, 2, 3], max_inflight_chunks=4096).payload["session"]["session_id"]
+    assert d.register_job("job", session_id=sid).ok
+    import numpy as np
+
+    src, dst = np.zeros(4 * MiB, np.uint8), world.alloc(0, 4 * MiB)
+    assert d.register_buffer("src-job", "job", "cpu_pinned", 4 * MiB, address=src.ctypes.data, pinned=True).ok
+    assert d.register_buffer("dst-job", "job", "gpu", 4 * MiB, device_index=0, address=dst.ctypes.data).ok
+    from pcie_pool_b200 import TurboBusClient
+
+    client = TurboBusClient(daemon=c)
+    for i in range(20):
+        it = TransferIntent(f"h{i}", "job", sid, "src-job", "dst-job", "h2d", 4 * MiB,
+                            ({"src_offset": 0, "dst_offset": 0, "bytes": 4 * MiB},), metadata={"chunk_bytes": MiB})
+        assert client.transfer(it, timeout_seconds=30).state.value == "complete"
+    desc = d.describe().payload
+    assert len(desc["transfer_queue"]) <= 6 and len(desc["transfer_statuses"]) <= 6
+    assert len(desc["audit_records"]) <= 16, "audit records are trimmed as transfers finish"
+    assert d.wait_transfer_receipt("h19").ok and not d.wait_transfer_receipt("h0").ok
