@@ -39,7 +39,7 @@ from ..schema import (BufferRegistration, CleanupRequest, DaemonRequest, DaemonR
                       ExecutionTicket, JobIdentity, LeaseToken, PeerIdentity, RelayQuota, RequestType,
                       SchedulingDecision, Session, TERMINAL_STATES, TransferIntent, TransferReceipt,
                       TransferReservation, TransferStatus, TransferStatusState,
-                      WorkerTransferAuthorization, WorkerTransferAuthorizationRequest)
+                      WorkerTransferAuthorization, WorkerTransferAuthorizationRequest, byte_ranges)
 from ..topology import TopologyProvider
 from .audit import build_audit_record
 from .wire import reserve_socket
@@ -1978,16 +1978,15 @@ def relay_devices(plan, direction: str) -> set[int]:
 
 
 def ticket_ranges(plan, direction: str) -> tuple[dict[str, int], ...]:
-    out = []
+    chunks = []
     for a, _p in _plan_chunks(plan, kind=None, relays=None, direction=str(direction).lower()):
         for c in a.get("chunks", ()) or ():
             if not isinstance(c, dict):
                 raise ValueError("transfer plan chunk must be an object")
-            out.append({"src_offset": int(c["src_offset"]), "dst_offset": int(c["dst_offset"]),
-                        "bytes": int(c["bytes"])})
-    if not out:
+            chunks.append(c)
+    if not chunks:
         raise ValueError("daemon plan has no authorized chunks")
-    return tuple(out)
+    return byte_ranges(chunks)
 
 
 def decision_direction(decision: SchedulingDecision) -> str:

@@ -187,7 +187,16 @@ def coerce_direction(value: Any, name: str = "direction") -> str:
     return d
 
 
+class ValidatedRanges(tuple):
+    """A tuple of byte ranges that ``byte_ranges`` already checked; passing it
+    to another contract skips the per-range work (tickets carry every chunk)."""
+
+    __slots__ = ()
+
+
 def byte_ranges(value: Any, name: str = "ranges") -> tuple[dict[str, int], ...]:
+    if type(value) is ValidatedRanges:
+        return value
     out = []
     append = out.append
     for item in value:
@@ -199,7 +208,7 @@ def byte_ranges(value: Any, name: str = "ranges") -> tuple[dict[str, int], ...]:
         if n <= 0:
             raise ValueError("range bytes must be positive")
         append({"src_offset": src, "dst_offset": dst, "bytes": n})
-    return tuple(out)
+    return ValidatedRanges(out)
 
 
 FORBIDDEN_POLICY_KEYS = frozenset({
