@@ -343,10 +343,15 @@ class OffloadStore:
         self._settle(b)
 
     def wait_many(self, names: Iterable[str]) -> None:
+        """Wait for the blocks' last transfers (a shared batch handle once) and
+        move each to where its transfer put it; a block that never moved
+        keeps its state, as with :meth:`wait`."""
         done = set()
         for n in names:
             b = self.block(n)
-            if b.last_handle is not None and id(b.last_handle) not in done:
+            if b.last_handle is None:
+                continue
+            if id(b.last_handle) not in done:
                 b.last_handle.wait()
                 done.add(id(b.last_handle))
             self._settle(b)
