@@ -99,3 +99,16 @@ def test_summary_dispatch_over_result_shapes(tmp_path, capsys):
     p.write_text(json.dumps(one_line))
     assert summarize_main([str(p)]) == 0
     assert "value=217.9" in capsys.readouterr().out
+
+
+def test_relay_interference_scenarios_and_args():
+    from pcie_pool_b200.benchmarks import relay_interference as ri
+
+    a = ri.parse_args(["--scenarios", "idle,relays_busy", "--bytes", "1G", "--load-bytes", "256M"])
+    assert a.scenario_list == ["idle", "relays_busy"] and ri.parse_size(a.bytes) == 1 << 30
+    assert ri.loaded_devices("relays_busy", 0, [1, 2]) == [1, 2]
+    assert ri.loaded_devices("target_busy", 0, [1, 2]) == [0]
+    assert ri.loaded_devices("all_busy", 0, [1]) == [0, 1]
+    assert ri.loaded_devices("target_link_busy", 0, [1]) == [] and ri.loaded_devices("idle", 0, [1]) == []
+    with pytest.raises(SystemExit):
+        ri.parse_args(["--scenarios", "idle,volcano"])
