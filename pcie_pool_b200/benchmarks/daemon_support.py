@@ -89,6 +89,9 @@ def receipt_to_trace(receipt: TransferReceipt) -> dict[str, object]:
     trace["path_split"] = dict(split)
     trace["fallback_reason"] = str(receipt.metadata.get("fallback_reason", "") or "")
     trace["measured_cuda_ms"] = cuda_ms
+    timing = receipt.metadata.get("timing") or {}
+    for k in ("queue_ms", "execution_ms", "lease_wait_ms"):  # daemon-side waits (0 when not reported)
+        trace[k] = float(timing.get(k) or 0.0)
     return trace
 
 

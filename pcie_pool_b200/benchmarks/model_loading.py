@@ -91,6 +91,9 @@ def summarize(samples: list[dict], prefix: str = "load") -> dict:
             f"median_{prefix}_ms": statistics.median(s[f"{prefix}_ms"] for s in samples),
             "median_gib_per_second": statistics.median(s[f"{prefix}_gib_per_second"] for s in samples),
             "median_measured_cuda_ms": statistics.median(s.get("measured_cuda_ms", 0.0) for s in samples),
+            "median_queue_ms": statistics.median(float(s["receipt"].get("queue_ms", 0.0)) for s in samples),
+            "median_lease_wait_ms": statistics.median(float(s["receipt"].get("lease_wait_ms", 0.0))
+                                                      for s in samples),
             **{k: int(statistics.median(s[k] for s in samples)) for k in keys},
             "decision_ids": sorted({s["decision_id"] for s in samples}),
             "topology_snapshot_ids": sorted({s["topology_snapshot_id"] for s in samples}),

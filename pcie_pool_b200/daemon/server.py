@@ -1560,6 +1560,7 @@ class TurboBusDaemon:
         if measured:
             md["measured"] = {k: v for k, v in measured.items() if k != "path_stats"}
         done_at = S.completed_at.get(tid) if st.state in TERMINAL_STATES else None
+        md["timing"] = transfer_timing(S.queue_records.get(tid) or {}, done_at)
         started = decision.issued_at
         if done_at is not None and done_at < started:
             done_at = started
@@ -1688,6 +1689,12 @@ class TurboBusDaemon:
         if adm:
             rec["admission_state"] = adm.get("state", rec.get("admission_state"))
             rec["admission_reason"] = adm.get("reason")
+            at0 = float(self._now() if now is None else now)
+            if rec["admission_state"] == DELAYED and rec.get("delayed_at") is None:
+                rec["delayed_at"] = at0
+            elif rec["admission_state"] == ADMITTED and rec.get("delayed_at") is not None \
+                    and rec.get("admitted_at") is None:
+                rec["admitted_at"] = at0
         rec["plan_generation"] = S.generations.get(str(tid), rec.get("plan_generation", 0))
         rec["plan_expires_at"] = S.plan_expiry.get(str(tid), rec.get("plan_expires_at"))
         d = S.decisions.get(str(tid))
@@ -1975,6 +1982,19 @@ def relay_devices(plan, direction: str) -> set[int]:
     return {int(p.get("relay_device", -1))
             for a, p in _plan_chunks(plan, kind="relay", relays=None, direction=str(direction).lower())
             if a.get("chunks")}
+
+
+def transfer_timing(rec: Mapping[str, Any], completed_at: float | None) -> dict[str, Any]:
+    """Daemon-side times of one transfer: when it was queued, started and
+    finished, and the derived queueing, execution, lease-wait (time parked in
+    delayed admission) and total milliseconds."""
+    def ms(a, b):
+        return None if a is None or b is None else round(max(0.0, (float(b) - float(a)) * 1e3), 3)
+
+    q, s, d, adm = rec.get("queued_at"), rec.get("started_at"), rec.get("delayed_at"), rec.get("admitted_at")
+    return {"queued_at": q, "started_at": s, "completed_at": completed_at, "queue_ms": ms(q, s),
+            "execution_ms": ms(s, completed_at), "total_ms": ms(q, completed_at),
+            "lease_wait_ms": ms(d, adm) if d is not None else 0.0}
 
 
 def ticket_ranges(plan, direction: str) -> tuple[dict[str, int], ...]:

@@ -67,6 +67,7 @@ def test_receipt_trace_and_line():
     t = ds.receipt_to_trace(receipt(fallback="fairness fallback"))
     assert (t["direct_bytes"], t["relay_bytes"], t["direct_chunks"], t["relay_chunks"]) == (60, 40, 3, 2)
     assert t["measured_cuda_ms"] == 2.5 and t["state"] == "complete" and t["fallback_reason"] == "fairness fallback"
+    assert t["queue_ms"] == 0.0 and t["lease_wait_ms"] == 0.0
     json.dumps(t)  # JSON ready
     line = ds.receipt_trace_line(receipt(fallback="fairness fallback"))
     assert line.startswith("daemon_receipt intent_id=i decision_id=d topology_snapshot_id=s ticket_id=tk state=")

@@ -450,3 +450,22 @@ def test_history_is_bounded_and_recent_receipts_stay_available():
     assert len(desc["transfer_queue"]) <= 6 and len(desc["transfer_statuses"]) <= 6
     assert len(desc["audit_records"]) <= 16, "audit records are trimmed as transfers finish"
     assert d.wait_transfer_receipt("h19").ok and not d.wait_transfer_receipt("h0").ok
+
+
+def test_receipts_carry_queue_execution_and_lease_wait_times():
+    from pcie_pool_b200.daemon.server import transfer_timing
+
+    clock = Clock()
+    d = daemon(clock)
+    sid = setup_job(d)
+    r = d.submit_transfer_intent(_intent(sid, "t1"))
+    assert r.ok
+    tid = r.payload["transfer_id"]
+    clock.t += 0.25
+    d.executor_started(tid)
+    clock.t += 0.5
+    d.executor_finished(tid, ok_=True, bytes_completed=32 * MiB)
+    t = d.wait_transfer_receipt("t1").payload["receipt"]["metadata"]["timing"]
+    assert (t["queue_ms"], t["execution_ms"], t["total_ms"], t["lease_wait_ms"]) == (250.0, 500.0, 750.0, 0.0)
+    parked = transfer_timing({"queued_at": 1.0, "delayed_at": 1.0, "admitted_at": 1.2, "started_at": 1.3}, 1.5)
+    assert parked["lease_wait_ms"] == 200.0 and parked["total_ms"] == 500.0
