@@ -415,3 +415,21 @@ def test_vllm_probe_observers_wrap_and_restore_vllm_methods():
         P.remove_observers(saved)
     assert (gm.GPUModelRunner.initialize_kv_cache, km.KVCacheManager.allocate_slots,
             km.KVCacheManager.get_computed_blocks) == before
+
+
+def test_checksum_at_offsets_compose_and_unit_addresses():
+    import numpy as np
+    import torch
+
+    from pcie_pool_b200.ops import unit_addresses
+    from pcie_pool_b200.utils.checksum import checksum_at, checksum_bytes, combine
+
+    data = np.random.default_rng(4).integers(0, 256, 4096 + 12, dtype=np.uint8)
+    whole = checksum_bytes(data)
+    parts = [checksum_at(data[a:b], a) for a, b in ((0, 1024), (1024, 3000), (3000, data.size))]
+    assert combine(np.array(parts, dtype=np.uint64)) == whole
+    with pytest.raises(ValueError, match="multiple of 4"):
+        checksum_at(data[:8], 2)
+    base = torch.zeros(64, dtype=torch.uint8)
+    addrs = unit_addresses(base, 16, [3, 0, 2])
+    assert addrs.tolist() == [base.data_ptr() + 48, base.data_ptr(), base.data_ptr() + 32]
