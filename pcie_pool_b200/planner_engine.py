@@ -117,12 +117,10 @@ class PlannerEngine:
         cands = [self._aligned_chunk(c) for c in candidates if max_chunk is None or c <= max_chunk]
         if not cands:
             raise ValueError("no chunk-size candidate fits")
-        try:
-            from ._native import native
-
-            return int(native(build_if_missing=False).choose_chunk_bytes(int(total_bytes), cands, bw, lat))
-        except Exception:
-            return min(cands, key=lambda c: _estimate(int(total_bytes), c, bw, lat))
+        C = _native_planner()
+        if C is not None:
+            return int(C.choose_chunk_bytes(int(total_bytes), cands, bw, lat))
+        return min(cands, key=lambda c: _estimate(int(total_bytes), c, bw, lat))
 
     def build_paths(self, profile, mode: TransferMode | str, direction: str) -> list[PlannerPath]:
         mode = TransferMode(mode)
@@ -222,16 +220,27 @@ class PlannerEngine:
             lat: list[float] = []
         else:
             bw, lat = self._lane_model(paths)
-        try:
-            import numpy as np
-
-            from ._native import native
-
-            C = native(build_if_missing=False)
-            pol = C.POLICY_LEGACY if policy == "legacy" else C.POLICY_EARLIEST_FINISH
-            return [int(i) for i in C.assign_chunks(np.asarray(sizes, dtype=np.uint64), bw, lat, pol)]
-        except Exception:
+        C = _native_planner()
+        if C is None:
             return assign_python(sizes, bw, lat, policy)
+        import numpy as np
+
+        pol = C.POLICY_LEGACY if policy == "legacy" else C.POLICY_EARLIEST_FINISH
+        return [int(i) for i in C.assign_chunks(np.asarray(sizes, dtype=np.uint64), bw, lat, pol)]
+
+
+def _native_planner():
+    """The native planner (C++), or None when the extension is not built --
+    a host-side computation whose Python twin (``assign_python`` /
+    ``_estimate``) gives the same assignment, so planning also works on
+    machines that never built the CUDA extension.  Errors inside a native
+    call are not caught."""
+    from ._native import native
+
+    try:
+        return native(build_if_missing=False)
+    except RuntimeError:
+        return None
 
 
 def assign_python(sizes: Sequence[int], bw: Sequence[float], lat: Sequence[float],

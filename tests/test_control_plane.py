@@ -345,3 +345,27 @@ def test_reserve_socket_refuses_a_live_socket_and_reclaims_a_stale_one(tmp_path)
     assert os.path.exists(path)  # closed listener leaves a stale file behind
     again = reserve_socket(path)
     again.close()
+
+
+def test_native_and_python_planners_agree():
+    """The C++ planner and its Python twin give the same chunk assignment and
+    the same chunk-size choice on random lane models."""
+    import numpy as np
+
+    from pcie_pool_b200._native import native
+    from pcie_pool_b200.planner_engine import _estimate, assign_python
+
+    C = native()
+    rng = np.random.default_rng(11)
+    for _ in range(40):
+        lanes = int(rng.integers(1, 9))
+        sizes = [int(x) for x in rng.choice([MiB, 4 * MiB, 16 * MiB], size=int(rng.integers(1, 200)))]
+        bw = [float(x) for x in rng.uniform(5.0, 60.0, lanes)]
+        lat = [float(x) for x in rng.uniform(0.0, 3e-5, lanes)]
+        for policy, pol in (("legacy", C.POLICY_LEGACY), ("earliest_finish", C.POLICY_EARLIEST_FINISH)):
+            lat_p = [] if policy == "legacy" else lat
+            native_idx = [int(i) for i in C.assign_chunks(np.asarray(sizes, dtype=np.uint64), bw, lat_p, pol)]
+            assert native_idx == assign_python(sizes, bw, lat_p, policy), policy
+        cands = [MiB, 4 * MiB, 16 * MiB, 64 * MiB]
+        total = int(rng.integers(1, 64)) * 16 * MiB
+        assert int(C.choose_chunk_bytes(total, cands, bw, lat)) == min(cands, key=lambda c: _estimate(total, c, bw, lat))
