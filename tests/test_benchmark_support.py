@@ -113,3 +113,16 @@ def test_relay_interference_scenarios_and_args():
     assert ri.loaded_devices("target_link_busy", 0, [1]) == [] and ri.loaded_devices("idle", 0, [1]) == []
     with pytest.raises(SystemExit):
         ri.parse_args(["--scenarios", "idle,volcano"])
+
+
+def test_op_kernel_benchmark_traffic_model_and_args():
+    from pcie_pool_b200.benchmarks import op_kernels as ok
+
+    assert ok.traffic_bytes("gather", 1 << 20) == 2 << 20
+    assert ok.traffic_bytes("checksum", 1 << 20) == 1 << 20
+    assert ok.traffic_bytes("adamw", 4 * 1000) == 1000 * 28, "fp32 master/m/v and bf16 grad in, all four out"
+    n = 2 * 128 * 128 * 4  # 4 blocks of bf16
+    assert ok.traffic_bytes("fp8", n) == n + n // 2 + 4 * 4
+    assert ok.parse_args(["--kernels", "adamw,fp8"]).kernel_list == ["adamw", "fp8"]
+    with pytest.raises(SystemExit):
+        ok.parse_args(["--kernels", "warp-drive"])
