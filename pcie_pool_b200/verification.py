@@ -302,10 +302,11 @@ def main(argv: Sequence[str] | None = None) -> int:
     return 0
 
 
-if __name__ == "__main__":
-    raise SystemExit(main())
-
-
 __all__ = ["WorkerManagedD2HRelayVerificationResult", "WorkerManagedH2DRelayVerificationResult",
            "WorkerManagedRelayVerificationResult", "build_verification_daemon", "main", "make_pattern", "verify",
            "verify_worker_managed_d2h_relay", "verify_worker_managed_h2d_relay"]
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
+
