@@ -1,0 +1,107 @@
+"""Control-plane cost of one intent, without a data plane.
+
+    python -m pcie_pool_b200.benchmarks.control_plane --lanes 8 --bytes 4G --chunk 16M --intents 200
+
+Runs ``TurboBusClient.transfer`` against an in-process daemon whose
+executor drives a stand-in engine that completes instantly, so the time per
+intent is the daemon's own work: planning on the profile, leases, ticket,
+dispatch to the executor thread, completion and the receipt.  The timing is
+repeated after ``--history`` earlier intents to show that the per-intent
+cost does not grow with the daemon's history.  Prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+import time
+
+UNITS = {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30}
+
+
+def parse_size(s: str) -> int:
+    s = str(s).strip().upper()
+    return int(float(s[:-1]) * UNITS[s[-1]]) if s and s[-1] in UNITS else int(s)
+
+
+class InstantEngine:
+    """Stand-in for ``PoolEngine``: every transfer completes at once with
+    per-lane statistics shaped like the real ones."""
+
+    def run(self, direction, target, host_ptr, host_bytes, dev_ptr, dev_bytes, lanes, checksum=False, **kw):
+        import numpy as np
+
+        from ..parallel.engine import LaneResult, TransferResult
+
+        stats = [LaneResult(device=l.device, direct=l.device == target, bytes=int(l.bytes.sum()),
+                            chunks=int(l.bytes.size), cuda_ms=1.0) for l in lanes]
+        nch = sum(s.chunks for s in stats)
+        return TransferResult(id=1, ok=True, status_code=0, error="", bytes=sum(s.bytes for s in stats),
+                              cuda_ms=1.0, submit_to_complete_ms=1.0, gib_per_s=1.0, lanes=stats,
+                              checksums=np.zeros((nch, 2), dtype=np.uint64))
+
+
+def build(lanes: int, nbytes: int, history_limit: int = 10000):
+    from .. import TurboBusClient
+    from ..e2e import build_inprocess_node
+
+    prof = {"target_device": 0, "direct_h2d_bw_gbps": 34.0, "direct_d2h_bw_gbps": 34.0,
+            "relays": [{"relay_device": r, "target_device": 0, "h2d_bw_gbps": 26.0, "d2h_bw_gbps": 26.0,
+                        "p2p_bw_gbps": 700.0, "effective_bw_gbps": 26.0, "effective_d2h_bw_gbps": 26.0,
+                        "p2p_enabled": True} for r in range(1, lanes)]}
+    daemon, dc = build_inprocess_node(InstantEngine(), list(range(lanes)), 0, prof if lanes > 1 else None)
+    daemon._history_limit = max(1, int(history_limit))
+    sid = dc.register_session(0, list(range(1, lanes)), max_inflight_chunks=1 << 16).payload["session"]["session_id"]
+    dc.register_job("cp", session_id=sid)
+    dc.register_buffer("h", "cp", "cpu_pinned", nbytes, address=4096, pinned=True)
+    dc.register_buffer("g", "cp", "gpu", nbytes, device_index=0, address=8192)
+    return daemon, TurboBusClient(daemon=dc), sid
+
+
+def main(argv=None) -> int:
+    from .. import TransferIntent
+
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--lanes", type=int, default=8)
+    p.add_argument("--bytes", default="4G")
+    p.add_argument("--chunk", default="16M")
+    p.add_argument("--intents", type=int, default=200)
+    p.add_argument("--history", type=int, default=2000, help="intents run before the second timing")
+    a = p.parse_args(argv)
+    n, chunk = parse_size(a.bytes), parse_size(a.chunk)
+    daemon, client, sid = build(a.lanes, n)
+    counter = iter(range(1 << 40))
+
+    def step():
+        it = TransferIntent(f"cp-{next(counter)}", "cp", sid, "h", "g", "h2d", n,
+                            ({"src_offset": 0, "dst_offset": 0, "bytes": n},), workload_kind="model_weights",
+                            metadata={"chunk_bytes": chunk})
+        r = client.transfer(it, timeout_seconds=60)
+        if r.state.value != "complete":
+            raise RuntimeError(r.error)
+
+    def timed(k):
+        out = []
+        for _ in range(5):
+            t0 = time.perf_counter()
+            for _ in range(max(1, k // 5)):
+                step()
+            out.append((time.perf_counter() - t0) * 1e3 / max(1, k // 5))
+        return statistics.median(out)
+
+    for _ in range(10):
+        step()
+    first = timed(a.intents)
+    for _ in range(a.history):
+        step()
+    later = timed(a.intents)
+    print(json.dumps({"metric": "control-plane ms per intent (instant data plane)", "lanes": a.lanes, "bytes": n,
+                      "chunk_bytes": chunk, "chunks": -(-n // chunk), "ms_per_intent": round(first, 3),
+                      "ms_per_intent_after_history": round(later, 3), "history": a.history,
+                      "retained_transfers": len(daemon.describe().payload["transfer_queue"])}), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -126,3 +126,11 @@ def test_op_kernel_benchmark_traffic_model_and_args():
     assert ok.parse_args(["--kernels", "adamw,fp8"]).kernel_list == ["adamw", "fp8"]
     with pytest.raises(SystemExit):
         ok.parse_args(["--kernels", "warp-drive"])
+
+
+def test_control_plane_benchmark_runs_on_cpu(capsys):
+    from pcie_pool_b200.benchmarks import control_plane as cp
+
+    assert cp.main(["--lanes", "3", "--bytes", "64M", "--chunk", "4M", "--intents", "10", "--history", "15"]) == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert out["chunks"] == 16 and out["ms_per_intent"] > 0 and out["retained_transfers"] >= 35
