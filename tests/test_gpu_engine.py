@@ -52,6 +52,7 @@ def test_direct_h2d_copy_exact(need_gpu, checksum):
     dev = torch.zeros(n, dtype=torch.uint8, device="cuda:0")
     eng = _engine([0])
     lanes = split_even(n, 1 << 20, [0])
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r = eng.run(H2D, 0, host.ptr, n, dev.data_ptr(), n, lanes, checksum=checksum)
     assert r.ok, r.error
     assert torch.equal(dev.cpu(), torch.from_numpy(host.numpy().copy()))
@@ -70,6 +71,7 @@ def test_staged_h2d_ragged_exact(need_gpu, total):
     lanes = split_even(total, 1 << 20, [0])
     for _ in range(3):  # ring reuse across transfers
         dev.zero_()
+        torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
         r = eng.run(H2D, 0, host.ptr, total, dev.data_ptr(), total, lanes, checksum=True,
                     stage_direct=True)
         assert r.ok, r.error
@@ -85,6 +87,7 @@ def test_misaligned_destination(need_gpu):
     dev = torch.zeros(total + 64, dtype=torch.uint8, device="cuda:0")
     eng = _engine([0])
     lane = make_lane(0, [(0, 3, 100000), (100000, 100003, 100000)])
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r = eng.run(H2D, 0, host.ptr, total, dev.data_ptr(), total + 64, [lane], checksum=True,
                 stage_direct=True)
     assert r.ok, r.error
@@ -102,6 +105,7 @@ def test_d2h_copy_exact(need_gpu, stage):
     src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda:0")
     eng = _engine([0])
     lanes = split_even(n, 1 << 20, [0])
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r = eng.run(D2H, 0, host.ptr, n, src.data_ptr(), n, lanes, checksum=True, stage_direct=stage)
     assert r.ok, r.error
     ref = src.cpu().numpy()
@@ -130,6 +134,7 @@ def test_scatter_units_paged_kv(need_gpu):
     lane = Lane(0, (starts * unit).astype(np.uint64), np.zeros(starts.size, np.uint64),
                 np.full(starts.size, per_chunk * unit, np.uint64), unit0=starts.astype(np.uint32))
     eng = _engine([0])
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r = eng.run(H2D, 0, host.ptr, n, kv.data_ptr(), n, [lane], op=C.OP_SCATTER_UNITS,
                 checksum=True, unit_bytes=unit, unit_addrs=addrs)
     assert r.ok, r.error
@@ -154,6 +159,7 @@ def test_gather_units_paged_kv(need_gpu):
     lane = Lane(0, np.zeros(starts.size, np.uint64), (starts * unit).astype(np.uint64),
                 np.full(starts.size, per_chunk * unit, np.uint64), unit0=starts.astype(np.uint32))
     eng = _engine([0])
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r = eng.run(D2H, 0, host.ptr, n, kv.data_ptr(), n, [lane], op=C.OP_GATHER_UNITS,
                 checksum=True, unit_bytes=unit, unit_addrs=addrs)
     assert r.ok, r.error
@@ -180,6 +186,7 @@ def test_fp8_landing_bit_exact(need_gpu):
     lane = Lane(0, (r0.astype(np.uint64) * row_bytes), np.zeros(3, np.uint64),
                 (nrows * row_bytes).astype(np.uint64), unit0=r0, tensor=np.zeros(3, np.uint32))
     eng = _engine([0])
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r = eng.run(H2D, 0, host.ptr, raw.size, q.data_ptr(), q.numel(), [lane], op=C.OP_FP8_QUANT,
                 checksum=True, tensors=[(q.data_ptr(), scales.data_ptr(), rows, cols)])
     assert r.ok, r.error
@@ -217,6 +224,7 @@ def test_ranges_unpack_and_pack(need_gpu):
     lane = Lane(0, np.array(src_off, np.uint64), np.zeros(2, np.uint64), np.array(cbytes, np.uint64),
                 unit0=np.array([0, 25], np.uint32), count=np.array([25, 15], np.uint32))
     eng = _engine([0])
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r = eng.run(H2D, 0, host.ptr, total, dst.data_ptr(), dst.numel(), [lane], op=C.OP_SCATTER_RANGES,
                 checksum=True, ranges=(addrs, sizes, pos))
     assert r.ok, r.error
@@ -231,6 +239,7 @@ def test_ranges_unpack_and_pack(need_gpu):
     back = _host(total, seed=11)
     lane2 = Lane(0, np.zeros(2, np.uint64), np.array(src_off, np.uint64), np.array(cbytes, np.uint64),
                  unit0=np.array([0, 25], np.uint32), count=np.array([25, 15], np.uint32))
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r2 = eng.run(D2H, 0, back.ptr, total, dst.data_ptr(), dst.numel(), [lane2], op=C.OP_GATHER_RANGES,
                  checksum=True, ranges=(addrs, sizes, pos))
     assert r2.ok, r2.error
@@ -247,10 +256,12 @@ def test_lane_timeout_reports_status_and_recovers(need_gpu):
     dev = torch.zeros(n, dtype=torch.uint8, device="cuda:0")
     eng = _engine([0], timeout_s=0.5)
     lanes = split_even(n, 1 << 20, [0])
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r = eng.run(H2D, 0, host.ptr, n, dev.data_ptr(), n, lanes, stage_direct=True,
                 debug_drop_publish=0)
     assert not r.ok
     assert r.status_code == 1
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r2 = eng.run(H2D, 0, host.ptr, n, dev.data_ptr(), n, lanes, stage_direct=True, checksum=True)
     assert r2.ok, r2.error
     assert torch.equal(dev.cpu(), torch.from_numpy(host.numpy().copy()))
@@ -269,11 +280,13 @@ def test_relay_h2d_and_d2h_exact(need_two_gpus):
     dev = torch.zeros(n, dtype=torch.uint8, device="cuda:0")
     eng = _engine(devs)
     lanes = split_even(n, 1 << 20, devs)
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r = eng.run(H2D, 0, host.ptr, n, dev.data_ptr(), n, lanes, checksum=True)
     assert r.ok, r.error
     assert torch.equal(dev.cpu(), torch.from_numpy(host.numpy().copy()))
     assert np.array_equal(r.checksums, _chunk_sums(host.numpy(), lanes))
     back = _host(n, seed=14)
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r2 = eng.run(D2H, 0, back.ptr, n, dev.data_ptr(), n, lanes, checksum=True)
     assert r2.ok, r2.error
     assert np.array_equal(back.numpy(), host.numpy())
@@ -295,6 +308,7 @@ def test_relay_scatter_units(need_two_gpus):
         lanes.append(Lane(dev, (sel * unit).astype(np.uint64), np.zeros(sel.size, np.uint64),
                           np.full(sel.size, 8 * unit, np.uint64), unit0=sel.astype(np.uint32)))
     eng = _engine([0, 1])
+    torch.cuda.synchronize()  # torch's stream and the engine's streams are not ordered
     r = eng.run(H2D, 0, host.ptr, n, kv.data_ptr(), n, lanes, op=C.OP_SCATTER_UNITS,
                 checksum=True, unit_bytes=unit, unit_addrs=addrs)
     assert r.ok, r.error
