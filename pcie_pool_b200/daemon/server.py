@@ -784,7 +784,7 @@ class TurboBusDaemon:
         S.plans[tid] = dict(decision.plan)
         S.decisions[tid] = decision
         S.plan_expiry[tid] = self._plan_expiry(decision, at)
-        adm = self._admission(decision, session, True, at)
+        adm = self._admission(decision, session, True, at, exclude=tid)
         reservations = []
         if adm["state"] == ADMITTED:
             reservations = self._commit_leases(session, decision, tid, bids)
@@ -1234,13 +1234,14 @@ class TurboBusDaemon:
                 filtered.append({"relay_gpu": g, "reason": "relay not configured"})
         return {**e, "eligible_relays": good, "filtered_relays": filtered}
 
-    def _admission(self, decision, session: Session, allow_delayed: bool, now: float) -> dict[str, Any]:
+    def _admission(self, decision, session: Session, allow_delayed: bool, now: float,
+                   exclude: str | None = None) -> dict[str, Any]:
         leases = scheduling_decision_leases(decision)
         if not leases:
             return {"state": ADMITTED, "reason": "direct_or_fallback_plan", "requested_lease_count": 0,
                     "requested_chunks": 0, "lease_ids": (), "admitted_at": float(now)}
         chunks = sum(l.chunk_limit for l in leases)
-        why = self._admission_block(session, leases)
+        why = self._admission_block(session, leases, exclude)
         if why is None:
             return {"state": ADMITTED, "reason": "relay_resources_available",
                     "requested_lease_count": len(leases), "requested_chunks": chunks, "lease_ids": (),
@@ -1251,10 +1252,13 @@ class TurboBusDaemon:
         return {"state": ADMITTED, "reason": "scheduler_fallback_or_rejection", "requested_lease_count": 0,
                 "requested_chunks": 0, "lease_ids": (), "admitted_at": float(now)}
 
-    def _admission_block(self, session: Session, leases) -> str | None:
+    def _admission_block(self, session: Session, leases, exclude: str | None = None) -> str | None:
         if session.active_chunks + sum(l.chunk_limit for l in leases) > session.max_inflight_chunks:
             return "session relay admission is delayed by chunk quota"
-        busy = busy_relays(self._runtime_state(active_only=True))
+        state = self._runtime_state(active_only=True)
+        if exclude is not None:  # a transfer being re-planned does not wait on its own old paths
+            state = state_without_transfer(state, str(exclude))
+        busy = busy_relays(state)
         for l in leases:
             if l.relay_device not in session.relay_gpus:
                 return "relay admission is delayed by session relay ownership"
