@@ -149,10 +149,10 @@ def make_vllm_block_refs_from_ids(request_id: str, group_id: int, block_ids: Ite
 
 
 def block_bytes_from_vllm_kv_tensor(tensor) -> int:
-    """Bytes of one KV block in a tensor shaped [*, blocks, ...]."""
-    if len(tensor.shape) < 2:
-        raise ValueError("vLLM KV tensor must have at least two dimensions")
-    return int(tensor.stride(1) * tensor.element_size())
+    """Bytes of one addressable KV unit: one block of one K/V plane for
+    ``[2, blocks, ...]`` tensors (``stride(1)``, as turbobus/adapters/vllm.py:
+    206-211 computes it), the whole block for ``[blocks, ...]`` layouts."""
+    return kv_layout(tensor).unit_bytes
 
 
 def make_vllm_layer_groups_from_kv_caches(cpu_backings: Iterable, kv_caches: Iterable, *,
@@ -182,22 +182,20 @@ def contiguous_runs(block_ids: list[int]) -> list[tuple[int, list[int]]]:
 
 def make_vllm_layer_range_refs_from_ids(request_id: str, block_ids: Iterable[int], kv_caches: Iterable,
                                         cpu_slot_start: int = 0) -> list[VllmKVBlockRef]:
-    """Byte-range refs for tensors shaped [kv, blocks, ...]: one ref per
-    lane per contiguous run of block ids."""
+    """Byte-range refs: one ref per K/V lane (``[2, blocks, ...]``) or per
+    block (``[blocks, ...]``) for each contiguous run of block ids, in the
+    CPU backing order ``[lane][index]``."""
     ids = [int(b) for b in block_ids]
     refs = []
     for layer, kv in enumerate(kv_caches):
-        lanes = int(kv.shape[0]) if len(kv.shape) >= 3 else 1
-        bb = block_bytes_from_vllm_kv_tensor(kv)
-        for lane in range(lanes):
+        lay = kv_layout(kv)
+        bb = lay.unit_bytes
+        for lane in range(lay.lanes):
             for start, run in contiguous_runs(ids):
                 slot = cpu_slot_start + lane * len(ids) + start
-                if lanes == 1:
-                    goff, lane_id = run[0] * bb, None
-                else:
-                    goff, lane_id = int((lane * kv.stride(0) + run[0] * kv.stride(1)) * kv.element_size()), lane
-                refs.append(VllmKVBlockRef(request_id, layer, run[0], slot, run[0], lane_id, slot * bb, goff,
-                                           len(run) * bb))
+                goff = lane * lay.lane_stride + run[0] * lay.block_stride
+                refs.append(VllmKVBlockRef(request_id, layer, run[0], slot, run[0],
+                                           None if lay.lanes == 1 else lane, slot * bb, int(goff), len(run) * bb))
     return refs
 
 
