@@ -210,3 +210,68 @@ def test_bucket_helpers():
     with pytest.raises(ValueError, match="bucket_bytes"):
         s.add_packed_buckets("q", Tensor(1), Tensor(1), bucket_bytes=0, bucket_count=1)
     assert [i.name for i in s.bucket_infos()] == ["p0", "p1", "p2", "p3"]
+
+
+# ---- further rules: empty batches, waits before any transfer, handle summaries ---------------------------
+
+def test_an_empty_batch_submits_nothing_and_waits_for_nothing():
+    c = Client()
+    s = store(c)
+    batch = s.submit_prefetch_many([])
+    assert batch.names == () and batch.handles == () and c.intents == []
+    batch.wait()
+    assert batch.transfer_stats().bytes == 0 and batch.as_dict()["blocks"] == []
+    assert s.prefetch_many([]) == [] and s.evict_many([]) == []
+
+
+def test_waiting_before_any_transfer_is_a_no_op():
+    c = Client()
+    s = store(c)
+    s.wait("b0")
+    s.wait_many(["b1", "b2"])
+    assert c.waits == [] and s.transfer_stats("b0") is None
+    assert s.block_info("b0").state == s.block("b0").state
+
+
+def test_packed_evict_reverses_each_range_and_keeps_block_order():
+    c = Client()
+    s = store(c)
+    s.evict_many(["b3", "b1"])
+    (it,) = c.intents
+    assert it.direction == "d2h" and it.source_buffer_id == "gpu" and it.destination_buffer_id == "cpu"
+    assert [(r["src_offset"], r["dst_offset"]) for r in it.ranges] == [(0, 3 * 2048), (2 * 2048, 2048)]
+    assert it.metadata["block_names"] == ["b3", "b1"] and it.metadata["operation"] == "evict"
+
+
+def test_blocks_carry_connector_fields_into_their_infos():
+    s = OffloadStore(Client(), ctx())
+    cpu, gpu = Tensor(4096), Tensor(4096)
+    s.add("kv", cpu, gpu, block_id=("req", 0, 7), cpu_slot=3, gpu_slot=7, cpu_offset=1024, gpu_offset=2048,
+          byte_count=512)
+    info = s.block_info("kv").as_dict()
+    assert (info["block_id"], info["cpu_slot"], info["gpu_slot"]) == (("req", 0, 7), 3, 7)
+    assert [i.name for i in s.block_infos(["kv"])] == ["kv"] and s.block_ids() == [("req", 0, 7)]
+    for bad in ({"cpu_offset": -1}, {"gpu_offset": -8}, {"byte_count": 0}):
+        with pytest.raises(ValueError):
+            s.add("other", cpu, gpu, **bad)
+    with pytest.raises(ValueError, match="already exists"):
+        s.add("kv", cpu, gpu)
+    with pytest.raises(ValueError, match="non-empty"):
+        s.add("", cpu, gpu)
+
+
+def test_handle_summaries_count_a_shared_handle_once_and_accept_dict_stats():
+    from types import SimpleNamespace
+
+    from pcie_pool_b200.offload_store import summarize_transfer_handles, transfer_stats_from_receipt
+
+    c = Client()
+    s = store(c)
+    batch = s.submit_prefetch_many(["b0", "b1", "b2"])
+    assert len({id(h) for h in batch.handles}) == 1
+    one = summarize_transfer_handles(batch.handles)
+    assert one == transfer_stats_from_receipt(batch.handles[0].receipt)
+    d = SimpleNamespace(stats={"bytes": 10, "direct_chunks": 1, "relay_chunks": 2})
+    both = summarize_transfer_handles([*batch.handles, d, object()])
+    assert (both.bytes, both.direct_chunks, both.relay_chunks) == (one.bytes + 10, one.direct_chunks + 1,
+                                                                   one.relay_chunks + 2)
