@@ -443,9 +443,11 @@ def _first_float(row: Mapping[str, object], keys) -> float | None:
 
 
 def _root_complex(bus_id: str | None) -> str | None:
+    """``domain:bus`` of a bus id, in the sysfs spelling (4-digit lower-case
+    domain) so it groups with root complexes read from sysfs."""
     if not bus_id:
         return None
-    parts = str(bus_id).split(":")
+    parts = _norm_bdf(bus_id).split(":")
     return ":".join(parts[:2]) if len(parts) >= 2 else str(bus_id)
 
 

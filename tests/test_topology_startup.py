@@ -118,3 +118,116 @@ def test_create_production_daemon_with_a_fake_provider_and_executor():
     static = StaticTopologyProvider(gpu_count=2)
     with pytest.raises(DaemonStartupError, match="synthetic"):
         create_production_daemon(DaemonStartupConfig(), topology_provider=static)
+
+
+# ---- the CUDA/NVML provider: versions, cache, sysfs, explicit gaps -----------------------------------------
+
+class Clock:
+    def __init__(self, t=100.0):
+        self.t = t
+
+    def __call__(self):
+        return self.t
+
+
+class CountingProbe(Probe):
+    def __init__(self, *a, **kw):
+        super().__init__(*a, **kw)
+        self.queries = 0
+
+    def query_gpu_inventory(self):
+        self.queries += 1
+        return super().query_gpu_inventory()
+
+
+def test_provider_builds_versioned_snapshots_and_caches_them():
+    clock = Clock()
+    probe = CountingProbe(rows(4), ANSI_TOPO)
+    prov = CudaNvmlTopologyProvider(probe, cache_max_age_seconds=30.0, now=clock, sysfs_root=None)
+    a = prov.snapshot()
+    assert (a.version, a.source, a.discovered_at) == (1, "cuda_nvml", 100.0)
+    assert a.topology_snapshot_id() == "topology-cuda_nvml-v1-100.000000"
+    snap = a.to_topology_snapshot()
+    assert snap.snapshot_id == a.topology_snapshot_id() and len(snap.devices) == 4
+    clock.t = 120.0
+    assert prov.snapshot() is a and probe.queries == 1, "inside the cache age the snapshot is reused"
+    clock.t = 131.0
+    b = prov.snapshot()
+    assert b.version == 2 and probe.queries == 2
+    prov.invalidate()
+    c = prov.snapshot()
+    assert c.version == 3 and probe.queries == 3 and c.topology_snapshot_id() != b.topology_snapshot_id()
+    uncached = CudaNvmlTopologyProvider(CountingProbe(rows(2), ANSI_TOPO), cache_max_age_seconds=0.0,
+                                        now=clock, sysfs_root=None)
+    assert uncached.snapshot().version == 1 and uncached.snapshot().version == 2
+
+
+def test_missing_pcie_capabilities_stay_explicit():
+    bare = [{"device_id": 0, "pci_bus_id": "00000000:1B:00.0"}, {"device_id": 1}]
+    inv = CudaNvmlTopologyProvider(Probe(bare, ANSI_TOPO[:3]), sysfs_root=None).snapshot()
+    p0, p1 = inv.pcie_paths
+    assert (p0.link_generation, p0.link_width, p0.bandwidth_source) == (None, None, None)
+    assert p0.bandwidth_gbps == 0.0 and p0.root_complex == "0000:1b" and p1.root_complex is None
+    given = [{"device_id": 0, "pcie_link_gen_current": 5, "pcie_link_width_current": 16,
+              "pcie_bandwidth_gbps": 55.0}]
+    (p,) = CudaNvmlTopologyProvider(Probe(given, []), sysfs_root=None).snapshot().pcie_paths
+    assert (p.bandwidth_gbps, p.bandwidth_source, p.negotiated_speed_gtps) == (55.0, "provider", 32.0)
+    (e,) = CudaNvmlTopologyProvider(Probe(given[:1] and [{k: v for k, v in given[0].items()
+                                                          if k != "pcie_bandwidth_gbps"}], []),
+                                    sysfs_root=None).snapshot().pcie_paths
+    assert e.bandwidth_source == "estimated_from_pcie_generation_width" and 60.0 < e.bandwidth_gbps < 64.0
+
+
+def test_sysfs_fills_numa_link_and_switch_chain(tmp_path):
+    from pcie_pool_b200.topology.cuda_nvml import pcie_tree
+
+    chain = tmp_path / "devices" / "pci0000:15" / "0000:15:01.0" / "0000:16:00.0" / "0000:17:00.0"
+    dev = chain / "0000:1b:00.0"
+    dev.mkdir(parents=True)
+    (dev / "numa_node").write_text("1\n")
+    (dev / "current_link_speed").write_text("32.0 GT/s PCIe\n")
+    (dev / "current_link_width").write_text("16\n")
+    link = tmp_path / "bus" / "pci" / "devices"
+    link.mkdir(parents=True)
+    (link / "0000:1b:00.0").symlink_to(dev)
+    t = pcie_tree("00000000:1B:00.0", tmp_path)
+    assert t["numa_node"] == 1 and t["negotiated_speed_gtps"] == 32.0 and t["link_width"] == 16
+    assert t["switch_hierarchy"] == ("0000:15:01.0", "0000:16:00.0", "0000:17:00.0")
+    assert t["root_complex"] == "0000:15"
+    (p,) = CudaNvmlTopologyProvider(Probe([{"device_id": 0, "pci_bus_id": "00000000:1B:00.0"}], []),
+                                    sysfs_root=str(tmp_path)).snapshot().pcie_paths
+    assert (p.link_generation, p.link_width, p.numa_node) == (5, 16, 1)
+    assert p.switch_hierarchy == ("0000:15:01.0", "0000:16:00.0", "0000:17:00.0")
+    assert pcie_tree("0000:99:00.0", tmp_path) == {}
+
+
+def test_fabric_links_are_normalised_per_pair():
+    links = fabric_links_from_matrix({0, 1, 2, 3}, ANSI_TOPO)
+    pairs = {(l.src_device_id, l.dst_device_id) for l in links}
+    assert pairs == {(0, 1), (0, 2), (1, 2)}, "one record per unordered pair, SYS pairs dropped"
+    assert all(l.enabled and l.fabric == "nvlink" and l.link_count == 18 for l in links)
+    pix = fabric_links_from_matrix({0, 1}, ["\tGPU0\tGPU1", "GPU0\t X \tPIX", "GPU1\tPIX\t X "])
+    assert len(pix) == 1 and pix[0].fabric != "nvlink"
+    assert fabric_links_from_matrix({0, 1}, []) == ()
+
+
+def test_startup_reports_why_relays_were_filtered():
+    inv = CudaNvmlTopologyProvider(Probe(rows(4), ANSI_TOPO), sysfs_root=None).snapshot()
+    with pytest.raises(DaemonStartupError) as e:
+        relay_candidates_for_policy(inv, DaemonStartupConfig(target_gpu=0, min_relay_count=3))
+    msg = str(e.value)
+    assert "eligible_relays=[1, 2]" in msg and "3:missing enabled fabric link" in msg
+
+
+def test_daemon_cli_builds_the_startup_config():
+    from pcie_pool_b200.daemon.__main__ import build_parser, startup_config_from_args
+
+    a = build_parser().parse_args(["--target-gpu", "2", "--min-relays", "3", "--allow-missing-fabric",
+                                   "--topology-provider", "cuda_nvml", "--max-inflight-chunks-per-relay", "64",
+                                   "--execute", "--profile-store", "/tmp/p.json"])
+    c = startup_config_from_args(a)
+    assert (c.topology_provider, c.target_gpu, c.min_relay_count, c.require_fabric, c.require_pcie) == \
+        ("cuda-nvml", 2, 3, False, True)
+    assert (c.max_inflight_chunks_per_relay, c.execute, c.profile_store_path) == (64, True, "/tmp/p.json")
+    with pytest.raises(SystemExit):
+        build_parser().parse_args([])
