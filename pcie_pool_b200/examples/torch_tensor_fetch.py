@@ -44,10 +44,16 @@ def self_contained(nbytes: int) -> str:
                         ({"src_offset": 0, "dst_offset": 0, "bytes": nbytes},))
     r = TurboBusClient(daemon=dc).transfer(it, timeout_seconds=120)
     ok = bool(torch.equal(dst.cpu(), src))
-    return receipt_trace_line(r) + f" bytes_match={ok}"
+    return receipt_line(r) + f" bytes_match={ok}"
 
 
-def main(argv=None) -> int:
+def receipt_line(receipt) -> str:
+    """The receipt's trace line: intent, decision, topology snapshot and
+    ticket ids, state, and the direct / relay byte and chunk split."""
+    return receipt_trace_line(receipt)
+
+
+def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--self-contained", action="store_true")
     p.add_argument("--daemon-socket-path")
@@ -62,6 +68,11 @@ def main(argv=None) -> int:
     p.add_argument("--dst-offset", type=int, default=0)
     p.add_argument("--policy", default="daemon-default")
     p.add_argument("--wait-timeout-seconds", type=float, default=120.0)
+    return p
+
+
+def main(argv=None) -> int:
+    p = build_parser()
     a = p.parse_args(argv)
     if a.self_contained:
         print(self_contained(a.bytes))
@@ -72,7 +83,7 @@ def main(argv=None) -> int:
     client = TurboBusClient(socket_path=a.daemon_socket_path)
     intent = build_intent(a)
     client.submit_transfer_intent(intent)
-    print(receipt_trace_line(client.wait_transfer_receipt(intent.intent_id, timeout_seconds=a.wait_timeout_seconds)))
+    print(receipt_line(client.wait_transfer_receipt(intent.intent_id, timeout_seconds=a.wait_timeout_seconds)))
     return 0
 
 

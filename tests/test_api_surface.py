@@ -433,3 +433,25 @@ def test_checksum_at_offsets_compose_and_unit_addresses():
     base = torch.zeros(64, dtype=torch.uint8)
     addrs = unit_addresses(base, 16, [3, 0, 2])
     assert addrs.tolist() == [base.data_ptr() + 48, base.data_ptr(), base.data_ptr() + 32]
+
+
+def test_public_intent_example_builds_a_path_free_intent_and_reports_trace_ids():
+    from pcie_pool_b200.examples import torch_tensor_fetch as ex
+    from pcie_pool_b200.schema import TransferReceipt, TransferStatusState
+
+    a = ex.build_parser().parse_args(["--daemon-socket-path", "/tmp/d.sock", "--session-id", "s1", "--job-id", "j1",
+                                      "--intent-id", "i1", "--source-buffer-id", "cpu", "--destination-buffer-id",
+                                      "gpu", "--bytes", "4096"])
+    it = ex.build_intent(a)
+    assert (it.workload_kind.value, it.direction, it.total_bytes, it.policy_hints) == ("generic", "h2d", 4096, {})
+    for key in ("mode", "target_gpu", "relay_gpus", "path"):
+        assert key not in it.policy_hints and key not in it.metadata
+    r = TransferReceipt(receipt_id="r1", ticket_id="t1", intent_id="i1", decision_id="d1", topology_snapshot_id="x1",
+                        job_id="j1", session_id="s1", state=TransferStatusState.COMPLETE, bytes_total=96,
+                        bytes_completed=96, path_stats=({"kind": "direct", "bytes": 64}, {"kind": "relay", "bytes": 32}))
+    line = ex.receipt_line(r)
+    for want in ("decision_id=d1", "topology_snapshot_id=x1", "ticket_id=t1", "direct_bytes=64", "relay_bytes=32",
+                 "state=complete"):
+        assert want in line
+    with pytest.raises(SystemExit):
+        ex.main(["--bytes", "16"])  # a daemon socket, session and buffers are required without --self-contained
