@@ -8,6 +8,13 @@ intent is the daemon's own work: planning on the profile, leases, ticket,
 dispatch to the executor thread, completion and the receipt.  The timing is
 repeated after ``--history`` earlier intents to show that the per-intent
 cost does not grow with the daemon's history.  Prints one JSON line.
+
+``--protocol daemon`` times the daemon protocol alone, the same way on this
+package's daemon and, with ``--impl reference``, on the unmodified reference
+daemon installed under ``baseline/_ref``: per intent ``submit_transfer_intent``
+(planning, leases, ticket), ``transfer_status`` complete and
+``release_transfer`` of every lease, in process, with the same synthetic
+8-GPU inventory and profile and no data plane.
 """
 
 from __future__ import annotations
@@ -59,6 +66,91 @@ def build(lanes: int, nbytes: int, history_limit: int = 10000):
     return daemon, TurboBusClient(daemon=dc), sid
 
 
+PROFILE_BW = {"direct": 34.0, "relay": 26.0, "p2p": 700.0}
+
+
+def profile_dict(lanes: int) -> dict:
+    return {"target_device": 0, "direct_h2d_bw_gbps": PROFILE_BW["direct"],
+            "direct_d2h_bw_gbps": PROFILE_BW["direct"],
+            "relays": [{"relay_device": r, "target_device": 0, "h2d_bw_gbps": PROFILE_BW["relay"],
+                        "d2h_bw_gbps": PROFILE_BW["relay"], "p2p_bw_gbps": PROFILE_BW["p2p"],
+                        "effective_bw_gbps": PROFILE_BW["relay"], "effective_d2h_bw_gbps": PROFILE_BW["relay"],
+                        "p2p_enabled": True} for r in range(1, lanes)]}
+
+
+def daemon_protocol_node(impl: str, lanes: int, nbytes: int):
+    """(daemon, TransferIntent class, session id) for the bare daemon protocol
+    on this package's daemon or the reference's (its own public classes: a
+    topology provider over its inventory records, then the same calls)."""
+    relays = list(range(1, lanes))
+    if impl == "reference":
+        import pathlib
+        import sys
+
+        ref = pathlib.Path(__file__).resolve().parents[2] / "baseline" / "_ref"
+        if not (ref / "turbobus").is_dir():
+            raise RuntimeError("reference not installed under baseline/_ref")
+        sys.path.insert(0, str(ref))
+        from turbobus.daemon.server import TurboBusDaemon as RefDaemon
+        from turbobus.schema import TransferIntent as RefIntent
+        from turbobus.topology import (DaemonResourceInventory, FabricLinkRecord, GpuInventoryRecord,
+                                       PciePathRecord, TopologyProvider)
+
+        inv = DaemonResourceInventory(
+            gpus=tuple(GpuInventoryRecord(device_id=g, role="relay" if g else "target") for g in range(lanes)),
+            pcie_paths=tuple(PciePathRecord(device_id=g) for g in range(lanes)),
+            fabric_links=tuple(FabricLinkRecord(src_device_id=r, dst_device_id=0, fabric="nvlink", enabled=True)
+                               for r in relays),
+            source="control_plane_benchmark", discovered_at=time.time())
+
+        class Provider(TopologyProvider):
+            def snapshot(self):
+                return inv
+
+            def invalidate(self):
+                return None
+
+        d = RefDaemon(relay_gpus=relays, max_inflight_chunks_per_relay=1 << 20, topology_provider=Provider())
+        intent_cls = RefIntent
+    else:
+        from ..daemon import TurboBusDaemon
+        from ..schema import TransferIntent
+        from ..topology import StaticTopologyProvider
+
+        d = TurboBusDaemon(relay_gpus=relays, max_inflight_chunks_per_relay=1 << 20,
+                           topology_provider=StaticTopologyProvider(gpu_count=lanes), link_hold_seconds=0.0)
+        intent_cls = TransferIntent
+    assert d.put_profile(target_gpu=0, relay_gpus=relays, profile=profile_dict(lanes)).ok
+    sid = d.register_session(target_gpu=0, requested_relays=relays,
+                             max_inflight_chunks=1 << 20).payload["session"]["session_id"]
+    assert d.register_job(job_id="cp", session_id=sid).ok
+    assert d.register_buffer(buffer_id="h", job_id="cp", kind="cpu_pinned", size_bytes=nbytes, address=4096,
+                             pinned=True).ok
+    assert d.register_buffer(buffer_id="g", job_id="cp", kind="gpu", size_bytes=nbytes, device_index=0,
+                             address=8192).ok
+    return d, intent_cls, sid
+
+
+def daemon_protocol_step(d, intent_cls, sid: str, i: int, n: int, chunk: int) -> int:
+    """One intent through the bare protocol; returns its relay lease count."""
+    it = intent_cls(intent_id=f"cp-{i}", job_id="cp", session_id=sid, source_buffer_id="h",
+                    destination_buffer_id="g", direction="h2d", total_bytes=n,
+                    ranges=({"src_offset": 0, "dst_offset": 0, "bytes": n},), workload_kind="model_weights",
+                    metadata={"chunk_bytes": chunk})
+    r = d.submit_transfer_intent(it)
+    if not r.ok:
+        raise RuntimeError(r.error)
+    tid = r.payload["transfer_id"]
+    ticket = r.payload.get("ticket") or {}
+    leases = list(ticket.get("lease_ids") or ())
+    st = d.transfer_status(tid, state="complete", bytes_completed=n)
+    if not st.ok:
+        raise RuntimeError(st.error)
+    for lid in leases:
+        d.release_transfer(lid)
+    return len(leases)
+
+
 def main(argv=None) -> int:
     from .. import TransferIntent
 
@@ -68,8 +160,14 @@ def main(argv=None) -> int:
     p.add_argument("--chunk", default="16M")
     p.add_argument("--intents", type=int, default=200)
     p.add_argument("--history", type=int, default=2000, help="intents run before the second timing")
+    p.add_argument("--protocol", choices=["client", "daemon"], default="client",
+                   help="client: TurboBusClient.transfer over an instant engine; daemon: bare daemon protocol")
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours",
+                   help="daemon implementation for --protocol daemon")
     a = p.parse_args(argv)
     n, chunk = parse_size(a.bytes), parse_size(a.chunk)
+    if a.protocol == "daemon":
+        return _daemon_protocol(a, n, chunk)
     daemon, client, sid = build(a.lanes, n)
     counter = iter(range(1 << 40))
 
@@ -100,6 +198,34 @@ def main(argv=None) -> int:
                       "chunk_bytes": chunk, "chunks": -(-n // chunk), "ms_per_intent": round(first, 3),
                       "ms_per_intent_after_history": round(later, 3), "history": a.history,
                       "retained_transfers": len(daemon.describe().payload["transfer_queue"])}), flush=True)
+    return 0
+
+
+def _daemon_protocol(a, n: int, chunk: int) -> int:
+    d, intent_cls, sid = daemon_protocol_node(a.impl, a.lanes, n)
+    counter = iter(range(1 << 40))
+    leases = []
+
+    def timed(k):
+        out = []
+        for _ in range(5):
+            t0 = time.perf_counter()
+            for _ in range(max(1, k // 5)):
+                leases.append(daemon_protocol_step(d, intent_cls, sid, next(counter), n, chunk))
+            out.append((time.perf_counter() - t0) * 1e3 / max(1, k // 5))
+        return statistics.median(out)
+
+    for _ in range(10):
+        daemon_protocol_step(d, intent_cls, sid, next(counter), n, chunk)
+    first = timed(a.intents)
+    for _ in range(a.history):
+        daemon_protocol_step(d, intent_cls, sid, next(counter), n, chunk)
+    later = timed(a.intents)
+    print(json.dumps({"metric": "daemon protocol ms per intent (submit, complete, release)", "impl": a.impl,
+                      "lanes": a.lanes, "bytes": n, "chunk_bytes": chunk, "chunks": -(-n // chunk),
+                      "relay_leases_per_intent": statistics.median(leases) if leases else 0,
+                      "ms_per_intent": round(first, 3), "ms_per_intent_after_history": round(later, 3),
+                      "history": a.history}), flush=True)
     return 0
 
 

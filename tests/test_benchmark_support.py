@@ -134,3 +134,19 @@ def test_control_plane_benchmark_runs_on_cpu(capsys):
     assert cp.main(["--lanes", "3", "--bytes", "64M", "--chunk", "4M", "--intents", "10", "--history", "15"]) == 0
     out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert out["chunks"] == 16 and out["ms_per_intent"] > 0 and out["retained_transfers"] >= 35
+
+
+@pytest.mark.parametrize("impl", ["ours", "reference"])
+def test_daemon_protocol_benchmark_runs_on_cpu(impl, capsys):
+    import os
+
+    from pcie_pool_b200.benchmarks import control_plane
+
+    ref = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref", "turbobus")
+    if impl == "reference" and not os.path.isdir(ref):
+        pytest.skip("reference not installed under baseline/_ref")
+    assert control_plane.main(["--protocol", "daemon", "--impl", impl, "--lanes", "4", "--bytes", "256M",
+                               "--chunk", "16M", "--intents", "10", "--history", "5"]) == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert out["impl"] == impl and out["chunks"] == 16 and out["relay_leases_per_intent"] == 3
+    assert out["ms_per_intent"] > 0
