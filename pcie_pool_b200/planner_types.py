@@ -71,6 +71,14 @@ class PlannerPath(_AsDict):
         """GPU whose PCIe link carries this path."""
         return self.target_device if self.kind == "direct" else self.relay_device
 
+    def as_dict(self) -> dict[str, object]:
+        # built field by field: every plan conversion calls this once per path
+        return {"kind": self.kind, "direction": self.direction, "target_device": self.target_device,
+                "relay_device": self.relay_device, "h2d_bw_gbps": self.h2d_bw_gbps,
+                "d2h_bw_gbps": self.d2h_bw_gbps, "p2p_bw_gbps": self.p2p_bw_gbps,
+                "effective_bw_gbps": self.effective_bw_gbps, "enabled": self.enabled,
+                "fabric_kind": self.fabric_kind}
+
 
 @dataclass(frozen=True)
 class PlannerPathAssignment:
@@ -87,7 +95,7 @@ class PlannerPathAssignment:
         chunks = [{"src_offset": c.src_offset, "dst_offset": c.dst_offset, "bytes": c.bytes,
                    "relay_device": c.relay_device} for c in self.chunks]
         return {"path": self.path.as_dict(), "chunks": chunks,
-                "bytes": sum(c.bytes for c in self.chunks), "chunk_count": len(chunks)}
+                "bytes": sum(c["bytes"] for c in chunks), "chunk_count": len(chunks)}
 
 
 @dataclass(frozen=True)

@@ -369,3 +369,16 @@ def test_native_and_python_planners_agree():
         cands = [MiB, 4 * MiB, 16 * MiB, 64 * MiB]
         total = int(rng.integers(1, 64)) * 16 * MiB
         assert int(C.choose_chunk_bytes(total, cands, bw, lat)) == min(cands, key=lambda c: _estimate(total, c, bw, lat))
+
+
+def test_plan_records_convert_exactly_like_dataclasses_asdict():
+    from dataclasses import asdict, fields
+
+    from pcie_pool_b200.planner_types import PlannerChunk, PlannerPath, PlannerPathAssignment
+
+    path = PlannerPath("relay", "h2d", 0, 3, 26.0, 25.0, 700.0, 26.0, True, "nvswitch")
+    assert path.as_dict() == asdict(path) and list(path.as_dict()) == [f.name for f in fields(PlannerPath)]
+    a = PlannerPathAssignment(path, (PlannerChunk(0, 0, 8, 3), PlannerChunk(8, 8, 4)))
+    d = a.as_dict()
+    assert d["path"] == asdict(path) and d["chunks"] == [asdict(c) for c in a.chunks]
+    assert (d["bytes"], d["chunk_count"]) == (12, 2)
