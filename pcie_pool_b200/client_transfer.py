@@ -342,11 +342,19 @@ def check_plan_matches_leases(p: Mapping[str, object], tokens, direction: str) -
 
 
 def _release_leases(daemon_client, tokens, reason: str) -> None:
+    """Best-effort cleanup on an error path: a lease that cannot be cleaned
+    here expires on the daemon; the failure is logged, not raised, so the
+    original error reaches the caller."""
+    from .utils.log import logger
+
     for t in tokens:
+        lid = str(t["lease_id"])
         try:
-            daemon_client.cleanup(target_kind="reservation", target_id=str(t["lease_id"]), reason=reason, force=True)
-        except Exception:  # noqa: BLE001 - best effort on an error path
-            pass
+            r = daemon_client.cleanup(target_kind="reservation", target_id=lid, reason=reason, force=True)
+            if not getattr(r, "ok", True):
+                logger("client").warning("lease_cleanup_refused", lease_id=lid, error=getattr(r, "error", ""))
+        except Exception as exc:  # noqa: BLE001 - best effort on an error path
+            logger("client").warning("lease_cleanup_failed", lease_id=lid, error=f"{type(exc).__name__}: {exc}")
 
 
 def submit_worker_execution(worker_client, auth: WorkerTransferAuthorizationRequest) -> WorkerServiceResponseEnvelope:
