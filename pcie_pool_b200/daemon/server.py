@@ -1623,7 +1623,10 @@ class TurboBusDaemon:
             "ranges": tuple(dict(r) for r in ranges) if ranges is not None else (),
             "source_buffer_id": bids[0] if len(bids) >= 1 else None,
             "destination_buffer_id": bids[1] if len(bids) >= 2 else None, "buffer_ids": bids,
-            "workload_kind": None, "priority": 0, "queued_at": float(now), "planned_at": decision.issued_at,
+            # the plan request's kind and priority (an intent's own values replace them on refresh)
+            "workload_kind": S.plan_requests.get(tid, {}).get("workload_kind"),
+            "priority": int(S.plan_requests.get(tid, {}).get("priority", 0) or 0),
+            "queued_at": float(now), "planned_at": decision.issued_at,
             "admission_state": adm.get("state", ADMITTED), "admission_reason": adm.get("reason"),
             "plan_generation": S.generations.get(tid, 0), "plan_expires_at": S.plan_expiry.get(tid),
             "started_at": None, "completed_at": None, "fallback_reason": decision.fallback_reason,

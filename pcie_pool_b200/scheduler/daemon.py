@@ -211,7 +211,11 @@ def parse_mode(mode: TransferMode | str) -> TransferMode:
     try:
         return TransferMode(str(mode))
     except ValueError:
+        pass
+    try:
         return TransferMode[str(mode).upper()]
+    except KeyError:
+        raise ValueError(f"mode must be one of {', '.join(m.value for m in TransferMode)}") from None
 
 
 def resolved_mode(plan: PlannerTransferPlan) -> TransferMode:

@@ -367,3 +367,39 @@ def test_intents_cannot_carry_physical_path_hints(hint):
     with pytest.raises(ValueError):
         TransferIntent("i", "job", "s", "a", "b", "h2d", 16, ({"src_offset": 0, "dst_offset": 0, "bytes": 16},),
                        policy_hints={hint: [1]})
+
+
+# ---- scheduler decisions seen through the daemon ----------------------------------------------------
+
+def test_without_a_profile_the_plan_falls_back_to_direct():
+    d = TurboBusDaemon(relay_gpus=[1, 2, 3], max_inflight_chunks_per_relay=4096,
+                       topology_provider=StaticTopologyProvider(gpu_count=4), clock=Clock())
+    sid = setup_job(d)
+    p = plan(d, sid).payload
+    assert relays_in(p) == [] and p["stats"]["resolved_mode"] == "direct"
+    assert "profile" in p["decision"]["fallback_reason"]
+
+
+@pytest.mark.parametrize("kw,msg", [({"total": -1}, "total_bytes"), ({"chunk": 0}, "chunk_bytes"),
+                                    ({"direction": "sideways"}, "direction"), ({"mode": "teleport"}, "mode"),
+                                    ({"mode": "AUTO"}, None), ({"mode": "relay"}, None)])
+def test_plan_request_values_are_checked(kw, msg):
+    d = daemon()
+    sid = setup_job(d)
+    r = plan(d, sid, **kw)
+    if msg is None:
+        assert r.ok, r.error
+    else:
+        assert not r.ok and msg in r.error
+    assert state(d, "reservations") == {} or r.ok
+
+
+def test_the_workload_kind_reaches_the_decision_and_its_leases():
+    d = daemon()
+    sid = setup_job(d)
+    p = plan(d, sid, workload_kind="kv_cache").payload
+    leases = p["decision"]["metadata"]["leases"]
+    assert len(leases) == 3 and {l["job_id"] for l in leases} == {"job"}
+    assert p["transfer_status"]["job_id"] == "job"
+    (rec,) = state(d, "transfer_queue")
+    assert rec["workload_kind"] == "kv_cache" and rec["transfer_id"] == p["transfer_id"]
