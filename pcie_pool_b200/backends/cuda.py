@@ -39,6 +39,12 @@ class CudaNativeBackend:
         same signature; this backend imports torch itself where it needs it."""
         self._loader = (lambda: native_module) if native_module is not None else None
 
+    def _call(self, name: str, what: str):
+        fn = getattr(self._native(), name, None)
+        if not callable(fn):
+            raise RuntimeError(f"native runtime does not support {what}")
+        return fn
+
     def require_available(self) -> None:
         self._native()
 
@@ -49,7 +55,7 @@ class CudaNativeBackend:
         d = int(device_index)
         if d < 0:
             raise ValueError("device_index must be non-negative")
-        self._native().set_device(d)
+        self._call("set_device", "device selection")(d)
 
     def transfer_mode_value(self, mode: TransferMode | str) -> TransferMode:
         return TransferMode(mode)
@@ -83,27 +89,28 @@ class CudaNativeBackend:
             raise ValueError("host_ptr must be positive")
         if int(bytes_) <= 0:
             raise ValueError("bytes must be positive")
-        self._native().host_register(int(host_ptr), int(bytes_))
+        self._call("host_register", "host memory registration")(int(host_ptr), int(bytes_))
 
     def unregister_host_memory(self, host_ptr: int) -> None:
         if int(host_ptr) <= 0:
             raise ValueError("host_ptr must be positive")
-        self._native().host_unregister(int(host_ptr))
+        self._call("host_unregister", "host memory registration")(int(host_ptr))
 
     def export_device_ipc_handle(self, device_ptr: int) -> bytes:
         if int(device_ptr) <= 0:
             raise ValueError("device_ptr must be positive")
-        return ipc_handle_bytes(bytes(self._native().export_ipc_handle(int(device_ptr))))
+        return ipc_handle_bytes(bytes(self._call("export_ipc_handle", "CUDA IPC export")(int(device_ptr))))
 
     def device_allocation_offset(self, device_ptr: int) -> int:
         """Offset of ``device_ptr`` inside its CUDA allocation (an IPC handle
         names the allocation; the receiver adds this offset to the mapping)."""
         if int(device_ptr) <= 0:
             raise ValueError("device_ptr must be positive")
-        return int(device_ptr) - int(self._native().allocation_base(int(device_ptr)))
+        return int(device_ptr) - int(self._call("allocation_base", "allocation lookup")(int(device_ptr)))
 
     def open_device_ipc_handle(self, cuda_ipc_handle: bytes | bytearray | str, device_index: int = 0) -> int:
-        ptr = int(self._native().open_ipc_handle(coerce_ipc_handle(cuda_ipc_handle), int(device_index)))
+        handle = coerce_ipc_handle(cuda_ipc_handle)  # malformed handles fail before the native call
+        ptr = int(self._call("open_ipc_handle", "CUDA IPC open")(handle, int(device_index)))
         if ptr <= 0:
             raise RuntimeError("native runtime returned an invalid CUDA IPC pointer")
         return ptr
@@ -111,7 +118,7 @@ class CudaNativeBackend:
     def close_device_ipc_handle(self, device_ptr: int) -> None:
         if int(device_ptr) <= 0:
             raise ValueError("device_ptr must be positive")
-        self._native().close_ipc_handle(int(device_ptr))
+        self._call("close_ipc_handle", "CUDA IPC close")(int(device_ptr))
 
     def fetch_plan_to_gpu(self, runtime, host_ptr, host_bytes, target_ptr, target_bytes, plan):
         fn = getattr(runtime, "fetch_plan_to_gpu", None)

@@ -243,3 +243,25 @@ def test_cuda_executor_maps_engine_results():
         assert f.state is WorkerTransferState.FAILED and "bound data-plane resources" in f.error
     finally:
         rig.close()
+
+
+def test_backend_names_missing_native_support_and_checks_handles_before_native_calls():
+    opened = []
+    partial = SimpleNamespace(export_ipc_handle=lambda p: b"\x01" * 10,
+                              open_ipc_handle=lambda h, d: opened.append(h) or 4096)
+    be = CudaNativeBackend(native_loader=lambda: partial)
+    for call, what in ((lambda: be.register_host_memory(4096, 8), "host memory registration"),
+                       (lambda: be.unregister_host_memory(4096), "host memory registration"),
+                       (lambda: be.close_device_ipc_handle(4096), "CUDA IPC close"),
+                       (lambda: be.device_allocation_offset(4096), "allocation lookup"),
+                       (lambda: be.set_device(0), "device selection")):
+        with pytest.raises(RuntimeError, match=f"does not support {what}"):
+            call()
+    with pytest.raises(ValueError, match="64 bytes"):
+        be.export_device_ipc_handle(4096)  # the native side returned a malformed handle
+    with pytest.raises(ValueError):
+        be.open_device_ipc_handle("zz" * 64)
+    assert opened == [], "a malformed handle never reaches the native open"
+    assert be.open_device_ipc_handle(b"\x02" * 64) == 4096 and len(opened) == 1
+    with pytest.raises(ValueError):
+        be.set_device(-1)
