@@ -139,3 +139,57 @@ def test_training_manager_prefetch_offload_cycle():
     tm.mark_on_cpu(["p3"])
     assert tm.bucket("p3").state is BlockState.CPU
     assert [b.info().as_dict()["bytes"] for b in tm.blocks()] == [1024] * 4
+
+
+# ---- model loading and training offload, rule by rule ---------------------------------------------------
+
+def test_buckets_carry_their_metadata_and_load_as_model_weight_intents():
+    c = Client()
+    ml = ModelWeightLoader(c, ctx(WorkloadKind.MODEL_WEIGHTS))
+    cpu, gpu = Tensor(4 << 20), Tensor(4 << 20)
+    b = ml.add_bucket("embed", cpu, gpu, bucket_id=7, cpu_offset=0, gpu_offset=1 << 20, byte_count=1 << 20)
+    assert (b.block_id, b.cpu_slot, b.gpu_slot, b.bytes) == (7, 7, 7, 1 << 20)
+    info = ml.bucket_info("embed")
+    assert info.state is not BlockState.GPU
+    ml.load_bucket("embed")
+    (it,) = c.intents
+    assert (it.direction, it.workload_kind.value, it.total_bytes) == ("h2d", "model_weights", 1 << 20)
+    assert it.ranges[0] == {"src_offset": 0, "dst_offset": 1 << 20, "bytes": 1 << 20}
+    ml.wait("embed")
+    assert ml.bucket_info("embed").state is BlockState.GPU
+    ml.mark_unloaded(["embed"])
+    assert ml.bucket_info("embed").state is BlockState.CPU and len(c.intents) == 1, "marking copies nothing"
+    assert ml.transfer_stats("embed") is None, "the transfer state is reset"
+
+
+def test_packed_model_buckets_load_as_one_intent_and_batches_are_objects():
+    c = Client()
+    ml = ModelWeightLoader(c, ctx(WorkloadKind.MODEL_WEIGHTS))
+    ml.add_packed_buckets("w", Tensor(8 << 20), Tensor(8 << 20), bucket_bytes=1 << 20, bucket_count=8)
+    batch = ml.load_batch([f"w{i}" for i in range(8)])
+    assert len(c.intents) == 1 and len(c.intents[0].ranges) == 8 and batch.operation == "prefetch"
+    batch.wait()
+    assert all(ml.bucket_info(f"w{i}").state is BlockState.GPU for i in range(8))
+    assert batch.transfer_stats().bytes == 8 << 20 and len(batch.as_dict()["blocks"]) == 8
+    with pytest.raises(ValueError):
+        ml.add_packed_buckets("x", Tensor(8), Tensor(8), bucket_bytes=0, bucket_count=1)
+
+
+def test_training_buckets_move_both_ways_as_range_intents():
+    c = Client()
+    tm = TrainingOffloadManager(c, ctx(WorkloadKind.OPTIMIZER_STATE))
+    tm.add_packed_buckets("opt", Tensor(4 << 20), Tensor(4 << 20), bucket_bytes=1 << 20, bucket_count=4,
+                          start_offset=0)
+    names = [f"opt{i}" for i in range(4)]
+    pre = tm.prefetch_batch(names)
+    pre.wait()
+    off = tm.offload_batch(names[::-1])
+    off.wait()
+    p, o = c.intents
+    assert (p.direction, o.direction) == ("h2d", "d2h") and p.workload_kind.value == "optimizer_state"
+    assert [r["src_offset"] for r in o.ranges] == [3 << 20, 2 << 20, 1 << 20, 0]
+    assert all(tm.bucket_info(n).state is BlockState.CPU for n in names)
+    tm.mark_on_gpu(names[:2])
+    assert [tm.bucket_info(n).state for n in names[:2]] == [BlockState.GPU] * 2 and len(c.intents) == 2
+    tm.mark_on_cpu()
+    assert all(tm.bucket_info(n).state is BlockState.CPU for n in names)
