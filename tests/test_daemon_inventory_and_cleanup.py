@@ -403,3 +403,33 @@ def test_the_workload_kind_reaches_the_decision_and_its_leases():
     assert p["transfer_status"]["job_id"] == "job"
     (rec,) = state(d, "transfer_queue")
     assert rec["workload_kind"] == "kv_cache" and rec["transfer_id"] == p["transfer_id"]
+
+
+# ---- checkpoint / resume of the profile cache ---------------------------------------------------------
+
+def test_a_restarted_daemon_resumes_from_its_profile_store(tmp_path):
+    store = tmp_path / "profiles.json"
+
+    def start(clock):
+        return TurboBusDaemon(relay_gpus=[1, 2, 3], topology_provider=StaticTopologyProvider(gpu_count=4),
+                              clock=clock, profile_store_path=str(store), profile_max_age_seconds=600.0)
+
+    clock = Clock(1000.0)
+    first = start(clock)
+    assert first.put_profile(0, [1, 2, 3], profile(), profile_bytes=64 * MiB).ok
+    assert first.put_profile(1, [2], {**profile(1), "target_device": 1,
+                                      "relays": [{**profile(1)["relays"][0], "relay_device": 2,
+                                                  "target_device": 1}]}).ok
+    assert json.loads(store.read_text())["profiles"], "the cache is written through on every update"
+    again = start(clock)
+    got = again.get_profile(0, [3, 2, 1]).payload["profile"]
+    assert got["profile_bytes"] == 64 * MiB and got["updated_at"] == 1000.0
+    assert again.get_profile(1, [2]).payload["profile"]["profile"]["relays"][0]["relay_device"] == 2
+    sid = setup_job(again)
+    assert relays_in(plan(again, sid).payload) == [1, 2, 3], "plans use the resumed profile without re-profiling"
+    assert again.invalidate_profile(1, [2]).payload["removed"]
+    assert start(clock).get_profile(1, [2]).payload["profile"] is None, "invalidation is persisted too"
+    clock.t += 601.0
+    assert start(clock).get_profile(0, [1, 2, 3]).payload["profile"] is None, "stale entries are not resumed"
+    store.write_text("{not json")
+    assert start(clock).get_profile(0, [1, 2, 3]).ok, "a damaged store starts an empty cache"
