@@ -204,10 +204,127 @@ def run_ours(args, dist: Dist) -> dict:
 
 # ---- reference implementation -----------------------------------------------------------
 
+def reference_e2e(args, ref_root: Path, host_np, dev, profile, relays) -> dict:
+    """The reference's own byte-moving public path, end to end, as an
+    application uses it: its daemon (``python -m turbobus.daemon``) and its
+    worker helper (``python -m turbobus.worker``) run as separate processes on
+    AF_UNIX sockets; this process is the client: a ``SharedPinnedCpuBuffer``
+    source, a ``CudaIpcDeviceBuffer`` target and
+    ``WorkerManagedTransferClient.fetch_shared_cpu_to_cuda_ipc`` per step
+    (turbobus/client_transfer.py:87-137).  Each step also reads 4 KiB of the
+    landed bytes back to the host (the step's result check).  Timed by wall
+    clock around whole steps with the device synchronised: the work runs in
+    the worker process, so no event on this process's streams brackets it."""
+    import shutil
+    import subprocess
+    import tempfile
+    import time
+
+    import numpy as np
+    import torch
+    from turbobus.client import CudaIpcDeviceBuffer, SharedPinnedCpuBufferAllocator
+    from turbobus.client_transfer import make_worker_managed_transfer_client
+    from turbobus.daemon import TurboBusDaemonClient
+    from turbobus.runtime_engine import _profile_to_daemon_dict
+    from turbobus.worker import WorkerServiceSocketClient
+
+    n = args.bytes
+    env = {**os.environ, "PYTHONPATH": os.pathsep.join([str(ref_root), os.environ.get("PYTHONPATH", "")])}
+    tmp = tempfile.mkdtemp(prefix="tbref-")
+    dsock, wsock = os.path.join(tmp, "d.sock"), os.path.join(tmp, "w.sock")
+    procs = []
+
+    def wait_sock(path, proc, what):
+        t_end = time.monotonic() + 120
+        while not os.path.exists(path):
+            if proc.poll() is not None:
+                raise RuntimeError(f"reference {what} exited with code {proc.returncode}")
+            if time.monotonic() > t_end:
+                raise RuntimeError(f"reference {what} did not open its socket")
+            time.sleep(0.05)
+
+    cpu = None
+    try:
+        procs.append(subprocess.Popen(
+            [sys.executable, "-m", "turbobus.daemon", "--target-gpu", "0", "--min-relays", "0",
+             "--max-inflight-chunks-per-relay", "4096", "--socket-path", dsock], env=env))
+        wait_sock(dsock, procs[-1], "daemon")
+        procs.append(subprocess.Popen(
+            [sys.executable, "-m", "turbobus.worker", "--daemon-socket-path", dsock, "--socket-path", wsock],
+            env=env))
+        wait_sock(wsock, procs[-1], "worker helper")
+        dc = TurboBusDaemonClient(dsock)
+        if relays:
+            r = dc.put_profile(0, list(relays), _profile_to_daemon_dict(profile), profile_bytes=256 << 20)
+            if not r.ok:
+                raise RuntimeError(f"reference daemon rejected the profile: {r.error}")
+        client = make_worker_managed_transfer_client(dc, target_gpu=0, relay_gpus=list(relays),
+                                                     worker_client=WorkerServiceSocketClient(wsock),
+                                                     max_inflight_chunks=4096)
+        job = f"bench-ref-{os.getpid()}"
+        cpu = SharedPinnedCpuBufferAllocator(name_prefix="tbref-bench").allocate("bench-src", job, n)
+        view = cpu.view  # the buffer's public shared-memory view (write() would copy via bytes)
+        try:
+            view[0:n] = memoryview(host_np).cast("B")
+        finally:
+            view.release()
+        gpu = CudaIpcDeviceBuffer.from_device_pointer(buffer_id="bench-dst", job_id=job, device_index=0,
+                                                      size_bytes=n, device_ptr=int(dev.data_ptr()))
+        mode = "pool" if relays else "direct"
+        probe = np.empty(4096, dtype=np.uint8)
+
+        def step():
+            res = client.fetch_shared_cpu_to_cuda_ipc(cpu, gpu, chunk_bytes=args.chunk, mode=mode, job_id=job)
+            if res.bytes_completed != n:
+                raise RuntimeError(f"reference transfer moved {res.bytes_completed} of {n} bytes")
+            probe[:] = dev[n - 4096:].cpu().numpy()
+            return res
+
+        for _ in range(max(1, min(args.warmup, 2))):
+            step()
+        steps = max(1, min(args.steps, 5))
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            last = step()
+        torch.cuda.synchronize()
+        ms = (time.perf_counter() - t0) * 1e3
+        ok = bool(np.array_equal(probe, host_np[n - 4096:]))
+        return {"value": round(n * steps / 1e9 / (ms / 1e3), 3), "unit": "GB/s",
+                "ms_per_step": round(ms / steps, 3), "steps": steps,
+                "h2d_bytes_per_step": n, "d2h_bytes_per_step": 4096, "verified_tail": ok,
+                "path": "WorkerManagedTransferClient.fetch_shared_cpu_to_cuda_ipc -> reference daemon "
+                        "(AF_UNIX) -> reference worker helper (AF_UNIX) -> _turbobus runtime per transfer",
+                "mode": mode, "final_state": last.state}
+    finally:
+        if cpu is not None:
+            try:
+                cpu.close()
+                cpu.unlink()
+            except Exception:  # noqa: BLE001 - best-effort cleanup
+                pass
+        for p in procs:
+            p.terminate()
+        for p in procs:
+            try:
+                p.wait(timeout=10)
+            except subprocess.TimeoutExpired:
+                p.kill()
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 def run_reference(args, dist: Dist) -> dict:
     ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "turbobus").exists() and dist.rank == 0:
+        # A fresh box gets the install only when it was made before the
+        # snapshot; build it here from the reference source if that exists.
+        from __graft_entry__ import install_reference
+
+        outcome = install_reference(str(ref_root))
+        print(f"reference arm: {outcome}", file=sys.stderr, flush=True)
+    dist.barrier()
     if not (ref_root / "turbobus").exists():
-        return {"unavailable": "reference not installed under baseline/_ref"}
+        return {"unavailable": "reference not installed under baseline/_ref and its source is not on this box"}
     sys.path.insert(0, str(ref_root))
     import torch
 
@@ -277,6 +394,11 @@ def run_reference(args, dist: Dist) -> dict:
             },
         }
         del rt
+        if not args.no_e2e and args.direction == "h2d":
+            try:
+                out["e2e"] = reference_e2e(args, ref_root, host_t.numpy(), dev, profile, relays)
+            except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+                out["e2e"] = {"error": f"{type(exc).__name__}: {exc}"}
     return out
 
 
@@ -326,6 +448,8 @@ def main(argv=None) -> int:
             if args.impl == "reference":
                 line["impl"] = "reference"
                 line["profile"] = res.get("profile")
+                if "e2e" in res:
+                    line["e2e"] = res["e2e"]
             else:
                 line["impl"] = "ours"
                 line["lane_set"] = res.get("lane_set")

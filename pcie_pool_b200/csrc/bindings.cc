@@ -191,6 +191,7 @@ PYBIND11_MODULE(_C, m) {
       .def_readwrite("op", &TransferSpec::op)
       .def_readwrite("checksum", &TransferSpec::checksum)
       .def_readwrite("stage_direct", &TransferSpec::stage_direct)
+      .def_readwrite("serialize", &TransferSpec::serialize)
       .def_readwrite("debug_drop_publish", &TransferSpec::debug_drop_publish)
       .def_readwrite("trace", &TransferSpec::trace)
       .def_readwrite("ctas_per_lane", &TransferSpec::ctas_per_lane)

@@ -89,6 +89,7 @@ struct PoolEngine::Pending {
   std::vector<Ring*> rings;
   std::vector<int> ring_devices;
   cudaEvent_t start = nullptr, stop = nullptr, kern_done = nullptr;
+  std::pair<uint8_t*, size_t> scratch{nullptr, 0};  // device scratch (reused buffer)
   void* desc_host = nullptr;
   void* result_host = nullptr;
   size_t kernel_chunks = 0;
@@ -146,6 +147,7 @@ PoolEngine::PoolEngine(const std::vector<int>& devices, const EngineOptions& opt
     }
     cudaGetLastError();
     D->max_ctas = lane_kernel_max_ctas(d);
+    D->can_flush_remote_writes = can_flush_remote_writes(d);
     devs_[d] = std::move(D);
   }
   if (options_.enable_peer_access) {
@@ -194,6 +196,8 @@ PoolEngine::~PoolEngine() {
       }
     }
     if (D.mbox) cudaFree(D.mbox);
+    for (auto& b : D.free_scratch) cudaFree(b.first);
+    for (auto* b : D.quarantine) cudaFree(b);
     for (auto e : D.free_events) cudaEventDestroy(e);
     for (int dir = 0; dir < 2; ++dir) {
       cudaStreamDestroy(D.main[dir]);
@@ -202,6 +206,10 @@ PoolEngine::~PoolEngine() {
     }
   }
   for (auto& kv : pending_) {
+    if (kv.second->scratch.first) {
+      cudaSetDevice(kv.second->target);
+      cudaFree(kv.second->scratch.first);
+    }
     if (kv.second->desc_host) cudaFreeHost(kv.second->desc_host);
     if (kv.second->result_host) cudaFreeHost(kv.second->result_host);
   }
@@ -239,6 +247,31 @@ cudaEvent_t PoolEngine::take_event(Dev& d) {
 
 void PoolEngine::give_event(Dev& d, cudaEvent_t e) {
   if (e) d.free_events.push_back(e);
+}
+
+std::pair<uint8_t*, size_t> PoolEngine::take_scratch(Dev& d, size_t bytes) {
+  // Smallest free buffer that fits; else a new one (rounded up to 1 MiB so a
+  // few sizes cover every transfer; made once, then reused).
+  size_t best = d.free_scratch.size();
+  for (size_t i = 0; i < d.free_scratch.size(); ++i) {
+    if (d.free_scratch[i].second >= bytes &&
+        (best == d.free_scratch.size() || d.free_scratch[i].second < d.free_scratch[best].second))
+      best = i;
+  }
+  if (best != d.free_scratch.size()) {
+    auto b = d.free_scratch[best];
+    d.free_scratch.erase(d.free_scratch.begin() + static_cast<long>(best));
+    return b;
+  }
+  const size_t cap = align_up(std::max<size_t>(bytes, 1), size_t(1) << 20);
+  DeviceGuard g(d.device);
+  void* p = nullptr;
+  PPB_CUDA(cudaMalloc(&p, cap));
+  return {static_cast<uint8_t*>(p), cap};
+}
+
+void PoolEngine::give_scratch(Dev& d, std::pair<uint8_t*, size_t> b) {
+  if (b.first) d.free_scratch.push_back(b);
 }
 
 void* PoolEngine::take_pinned(size_t bytes) {
@@ -307,7 +340,7 @@ void PoolEngine::reset_rings(Pending& P) {
 
 namespace {
 
-void validate_spec(const TransferSpec& s, uint64_t slot_bytes) {
+void validate_spec(const TransferSpec& s, uint64_t slot_bytes, size_t slots) {
   if (s.direction != 0 && s.direction != 1) throw std::invalid_argument("direction must be 0 or 1");
   if (s.host_ptr == 0 || s.dev_ptr == 0) throw std::invalid_argument("null buffer pointer");
   if (s.lanes.empty()) throw std::invalid_argument("transfer has no lanes");
@@ -355,6 +388,8 @@ void validate_spec(const TransferSpec& s, uint64_t slot_bytes) {
       const bool staged = L.device != s.target || s.op != kOpCopy || s.stage_direct;
       if (staged && c.bytes > slot_bytes)
         throw std::invalid_argument("chunk larger than the staging slot");
+      if (staged && s.serialize && L.chunks.size() > slots)
+        throw std::invalid_argument("serialized transfer: a staged lane holds more chunks than slots");
       if (s.op == kOpScatterUnits || s.op == kOpGatherUnits) {
         if (c.bytes % s.unit_bytes != 0) throw std::invalid_argument("chunk not a whole number of units");
         if (uint64_t(c.unit0) + c.bytes / s.unit_bytes > s.unit_addrs.size())
@@ -389,7 +424,7 @@ void validate_spec(const TransferSpec& s, uint64_t slot_bytes) {
 
 uint64_t PoolEngine::submit(const TransferSpec& s) {
   std::lock_guard<std::mutex> guard(mu_);
-  validate_spec(s, options_.slot_bytes);
+  validate_spec(s, options_.slot_bytes, static_cast<size_t>(options_.slots));
   const bool h2d = s.direction == 0;
   Dev& T = dev(s.target);
   for (const auto& L : s.lanes) dev(L.device);  // every lane device is managed
@@ -574,8 +609,12 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     PPB_CUDA(cudaEventRecord(R.t0, R.stream));
   }
 
-  void* scratch = nullptr;
-  if (P.has_kernel) {
+  // Pipelined (default): the kernel is queued before any copy-engine work so a
+  // failed launch leaves no relay stream waiting on it.  Serialised: H2D
+  // launches after the copies (below); D2H copies start after the kernel.
+  const bool kernel_after_copies = s.serialize && h2d;
+  auto launch_kernel = [&]() {
+    if (!P.has_kernel) return;
     P.desc_host = take_pinned(upload_bytes + 256);
     P.result_host = take_pinned(result_bytes + 256);
     uint8_t* h = static_cast<uint8_t*>(P.desc_host);
@@ -592,9 +631,9 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
       qt.push_back(QuantTensor{reinterpret_cast<uint8_t*>(t.q), reinterpret_cast<float*>(t.scales), t.rows, t.cols});
     put(o_tensors, qt.data(), qt.size() * sizeof(QuantTensor));
 
+    P.scratch = take_scratch(T, scratch_bytes);
     PPB_CUDA(cudaStreamWaitEvent(tkern, P.start, 0));
-    PPB_CUDA(cudaMallocAsync(&scratch, scratch_bytes, tkern));
-    uint8_t* dsc = static_cast<uint8_t*>(scratch);
+    uint8_t* dsc = P.scratch.first;
     PPB_CUDA(cudaMemcpyAsync(dsc, h, upload_bytes, cudaMemcpyHostToDevice, tkern));
     PPB_CUDA(cudaMemsetAsync(dsc + o_csum, 0, scratch_bytes - o_csum, tkern));
 
@@ -621,16 +660,29 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     const cudaError_t lrc = h2d ? launch_land(kp, static_cast<int>(cta), tkern)
                                 : launch_push(kp, static_cast<int>(cta), tkern);
     if (lrc != cudaSuccess) {
-      cudaFreeAsync(scratch, tkern);
-      for (auto& R : P.lanes)
-        if (R.ring) R.ring->issued = R.seq0;
+      cudaStreamSynchronize(tkern);  // the scratch upload is done before reuse
+      give_scratch(T, P.scratch);
+      P.scratch = {nullptr, 0};
+      for (auto& R : P.lanes) {
+        if (!R.ring) continue;
+        R.ring->issued = R.seq0;
+        // serialised H2D: the copies already published their chunks
+        if (kernel_after_copies) R.ring->poisoned = true;
+      }
       give_pinned(P.desc_host);
       give_pinned(P.result_host);
       check_cuda(lrc, "lane kernel launch");
     }
     PPB_CUDA(cudaMemcpyAsync(P.result_host, dsc + o_csum, result_bytes, cudaMemcpyDeviceToHost, tkern));
-    PPB_CUDA(cudaFreeAsync(scratch, tkern));
     PPB_CUDA(cudaEventRecord(P.kern_done, tkern));
+  };
+
+  if (!kernel_after_copies) launch_kernel();
+  if (s.serialize && !h2d && P.has_kernel) {
+    for (auto& R : P.lanes) {
+      DeviceGuard lg(R.device);
+      PPB_CUDA(cudaStreamWaitEvent(R.stream, P.kern_done, 0));
+    }
   }
 
   // ---- copy-engine side, chunks interleaved round-robin across lanes ------------
@@ -691,7 +743,7 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
       } else {
         uint8_t* hdst = const_cast<uint8_t*>(host) + c.dst_off;
         if (R.staged) {
-          stream_wait_geq(R.stream, R.ring->ready, seq, can_flush_remote_writes(R.device));
+          stream_wait_geq(R.stream, R.ring->ready, seq, R.d->can_flush_remote_writes);
           PPB_CUDA(cudaMemcpyAsync(hdst, slot, c.bytes, cudaMemcpyDeviceToHost, R.stream));
           stream_write(R.stream, R.ring->freec, seq);
         } else {
@@ -704,6 +756,11 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
   for (auto& R : P.lanes) {
     DeviceGuard lg(R.device);
     PPB_CUDA(cudaEventRecord(R.t1, R.stream));
+  }
+  if (kernel_after_copies && P.has_kernel) {
+    DeviceGuard kg(s.target);
+    for (auto& R : P.lanes) PPB_CUDA(cudaStreamWaitEvent(tkern, R.t1, 0));
+    launch_kernel();
   }
   PPB_CUDA(cudaSetDevice(s.target));
   for (auto& R : P.lanes) PPB_CUDA(cudaStreamWaitEvent(tmain, R.t1, 0));
@@ -856,6 +913,15 @@ TransferResult PoolEngine::wait(uint64_t id, double host_timeout_s) {
     give_event(*R.d, R.t0);
     give_event(*R.d, R.t1);
   }
+  if (done || cudaEventQuery(stop) == cudaSuccess) {
+    give_scratch(T, P.scratch);
+  } else if (P.scratch.first) {
+    // The kernel may still run (its own waits are bounded): keep the buffer
+    // out of reuse until the engine is destroyed.
+    T.quarantine.push_back(P.scratch.first);
+  }
+  cudaGetLastError();
+  P.scratch = {nullptr, 0};
   give_pinned(P.desc_host);
   give_pinned(P.result_host);
   if (!res.ok) {

@@ -79,6 +79,12 @@ struct TransferSpec {
   int op = kOpCopy;
   bool checksum = false;
   bool stage_direct = false;  // route a plain-copy direct lane through the landing ring
+  // Serialised mode: H2D issues and finishes every copy-engine copy before the
+  // landing kernel starts; D2H starts the copy-out after the push kernel ends.
+  // No kernel then waits on a copy running beside it, so the transfer also
+  // completes when a profiler serialises all GPU work.  Each staged lane may
+  // hold at most `slots` chunks (nothing frees a slot mid-transfer).
+  bool serialize = false;
   int debug_drop_publish = -1;  // tests: lane whose "ready" publications are skipped
   bool trace = false;        // record per-chunk %globaltimer stamps (TransferResult::trace)
   int ctas_per_lane = 0;     // 0: engine default
@@ -161,7 +167,13 @@ class PoolEngine {
     uint32_t* mbox = nullptr;  // 8 counters, each on its own 128-byte line
     Ring relay[2], land[2];
     std::vector<cudaEvent_t> free_events;
+    // Lane-kernel scratch (descriptor tables, checksums, status, arrival
+    // counters): device buffers made once and reused, one per transfer in
+    // flight; a buffer returns here when its transfer is waited on.
+    std::vector<std::pair<uint8_t*, size_t>> free_scratch;
+    std::vector<uint8_t*> quarantine;  // scratch of transfers abandoned by the watchdog
     int max_ctas = 0;
+    bool can_flush_remote_writes = false;
   };
   struct Pending;
 
@@ -169,6 +181,8 @@ class PoolEngine {
   void ensure_ring(Dev& d, Ring& r, bool relay);
   cudaEvent_t take_event(Dev& d);
   void give_event(Dev& d, cudaEvent_t e);
+  std::pair<uint8_t*, size_t> take_scratch(Dev& d, size_t bytes);
+  void give_scratch(Dev& d, std::pair<uint8_t*, size_t> b);
   void* take_pinned(size_t bytes);
   void give_pinned(void* p);
   void reset_rings(Pending& p);

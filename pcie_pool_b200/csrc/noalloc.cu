@@ -20,11 +20,13 @@ using ppb::LaneKernelParams;
 constexpr size_t kOffLane = 0;
 constexpr size_t kOffReady = 256;
 constexpr size_t kOffStatus = 512;
+constexpr size_t kOffBadUnit = 640;  // first bad unit index + 1 (0: table is good)
 constexpr size_t kOffDone = 768;
 constexpr size_t kOffCsum = kOffDone + size_t(PPB_NOALLOC_MAX_CHUNKS) * sizeof(uint32_t);
 constexpr size_t kOffChunks = kOffCsum + size_t(PPB_NOALLOC_MAX_CHUNKS) * 2 * sizeof(unsigned long long);
 constexpr size_t kScratchUsed = kOffChunks + size_t(PPB_NOALLOC_MAX_CHUNKS) * sizeof(ChunkDesc);
 static_assert(sizeof(LaneDesc) <= kOffReady - kOffLane, "lane descriptor region");
+static_assert(kOffBadUnit + 8 <= kOffDone && kOffStatus + 16 <= kOffBadUnit, "status regions");
 static_assert(kOffCsum % 256 == 0 && kOffChunks % 256 == 0, "scratch regions stay 256-byte aligned");
 static_assert(kScratchUsed <= PPB_NOALLOC_SCRATCH_BYTES, "scratch array too small for the layout");
 
@@ -61,6 +63,7 @@ __global__ void noalloc_prepare(unsigned char* s, const uint8_t* src, uint64_t s
     *reinterpret_cast<uint32_t*>(s + kOffReady) = 1u;  // every chunk is published (seq 1)
     int* st = reinterpret_cast<int*>(s + kOffStatus);
     st[0] = st[1] = st[2] = st[3] = 0;
+    *reinterpret_cast<unsigned long long*>(s + kOffBadUnit) = ~0ull;
   }
   if (i < nchunks) {
     const uint64_t off = uint64_t(i) * chunk_bytes;
@@ -80,6 +83,30 @@ __global__ void noalloc_prepare(unsigned char* s, const uint8_t* src, uint64_t s
     cs[2 * i] = 0ull;
     cs[2 * i + 1] = 0ull;
   }
+}
+
+// Checks every unit address of a scatter (non-null, 16-byte aligned) and
+// records the first bad unit.  Grid-stride over all units.
+__global__ void noalloc_check_units(unsigned char* s, const uint64_t* unit_addrs, uint64_t units) {
+  unsigned long long* bad = reinterpret_cast<unsigned long long*>(s + kOffBadUnit);
+  for (uint64_t u = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; u < units;
+       u += uint64_t(gridDim.x) * blockDim.x) {
+    const uint64_t a = unit_addrs[u];
+    if (a == 0 || (a & 15u) != 0) atomicMin(bad, static_cast<unsigned long long>(u + 1));
+  }
+}
+
+// After the check: a bad table empties the lane (the landing kernel then
+// issues no copy at all) and reports kStatusBadArgument with the unit index.
+__global__ void noalloc_gate(unsigned char* s) {
+  const unsigned long long bad = *reinterpret_cast<unsigned long long*>(s + kOffBadUnit);
+  if (bad == ~0ull) return;
+  reinterpret_cast<LaneDesc*>(s + kOffLane)->chunk_count = 0;
+  int* st = reinterpret_cast<int*>(s + kOffStatus);
+  st[0] = ppb::kStatusBadArgument;
+  st[1] = 0;
+  st[2] = -1;
+  st[3] = static_cast<int>(bad - 1);
 }
 
 struct CurrentDevice {
@@ -147,7 +174,12 @@ __attribute__((visibility("default"))) int ppb_noalloc_land(
   if (op == PPB_NOALLOC_OP_COPY) {
     if (dst == nullptr || dst_bytes < src_bytes) return PPB_NOALLOC_E_ARGUMENT;
   } else {
-    if (unit_addrs == nullptr || unit_bytes == 0) return PPB_NOALLOC_E_ARGUMENT;
+    // The scatter moves whole units with 16-byte bulk copies: the source, the
+    // unit size and (checked on the device) every unit address must be
+    // 16-byte aligned.
+    if (unit_addrs == nullptr || unit_bytes == 0 || unit_bytes % 16 != 0) return PPB_NOALLOC_E_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0) return PPB_NOALLOC_E_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(unit_addrs) & 7u) != 0) return PPB_NOALLOC_E_ARGUMENT;
     if (src_bytes % unit_bytes != 0 || chunk_bytes % unit_bytes != 0) return PPB_NOALLOC_E_ARGUMENT;
     if (src_bytes / unit_bytes > 0xFFFFFFFFull) return PPB_NOALLOC_E_TOO_LARGE;
   }
@@ -167,6 +199,15 @@ __attribute__((visibility("default"))) int ppb_noalloc_land(
                                                    op == PPB_NOALLOC_OP_SCATTER_UNITS ? 1u : 0u);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return static_cast<int>(e);
+  if (op == PPB_NOALLOC_OP_SCATTER_UNITS) {
+    const uint64_t units = src_bytes / unit_bytes;
+    const uint64_t want = (units + 255) / 256;
+    const unsigned int blocks = static_cast<unsigned int>(want < 1184 ? want : 1184);
+    noalloc_check_units<<<blocks, 256, 0, st>>>(s, unit_addrs, units);
+    noalloc_gate<<<1, 1, 0, st>>>(s);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
 
   LaneKernelParams p{};
   p.lanes = reinterpret_cast<const LaneDesc*>(s + kOffLane);
@@ -217,7 +258,8 @@ __attribute__((visibility("default"))) const char* ppb_noalloc_strerror(int code
     case 0:
       return "ok";
     case PPB_NOALLOC_E_ARGUMENT:
-      return "invalid argument (null pointer, zero size, unknown op or unit/chunk mismatch)";
+      return "invalid argument (null pointer, zero size, unknown op, unit/chunk mismatch, or a "
+             "scatter whose source or unit size is not 16-byte aligned)";
     case PPB_NOALLOC_E_TOO_LARGE:
       return "request exceeds the static scratch: more than 4096 chunks, chunk_bytes >= 4 GiB "
              "or more than 2^32-1 units";

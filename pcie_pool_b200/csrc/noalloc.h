@@ -53,7 +53,11 @@ int ppb_noalloc_setup(int device);
 //   COPY:          dst[i] = src[i] for i < src_bytes (dst_bytes >= src_bytes)
 //   SCATTER_UNITS: unit u (bytes [u*unit_bytes, (u+1)*unit_bytes) of src)
 //                  -> unit_addrs[u]; src_bytes and chunk_bytes are multiples
-//                  of unit_bytes; dst/dst_bytes are unused.
+//                  of unit_bytes; dst/dst_bytes are unused.  src and
+//                  unit_bytes must be 16-byte aligned (checked here); the
+//                  unit table is device memory, so its entries are checked on
+//                  the device: a null or misaligned address makes the call
+//                  land nothing and report status 3 with detail = unit index.
 // Chunk c covers src bytes [c*chunk_bytes, min(src_bytes, (c+1)*chunk_bytes)).
 // `ctas` CTAs share the chunks (clamped to the device's resident maximum);
 // timeout_ns bounds every device-side wait (0 = 10 s).
@@ -64,7 +68,8 @@ int ppb_noalloc_land(int device, int op, const void* src, uint64_t src_bytes, vo
 
 // Wait for `stream` and copy back the status words {code, lane, chunk, detail}
 // and the first `chunks` per-chunk checksums {sum, weighted} (2*chunks words;
-// csum may be null).  Status code 0 = ok, 1/2 = a wait ran out, 3 = bad op.
+// csum may be null).  Status code 0 = ok, 1/2 = a wait ran out, 3 = bad
+// argument (op, or a unit address; then nothing was written).
 int ppb_noalloc_result(int device, int* status4, unsigned long long* csum, uint32_t chunks,
                        void* stream);
 

@@ -11,6 +11,8 @@
 // Synchronisation with the copy engines uses two monotonically increasing
 // 32-bit counters per lane (ready / free) compared wrap-around safely; every
 // wait is bounded and ends in an error status, never a trap.
+#include <atomic>
+
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
@@ -480,20 +482,23 @@ __global__ void __launch_bounds__(kLaneThreads, 1) push_kernel(const LaneKernelP
   if (threadIdx.x == 0) bulk_wait_all<0>();
 }
 
-bool g_attr_set[64] = {false};
+// Per-device "attributes set" flags.  Launchers run from several host threads
+// (PoolEngine under its lock, the allocation-free entry point without it);
+// setting the attribute twice is harmless, the flag only has to be race-free.
+std::atomic<bool> g_attr_set[64];
 
 cudaError_t prepare_attrs() {
   int dev = 0;
   cudaError_t rc = cudaGetDevice(&dev);
   if (rc != cudaSuccess) return rc;
-  if (dev >= 0 && dev < 64 && g_attr_set[dev]) return cudaSuccess;
+  if (dev >= 0 && dev < 64 && g_attr_set[dev].load(std::memory_order_acquire)) return cudaSuccess;
   rc = cudaFuncSetAttribute(land_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             static_cast<int>(kLaneSmemBytes));
   if (rc != cudaSuccess) return rc;
   rc = cudaFuncSetAttribute(push_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             static_cast<int>(kLaneSmemBytes));
   if (rc != cudaSuccess) return rc;
-  if (dev >= 0 && dev < 64) g_attr_set[dev] = true;
+  if (dev >= 0 && dev < 64) g_attr_set[dev].store(true, std::memory_order_release);
   return cudaSuccess;
 }
 

@@ -826,23 +826,38 @@ class TurboBusDaemon:
         with self._lock:
             self._purge_profiles(self._now())
             self._st.profiles[profile_key(target, relays)] = entry
-            self._save_profiles()
+            stored = self._save_profiles()
+        if stored is not None:
+            return ok(profile=dict(entry), profile_store_error=stored)
         return ok(profile=dict(entry))
 
     def invalidate_profile(self, target_gpu: int, relay_gpus: Iterable[int]) -> DaemonResponse:
         key = profile_key(target_gpu, relay_gpus)
         with self._lock:
             gone = self._st.profiles.pop(key, None)
-            self._save_profiles()
-            return ok(profile_key=key, removed=gone is not None)
+            stored = self._save_profiles()
+        extra = {} if stored is None else {"profile_store_error": stored}
+        return ok(profile_key=key, removed=gone is not None, **extra)
 
-    def _save_profiles(self) -> None:
+    def _save_profiles(self) -> str | None:
+        """Write the profile cache through to disk (temp file, fsync, atomic
+        rename).  The in-memory cache stays authoritative: a failed write is
+        logged and returned as a message, never raised, so a full or
+        read-only disk cannot turn a profile update into a daemon error."""
         if not self._profile_store:
-            return
+            return None
         tmp = f"{self._profile_store}.tmp"
-        with open(tmp, "w", encoding="utf-8") as fh:
-            json.dump({"format": PROFILE_STORE_FORMAT, "profiles": self._st.profiles}, fh, sort_keys=True)
-        os.replace(tmp, self._profile_store)
+        try:
+            with open(tmp, "w", encoding="utf-8") as fh:
+                json.dump({"format": PROFILE_STORE_FORMAT, "profiles": self._st.profiles}, fh, sort_keys=True)
+                fh.flush()
+                os.fsync(fh.fileno())
+            os.replace(tmp, self._profile_store)
+        except OSError as exc:
+            msg = f"profile store not written: {exc}"
+            _LOG.warning("profile_store_write_failed", path=self._profile_store, error=str(exc))
+            return msg
+        return None
 
     def _load_profiles(self, path: str) -> None:
         try:

@@ -43,12 +43,38 @@ def setup(device: int) -> None:
     _check(library().ppb_noalloc_setup(int(device)))
 
 
+def _check_tensors(src, dst, unit_addrs) -> None:
+    """The C entry point takes raw device addresses: reject what would make it
+    read or write the wrong memory (host tensors, another device, strided
+    views, a unit table that is not 64-bit)."""
+    import torch
+
+    named = [("src", src)] + ([("dst", dst)] if dst is not None else []) + \
+        ([("unit_addrs", unit_addrs)] if unit_addrs is not None else [])
+    for name, t in named:
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor (the unit table too: it is read on the device)")
+        if t.device != src.device:
+            raise ValueError(f"{name} is on {t.device}, src is on {src.device}")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if unit_addrs is not None and unit_addrs.dtype not in (torch.int64, torch.uint64):
+        raise ValueError("unit_addrs must be an int64 or uint64 tensor of device addresses")
+    if dst is not None and unit_addrs is not None:
+        raise ValueError("give dst (copy) or unit_addrs (scatter), not both")
+
+
 def land(src, dst=None, *, chunk_bytes: int, ctas: int = 4, unit_addrs=None, unit_bytes: int = 0,
          checksum: bool = True, timeout_ns: int = 0, stream=None) -> None:
     """Queue a copy (``dst`` given) or a unit scatter (``unit_addrs`` given) on
     the current torch stream of ``src``'s device; asynchronous."""
     import torch
 
+    _check_tensors(src, dst, unit_addrs)
+    if unit_addrs is not None and unit_addrs.numel() * int(unit_bytes or 1) < src.numel() * src.element_size():
+        raise ValueError("unit_addrs has fewer entries than src holds units")
     dev = src.device.index
     s = torch.cuda.current_stream(src.device) if stream is None else stream
     op = OP_COPY if unit_addrs is None else OP_SCATTER_UNITS

@@ -122,7 +122,8 @@ class PoolEngine:
     # -- submission -------------------------------------------------------------
     def submit(self, direction: int, target: int, host_ptr: int, host_bytes: int, dev_ptr: int,
                dev_bytes: int, lanes: Sequence[Lane], op: int | None = None,
-               checksum: bool = False, stage_direct: bool = False, ctas_per_lane: int = 0, timeout_s: float = 0.0,
+               checksum: bool = False, stage_direct: bool = False, serialize: bool = False,
+               ctas_per_lane: int = 0, timeout_s: float = 0.0,
                unit_bytes: int = 0, unit_addrs: np.ndarray | None = None,
                ranges: tuple[np.ndarray, np.ndarray, np.ndarray] | None = None,
                tensors: Sequence[tuple[int, int, int, int]] = (),
@@ -138,6 +139,7 @@ class PoolEngine:
         spec.op = C.OP_COPY if op is None else int(op)
         spec.checksum = bool(checksum)
         spec.stage_direct = bool(stage_direct)
+        spec.serialize = bool(serialize)
         spec.debug_drop_publish = int(debug_drop_publish)
         spec.trace = bool(trace)
         spec.ctas_per_lane = int(ctas_per_lane)
