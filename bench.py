@@ -246,8 +246,11 @@ def reference_e2e(args, ref_root: Path, host_np, dev, profile, relays) -> dict:
     cpu = None
     try:
         procs.append(subprocess.Popen(
+            # --allow-missing-fabric: the reference's own switch for a node
+            # whose discovery reports no GPU-GPU links (a 1-GPU run)
             [sys.executable, "-m", "turbobus.daemon", "--target-gpu", "0", "--min-relays", "0",
-             "--max-inflight-chunks-per-relay", "4096", "--socket-path", dsock], env=env))
+             "--max-inflight-chunks-per-relay", "4096", "--socket-path", dsock]
+            + ([] if relays else ["--allow-missing-fabric"]), env=env))
         wait_sock(dsock, procs[-1], "daemon")
         procs.append(subprocess.Popen(
             [sys.executable, "-m", "turbobus.worker", "--daemon-socket-path", dsock, "--socket-path", wsock],
