@@ -191,12 +191,16 @@ def run_ours(args, dist: Dist) -> dict:
             "probe": None if profile is None else profile.get("concurrent"),
         }
         if not args.no_e2e and direction == H2D:
-            try:
-                from pcie_pool_b200.e2e import public_api_pooled_load
+            from pcie_pool_b200.e2e import public_api_pooled_load, socket_daemon_pooled_load
 
-                out["e2e"] = public_api_pooled_load(args, eng, host, dev, profile)
+            try:
+                out["e2e"] = socket_daemon_pooled_load(args, host.numpy(), dev, profile, lane_set)
             except Exception as exc:  # pragma: no cover - reported in the JSON line
                 out["e2e"] = {"error": f"{type(exc).__name__}: {exc}"}
+            try:
+                out["e2e_inprocess"] = public_api_pooled_load(args, eng, host, dev, profile)
+            except Exception as exc:  # pragma: no cover - reported in the JSON line
+                out["e2e_inprocess"] = {"error": f"{type(exc).__name__}: {exc}"}
         del eng
         host.release()
     return out
@@ -459,6 +463,8 @@ def main(argv=None) -> int:
                 line["probe"] = res.get("probe")
                 if "e2e" in res:
                     line["e2e"] = res["e2e"]
+                if "e2e_inprocess" in res:
+                    line["e2e_inprocess"] = res["e2e_inprocess"]
         s = json.dumps(line)
         print(s, flush=True)
         if args.json_out:

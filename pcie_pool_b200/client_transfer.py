@@ -12,6 +12,8 @@ planning releases the planned relay leases.
 
 from __future__ import annotations
 
+from .planner_types import assignment_has_chunks, assignment_spans
+
 from dataclasses import asdict, dataclass, field
 from collections.abc import Mapping
 from typing import Iterable
@@ -305,8 +307,7 @@ def check_direct_plan(plan: Mapping[str, object], target: int, direction: str, h
             raise RuntimeError("daemon direct plan target does not match buffer device")
         if not bool(path.get("enabled", True)):
             raise RuntimeError("daemon direct plan path is disabled")
-        for c in a.get("chunks") or ():
-            s, d, n = int(c["src_offset"]), int(c["dst_offset"]), int(c["bytes"])
+        for s, d, n in assignment_spans(a):
             if n <= 0:
                 raise RuntimeError("daemon direct plan chunk bytes must be positive")
             if s < 0 or s + n > src_size:
@@ -333,7 +334,7 @@ def check_plan_matches_leases(p: Mapping[str, object], tokens, direction: str) -
         path = a["path"]
         if str(path.get("direction", direction)).lower() != direction:
             raise RuntimeError("daemon transfer plan direction does not match request")
-        if str(path.get("kind", "")).lower() == "relay" and a.get("chunks"):
+        if str(path.get("kind", "")).lower() == "relay" and assignment_has_chunks(a):
             relays.add(int(path.get("relay_device", -1)))
     if not relays:
         raise RuntimeError("daemon relay plan did not include worker chunks")

@@ -28,6 +28,10 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--profile-on-start", action="store_true",
                    help="measure link bandwidth at startup and cache the profiles")
     p.add_argument("--profile-store", default=None, help="persist the profile cache in this JSON file")
+    p.add_argument("--gpus", default=None,
+                   help="comma-separated GPU indices the daemon may use (default: every GPU of the node)")
+    p.add_argument("--executor-workers", type=int, default=4,
+                   help="intents executed at once (a session's next intent queues behind its current one)")
     p.add_argument("--socket-path", default=None,
                    help="serve on this Unix socket instead of printing the daemon state")
     return p
@@ -41,7 +45,9 @@ def startup_config_from_args(args) -> DaemonStartupConfig:
         max_inflight_chunks_per_relay=args.max_inflight_chunks_per_relay,
         session_timeout_seconds=args.session_timeout_seconds,
         profile_max_age_seconds=args.profile_max_age_seconds, execute=args.execute,
-        profile_on_start=args.profile_on_start, profile_store_path=args.profile_store)
+        profile_on_start=args.profile_on_start, profile_store_path=args.profile_store,
+        devices=None if not args.gpus else tuple(int(x) for x in str(args.gpus).split(",") if x.strip()),
+        executor_workers=args.executor_workers)
 
 
 def main(argv=None) -> None:

@@ -40,6 +40,7 @@ from ..schema import (BufferRegistration, CleanupRequest, DaemonRequest, DaemonR
                       SchedulingDecision, Session, TERMINAL_STATES, TransferIntent, TransferReceipt,
                       TransferReservation, TransferStatus, TransferStatusState,
                       WorkerTransferAuthorization, WorkerTransferAuthorizationRequest, byte_ranges)
+from ..planner_types import assignment_bytes, assignment_chunk_count, assignment_has_chunks, assignment_spans
 from ..topology import TopologyProvider
 from .audit import build_audit_record
 from .wire import reserve_socket
@@ -1273,7 +1274,12 @@ class TurboBusDaemon:
         state = self._runtime_state(active_only=True)
         if exclude is not None:  # a transfer being re-planned does not wait on its own old paths
             state = state_without_transfer(state, str(exclude))
-        busy = busy_relays(state)
+        # A session's next intent in the same direction to the same target may
+        # queue behind its own running transfer on the relays that session
+        # already holds (the data plane runs them in submit order on those
+        # lanes); another tenant's active path still blocks.
+        dirs = {str(l.direction).lower() for l in leases}
+        busy = busy_relays(state, queue_behind=(session.session_id, session.target_gpu, dirs))
         for l in leases:
             if l.relay_device not in session.relay_gpus:
                 return "relay admission is delayed by session relay ownership"
@@ -1827,17 +1833,16 @@ class TurboBusDaemon:
                 if not isinstance(a, Mapping) or not isinstance(a.get("path"), Mapping):
                     continue
                 p = a["path"]
-                chunks = a.get("chunks", ()) or ()
-                nbytes = int(a.get("bytes", 0) or 0) or sum(int(c.get("bytes", 0) or 0) for c in chunks
-                                                           if isinstance(c, Mapping))
+                nchunks = assignment_chunk_count(a)
+                nbytes = int(a.get("bytes", 0) or 0) or assignment_bytes(a)
                 kind, dirn = str(p.get("kind", "unknown")), str(p.get("direction", "unknown"))
                 b = summ.setdefault(f"{dirn}:{kind}", {"path_count": 0, "chunk_count": 0, "bytes_total": 0})
                 b["path_count"] += 1
-                b["chunk_count"] += len(chunks)
+                b["chunk_count"] += nchunks
                 b["bytes_total"] += nbytes
                 recs.append({"transfer_id": tid, "kind": kind, "direction": dirn,
                              "target_device": p.get("target_device"), "relay_device": p.get("relay_device"),
-                             "bytes_total": nbytes, "chunk_count": len(chunks)})
+                             "bytes_total": nbytes, "chunk_count": nchunks, "session_id": d.session_id})
         return recs, summ
 
     def _discovery(self, inv, target: int | None, cands: tuple[int, ...]) -> dict[str, Any]:
@@ -1990,11 +1995,8 @@ def relay_ranges(plan, relay_gpu, direction: str) -> tuple[dict[str, int], ...]:
         raise ValueError("daemon plan has no authorized relay chunks")
     out = []
     for a, _p in _plan_chunks(plan, kind="relay", relays=relays, direction=str(direction).lower()):
-        for c in a.get("chunks", ()) or ():
-            if not isinstance(c, dict):
-                raise ValueError("transfer plan chunk must be an object")
-            out.append({"src_offset": int(c["src_offset"]), "dst_offset": int(c["dst_offset"]),
-                        "bytes": int(c["bytes"])})
+        for s, d, n in assignment_spans(a):
+            out.append({"src_offset": s, "dst_offset": d, "bytes": n})
     if not out:
         raise ValueError("daemon plan has no authorized relay chunks")
     return tuple(out)
@@ -2003,7 +2005,7 @@ def relay_ranges(plan, relay_gpu, direction: str) -> tuple[dict[str, int], ...]:
 def relay_devices(plan, direction: str) -> set[int]:
     return {int(p.get("relay_device", -1))
             for a, p in _plan_chunks(plan, kind="relay", relays=None, direction=str(direction).lower())
-            if a.get("chunks")}
+            if assignment_has_chunks(a)}
 
 
 def transfer_timing(rec: Mapping[str, Any], completed_at: float | None) -> dict[str, Any]:
@@ -2022,10 +2024,7 @@ def transfer_timing(rec: Mapping[str, Any], completed_at: float | None) -> dict[
 def ticket_ranges(plan, direction: str) -> tuple[dict[str, int], ...]:
     chunks = []
     for a, _p in _plan_chunks(plan, kind=None, relays=None, direction=str(direction).lower()):
-        for c in a.get("chunks", ()) or ():
-            if not isinstance(c, dict):
-                raise ValueError("transfer plan chunk must be an object")
-            chunks.append(c)
+        chunks.extend({"src_offset": s, "dst_offset": d, "bytes": n} for s, d, n in assignment_spans(a))
     if not chunks:
         raise ValueError("daemon plan has no authorized chunks")
     return byte_ranges(chunks)
@@ -2055,13 +2054,19 @@ def plan_targets(plan: Mapping[str, Any]) -> tuple[int, ...]:
     return tuple(sorted(out))
 
 
-def busy_relays(state: Mapping[str, Any]) -> set[int]:
+def busy_relays(state: Mapping[str, Any], queue_behind: tuple | None = None) -> set[int]:
     """GPUs whose PCIe link is in use: relays of active relay paths and the
     targets of active direct paths.  (GPUs inside the link-hold window are
-    only kept out of new plans; admission never waits on them.)"""
+    only kept out of new plans; admission never waits on them.)
+    ``queue_behind=(session_id, target, directions)`` leaves out the paths of
+    that session's own transfers to that target in those directions."""
     out: set[int] = set()
     for p in state.get("active_paths", ()) or ():
         if not isinstance(p, Mapping):
+            continue
+        if queue_behind is not None and p.get("session_id") == queue_behind[0] \
+                and p.get("target_device") is not None and int(p["target_device"]) == int(queue_behind[1]) \
+                and str(p.get("direction", "")).lower() in queue_behind[2]:
             continue
         kind = str(p.get("kind", "")).lower()
         if kind == "relay" and p.get("relay_device") is not None:

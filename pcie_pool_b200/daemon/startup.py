@@ -36,8 +36,18 @@ class DaemonStartupConfig:
     execute: bool = False            # attach the GPU executor (data plane in the daemon)
     profile_on_start: bool = False   # run the link probe and cache profiles at startup
     profile_store_path: str | None = None
+    # GPUs the daemon may discover, lend and drive (None: every GPU of the
+    # node); on a shared node the others are never queried or touched
+    devices: tuple[int, ...] | None = None
+    executor_workers: int = 4
 
     def __post_init__(self) -> None:
+        if self.devices is not None:
+            object.__setattr__(self, "devices", tuple(int(d) for d in self.devices))
+            if self.target_gpu is not None and int(self.target_gpu) not in self.devices:
+                raise ValueError("target_gpu must be one of the daemon's devices")
+        if int(self.executor_workers) < 1:
+            raise ValueError("executor_workers must be >= 1")
         if int(self.min_relay_count) < 0:
             raise ValueError("min_relay_count must be non-negative")
         if self.target_gpu is not None and int(self.target_gpu) < 0:
@@ -49,10 +59,10 @@ class DaemonStartupConfig:
             object.__setattr__(self, "target_gpu", int(self.target_gpu))
 
 
-def build_topology_provider(name: str) -> TopologyProvider:
+def build_topology_provider(name: str, devices=None) -> TopologyProvider:
     n = str(name).strip().lower().replace("_", "-")
     if n in ("cuda-nvml", "nvidia-smi", "nvml"):
-        return CudaNvmlTopologyProvider()
+        return CudaNvmlTopologyProvider(devices=devices)
     raise DaemonStartupError(f"unsupported topology provider: {name}")
 
 
@@ -88,7 +98,7 @@ def relay_candidates_for_policy(inventory: DaemonResourceInventory, config: Daem
 def create_production_daemon(config: DaemonStartupConfig, *,
                              topology_provider: TopologyProvider | None = None,
                              executor_factory: Callable[[], object] | None = None) -> TurboBusDaemon:
-    provider = topology_provider or build_topology_provider(config.topology_provider)
+    provider = topology_provider or build_topology_provider(config.topology_provider, config.devices)
     try:
         inventory = provider.snapshot()
     except TopologyDiscoveryError as exc:
@@ -99,7 +109,8 @@ def create_production_daemon(config: DaemonStartupConfig, *,
         if executor_factory is None:
             from .executor import EngineDataPlane, IntentExecutor
 
-            executor = IntentExecutor(EngineDataPlane(devices=[g.device_id for g in inventory.gpus]))
+            executor = IntentExecutor(EngineDataPlane(devices=[g.device_id for g in inventory.gpus]),
+                                      max_workers=int(config.executor_workers))
         else:
             executor = executor_factory()
     daemon = TurboBusDaemon(relays, max_sessions_per_relay=config.max_sessions_per_relay,

@@ -10,6 +10,8 @@ on the lane the plan chose.
 
 from __future__ import annotations
 
+from ..planner_types import assignment_chunks
+
 import ctypes
 import threading
 import time
@@ -88,7 +90,7 @@ class MockDataPlane:
             p = asg["path"]
             dev = int(p["target_device"]) if p["kind"] == "direct" else int(p["relay_device"])
             lanes.append((dev, p["kind"], [(int(c["src_offset"]), int(c["dst_offset"]), int(c["bytes"]))
-                                            for c in asg.get("chunks", []) or []]))
+                                            for c in assignment_chunks(asg)]))
         return self.run_lanes(ticket.direction, int(src.address), int(src.size_bytes),
                               int(dst.address), int(dst.size_bytes), lanes,
                               transfer_id=str(ticket.metadata.get("transfer_id", ticket.ticket_id)))
@@ -241,7 +243,7 @@ class MockWorkerExecutor:
         for a in plan["assignments"]:
             p = a["path"]
             dev = target if p["kind"] == "direct" else int(p["relay_device"])
-            lanes.append((dev, p["kind"], [(c["src_offset"], c["dst_offset"], c["bytes"]) for c in a["chunks"]]))
+            lanes.append((dev, p["kind"], [(c["src_offset"], c["dst_offset"], c["bytes"]) for c in assignment_chunks(a)]))
         src, sb, dst, db = ((resources.host_ptr, resources.host_bytes, resources.device_ptr, resources.device_bytes)
                             if h2d else
                             (resources.device_ptr, resources.device_bytes, resources.host_ptr, resources.host_bytes))

@@ -49,7 +49,10 @@ def make_lane(device: int, chunks: Iterable, **extra) -> Lane:
 
 
 def lanes_from_plan(plan: Mapping, target: int) -> list[Lane]:
-    """Convert a reference-format plan dict into engine lanes."""
+    """Convert a plan dict (chunk-list or compact chunk-run form) into engine
+    lanes; runs expand with vector arithmetic."""
+    from ..planner_types import assignment_arrays, assignment_has_chunks
+
     lanes: list[Lane] = []
     for asg in plan.get("assignments", []) or []:
         path = asg["path"]
@@ -57,9 +60,9 @@ def lanes_from_plan(plan: Mapping, target: int) -> list[Lane]:
             raise ValueError("plan contains a disabled path")
         kind = str(path.get("kind", "direct"))
         dev = target if kind == "direct" else int(path["relay_device"])
-        chunks = asg.get("chunks", []) or []
-        if chunks:
-            lanes.append(make_lane(dev, chunks))
+        if assignment_has_chunks(asg):
+            src, dst, nbytes = assignment_arrays(asg)
+            lanes.append(Lane(dev, src, dst, nbytes))
     return lanes
 
 

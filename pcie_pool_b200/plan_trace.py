@@ -16,7 +16,7 @@ from collections.abc import Mapping
 from typing import Any
 
 from .planner_types import (PlannerChunk, PlannerPath, PlannerPathAssignment,
-                            PlannerTransferPlan)
+                            PlannerTransferPlan, assignment_chunks, expand_plan)
 
 TRACE_FORMAT = "pcie_pool_b200.plan_trace.v1"
 
@@ -25,18 +25,20 @@ _PATH_KEYS = ("kind", "direction", "target_device", "relay_device", "h2d_bw_gbps
 
 
 def transfer_plan_to_dict(plan) -> dict:
+    """The plan in the reference's chunk-list form (compact chunk runs are
+    expanded, so files written from it read the same in both projects)."""
     if isinstance(plan, Mapping):
-        return dict(plan)
+        return expand_plan(plan)
     as_dict = getattr(plan, "as_dict", None)
     if callable(as_dict):
         out = as_dict()
         if isinstance(out, dict):
-            return out
+            return expand_plan(out)
     assignments = []
     for asg in plan.assignments:
         path = asg.path
         chunks = [{"src_offset": int(c.src_offset), "dst_offset": int(c.dst_offset),
-                   "bytes": int(c.bytes)} for c in asg.chunks]
+                   "bytes": int(c.bytes)} for c in asg.chunk_list()]
         assignments.append({
             "path": {k: getattr(path, k) for k in _PATH_KEYS},
             "chunks": chunks,
@@ -61,7 +63,7 @@ def plan_from_dict(data: Mapping[str, Any]) -> PlannerTransferPlan:
             effective_bw_gbps=float(p.get("effective_bw_gbps", 0.0) or 0.0),
             enabled=bool(p.get("enabled", True)), fabric_kind=p.get("fabric_kind"))
         chunks = tuple(PlannerChunk(int(c["src_offset"]), int(c["dst_offset"]), int(c["bytes"]),
-                                    c.get("relay_device")) for c in asg.get("chunks", []) or [])
+                                    c.get("relay_device")) for c in assignment_chunks(asg))
         assignments.append(PlannerPathAssignment(path, chunks))
     return PlannerTransferPlan(int(data.get("total_bytes", 0)),
                                int(data.get("chunk_bytes", 16 << 20)), tuple(assignments))
@@ -75,7 +77,7 @@ def validate_plan_dict(data: Mapping[str, Any]) -> None:
         if not asg.get("path", {}).get("enabled", True):
             raise ValueError("transfer plan contains a disabled path")
         n = 0
-        for c in asg.get("chunks", []) or []:
+        for c in assignment_chunks(asg):
             if int(c["bytes"]) <= 0 or int(c["src_offset"]) < 0 or int(c["dst_offset"]) < 0:
                 raise ValueError("plan chunk offsets must be non-negative and bytes positive")
             n += int(c["bytes"])

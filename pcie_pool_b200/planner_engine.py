@@ -72,6 +72,8 @@ class PlannerEngine:
     def plan(self, total_bytes: int, chunk_bytes: int, profile,
              mode: TransferMode | str = TransferMode.POOL, *,
              direction: str = "h2d") -> PlannerTransferPlan:
+        import numpy as np
+
         total = max(0, int(total_bytes))
         if total == 0:
             return PlannerTransferPlan()
@@ -79,31 +81,34 @@ class PlannerEngine:
         if chunk <= 0:
             raise ValueError("chunk_bytes must be greater than zero")
         chunk = self._aligned_chunk(chunk)
-        chunks = [PlannerChunk(o, o, min(chunk, total - o)) for o in range(0, total, chunk)]
-        return self._finish(chunks, total, chunk, profile, mode, direction)
+        offs = np.arange(0, total, chunk, dtype=np.int64)
+        return self._finish(offs, offs, np.minimum(chunk, total - offs), total, chunk, profile, mode,
+                            direction)
 
     def plan_ranges(self, ranges: Iterable, chunk_bytes: int, profile,
                     mode: TransferMode | str = TransferMode.POOL, *,
                     direction: str = "h2d") -> PlannerTransferPlan:
+        import numpy as np
+
         chunk = int(chunk_bytes)
         if chunk <= 0:
             raise ValueError("chunk_bytes must be greater than zero")
         chunk = self._aligned_chunk(chunk)
-        chunks: list[PlannerChunk] = []
+        srcs, dsts, sizes = [], [], []
         total = 0
         for item in ranges:
             r = _range_tuple(item)
             if r[2] <= 0:
                 continue
             total += r[2]
-            done = 0
-            while done < r[2]:
-                n = min(chunk, r[2] - done)
-                chunks.append(PlannerChunk(r[0] + done, r[1] + done, n))
-                done += n
-        if not chunks:
+            o = np.arange(0, r[2], chunk, dtype=np.int64)
+            srcs.append(o + r[0])
+            dsts.append(o + r[1])
+            sizes.append(np.minimum(chunk, r[2] - o))
+        if not srcs:
             return PlannerTransferPlan()
-        return self._finish(chunks, total, chunk, profile, mode, direction)
+        return self._finish(np.concatenate(srcs), np.concatenate(dsts), np.concatenate(sizes), total, chunk,
+                            profile, mode, direction)
 
     def auto_chunk_bytes(self, total_bytes: int, profile, *, direction: str = "h2d",
                          candidates: Sequence[int] = CHUNK_CANDIDATES,
@@ -172,30 +177,41 @@ class PlannerEngine:
         a = self.options.align_bytes
         return chunk if a <= 1 else max(a, (chunk // a) * a)
 
-    def _finish(self, chunks: list[PlannerChunk], total: int, chunk: int, profile, mode,
+    def _finish(self, src, dst, sizes, total: int, chunk: int, profile, mode,
                 direction: str) -> PlannerTransferPlan:
+        import numpy as np
+
         mode = TransferMode(mode)
         if mode is TransferMode.AUTO:
             mode = TransferMode.POOL
-        if mode is TransferMode.POOL and len(chunks) < self.options.min_chunks_for_relay:
+        if mode is TransferMode.POOL and sizes.size < self.options.min_chunks_for_relay:
             mode = TransferMode.DIRECT
         paths = self.build_paths(profile, mode, direction)
         if not paths:
             raise RuntimeError("no enabled transfer path is available")
         if sum(p.effective_bw_gbps for p in paths) <= 0.0:
             raise RuntimeError("enabled paths have zero effective bandwidth")
-        idx = self._assign([c.bytes for c in chunks], paths)
+        idx = np.asarray(self._assign(sizes, paths), dtype=np.int64)
+        out = []
         if self.options.layout == "blocked":
-            counts = [0] * len(paths)
-            for i in idx:
-                counts[i] += 1
-            idx = [i for i, n in enumerate(counts) for _ in range(n)]
-        per: list[list[PlannerChunk]] = [[] for _ in paths]
-        for c, i in zip(chunks, idx):
-            per[i].append(c)
-        return PlannerTransferPlan(
-            total_bytes=int(total), chunk_bytes=int(chunk),
-            assignments=tuple(PlannerPathAssignment(p, tuple(cs)) for p, cs in zip(paths, per) if cs))
+            # each lane takes one contiguous slice of the chunk sequence, kept
+            # as runs (one per lane unless a range boundary splits it)
+            counts = np.bincount(idx, minlength=len(paths))
+            start = 0
+            for p, n in zip(paths, counts):
+                n = int(n)
+                if n:
+                    out.append(PlannerPathAssignment(p, runs=_runs(src[start:start + n], dst[start:start + n],
+                                                                   sizes[start:start + n], chunk)))
+                start += n
+        else:
+            for i, p in enumerate(paths):
+                sel = np.flatnonzero(idx == i)
+                if sel.size:
+                    out.append(PlannerPathAssignment(p, tuple(
+                        PlannerChunk(s_, d_, n_) for s_, d_, n_ in
+                        zip(src[sel].tolist(), dst[sel].tolist(), sizes[sel].tolist()))))
+        return PlannerTransferPlan(total_bytes=int(total), chunk_bytes=int(chunk), assignments=tuple(out))
 
     def _lane_model(self, paths: Sequence[PlannerPath]) -> tuple[list[float], list[float]]:
         o = self.options
@@ -213,8 +229,12 @@ class PlannerEngine:
         lat = [float(o.lane_latency_s.get(p.lane_device, default_lat)) for p in paths]
         return bw, lat
 
-    def _assign(self, sizes: list[int], paths: Sequence[PlannerPath]) -> list[int]:
+    def _assign(self, sizes, paths: Sequence[PlannerPath]):
+        import numpy as np
+
         policy = self.options.policy
+        if len(paths) == 1:
+            return np.zeros(len(sizes), dtype=np.int64)
         if policy == "legacy":
             bw = [max(p.effective_bw_gbps, 1e-12) for p in paths]
             lat: list[float] = []
@@ -222,11 +242,26 @@ class PlannerEngine:
             bw, lat = self._lane_model(paths)
         C = _native_planner()
         if C is None:
-            return assign_python(sizes, bw, lat, policy)
-        import numpy as np
-
+            return assign_python([int(x) for x in sizes], bw, lat, policy)
         pol = C.POLICY_LEGACY if policy == "legacy" else C.POLICY_EARLIEST_FINISH
-        return [int(i) for i in C.assign_chunks(np.asarray(sizes, dtype=np.uint64), bw, lat, pol)]
+        return np.asarray(C.assign_chunks(np.asarray(sizes, dtype=np.uint64), bw, lat, pol), dtype=np.int64)
+
+
+def _runs(src, dst, sizes, chunk: int) -> tuple[tuple[int, int, int, int], ...]:
+    """Runs of a contiguous slice of the chunk sequence: a new run starts
+    where a chunk is not contiguous with the previous one on either side, or
+    after a chunk shorter than ``chunk`` (a range's tail)."""
+    import numpy as np
+
+    if len(sizes) == 0:
+        return ()
+    brk = np.flatnonzero((src[1:] != src[:-1] + sizes[:-1]) | (dst[1:] != dst[:-1] + sizes[:-1])
+                         | (sizes[:-1] != chunk)) + 1
+    starts = np.concatenate(([0], brk))
+    ends = np.concatenate((brk, [len(sizes)]))
+    csum = np.concatenate(([0], np.cumsum(sizes)))
+    return tuple((int(src[a]), int(dst[a]), int(csum[b] - csum[a]), int(chunk))
+                 for a, b in zip(starts.tolist(), ends.tolist()))
 
 
 def _native_planner():

@@ -13,6 +13,8 @@
 
 from __future__ import annotations
 
+from .planner_types import assignment_chunks
+
 import json
 import time
 from dataclasses import dataclass, field
@@ -193,7 +195,7 @@ def plan_to_lanes(plan, target: int, *, source_bytes: int | None = None,
         if kind not in ("direct", "relay"):
             raise ValueError(f"unsupported transfer plan path: {kind}")
         chunks = []
-        for c in asg.get("chunks", []) or []:
+        for c in assignment_chunks(asg):
             s, d, n = int(c.get("src_offset", 0)), int(c.get("dst_offset", 0)), int(c.get("bytes", 0))
             if s < 0 or d < 0 or n <= 0:
                 raise ValueError("transfer plan chunk offsets must be non-negative and bytes positive")

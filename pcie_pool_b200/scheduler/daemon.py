@@ -19,7 +19,7 @@ from dataclasses import dataclass
 from collections.abc import Mapping
 from typing import Callable
 
-from ..planner_engine import PlannerEngine
+from ..planner_engine import PlannerEngine, PlannerEngineOptions
 from ..planner_types import PlannerLease, PlannerStats, PlannerTransferPlan
 from ..schema import (RelayQuota, SchedulingDecision, SchedulingDecisionState, Session, TransferMode,
                       WorkloadKind)
@@ -65,7 +65,9 @@ class DaemonScheduler:
                  lease_id_factory: Callable[[], str] | None = None,
                  decision_id_factory: Callable[[], str] | None = None,
                  lease_seconds: float = LEASE_SECONDS) -> None:
-        self._planner = planner or PlannerEngine()
+        # Blocked layout: each lane takes one contiguous span (host-sequential
+        # reads per lane) and the plan carries one chunk run per lane.
+        self._planner = planner or PlannerEngine(PlannerEngineOptions(layout="blocked"))
         self._lease_id = lease_id_factory or (lambda: str(uuid.uuid4()))
         self._decision_id = decision_id_factory or (lambda: str(uuid.uuid4()))
         self._lease_seconds = max(0.0, float(lease_seconds))
@@ -183,8 +185,8 @@ class DaemonScheduler:
 
     def _leases(self, plan: PlannerTransferPlan, session: Session, quotas, direction, now, job_id,
                 defer) -> tuple[tuple[PlannerLease, ...], str | None]:
-        specs = [(int(a.path.relay_device), len(a.chunks), a.bytes)
-                 for a in plan.assignments if a.path.kind == "relay" and a.chunks]
+        specs = [(int(a.path.relay_device), a.chunk_count, a.bytes)
+                 for a in plan.assignments if a.path.kind == "relay" and a.chunk_count]
         if not specs:
             return (), None
         if not defer and session.active_chunks + sum(s[1] for s in specs) > session.max_inflight_chunks:
@@ -231,11 +233,11 @@ def plan_stats(plan: PlannerTransferPlan, *, requested_mode: TransferMode,
     for a in plan.assignments:
         if a.path.kind == "relay":
             r_b += a.bytes
-            r_c += len(a.chunks)
+            r_c += a.chunk_count
             r_p += 1
         else:
             d_b += a.bytes
-            d_c += len(a.chunks)
+            d_c += a.chunk_count
     return PlannerStats(bytes=int(plan.total_bytes), direct_bytes=d_b, relay_bytes=r_b,
                         direct_chunks=d_c, relay_chunks=r_c, path_count=len(plan.assignments),
                         relay_path_count=r_p, fallback_reason=fallback_reason,
@@ -245,7 +247,7 @@ def plan_stats(plan: PlannerTransferPlan, *, requested_mode: TransferMode,
 def path_summary(plan: PlannerTransferPlan) -> tuple[dict[str, object], ...]:
     return tuple({"kind": a.path.kind, "direction": a.path.direction,
                   "target_device": a.path.target_device, "relay_device": a.path.relay_device,
-                  "bytes": a.bytes, "chunk_count": len(a.chunks)} for a in plan.assignments)
+                  "bytes": a.bytes, "chunk_count": a.chunk_count} for a in plan.assignments)
 
 
 def runtime_state_metadata(state: Mapping[str, object] | None) -> dict[str, object]:

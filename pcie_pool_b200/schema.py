@@ -750,10 +750,16 @@ def check_plan_chunk_bounds(plan: Mapping[str, Any], src_size: int, dst_size: in
     for asg in plan.get("assignments", ()) or ():
         if not isinstance(asg, Mapping):
             raise ValueError("daemon plan assignment must be a mapping")
-        for ch in asg.get("chunks", ()) or ():
-            if not isinstance(ch, Mapping):
+        runs = asg.get("chunk_runs")
+        spans = ([(r[0], r[1], r[2]) for r in runs if isinstance(r, (list, tuple)) and len(r) == 4]
+                 if runs else asg.get("chunks", ()) or ())
+        if runs and len(spans) != len(runs):
+            raise ValueError("daemon plan chunk run must be [src_offset, dst_offset, bytes, chunk_bytes]")
+        for ch in spans:
+            if not isinstance(ch, (Mapping, tuple)):
                 raise ValueError("daemon plan chunk must be a mapping")
-            s, d, n = int(ch["src_offset"]), int(ch["dst_offset"]), int(ch["bytes"])
+            s, d, n = ((int(ch["src_offset"]), int(ch["dst_offset"]), int(ch["bytes"])) if isinstance(ch, Mapping)
+                       else (int(ch[0]), int(ch[1]), int(ch[2])))
             if s < 0 or d < 0:
                 raise ValueError("daemon plan chunk offsets must be non-negative")
             if n <= 0:

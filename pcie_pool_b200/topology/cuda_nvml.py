@@ -124,13 +124,15 @@ class NvmlProbe:
     """NVML probe.  ``lib`` may be injected (tests pass a fake with the same
     function names); otherwise ``libnvidia-ml.so.1`` is loaded."""
 
-    def __init__(self, lib=None) -> None:
+    def __init__(self, lib=None, devices: Sequence[int] | None = None) -> None:
         if lib is None:
             try:
                 lib = ctypes.CDLL("libnvidia-ml.so.1")
             except OSError as exc:
                 raise TopologyDiscoveryError(f"NVML unavailable: {exc}") from exc
         self._lib = lib
+        # only these GPU indices are queried (None: every GPU of the node)
+        self.devices = None if devices is None else tuple(int(d) for d in devices)
         rc = self._lib.nvmlInit_v2()
         if rc != 0:
             raise TopologyDiscoveryError(f"nvmlInit failed with {rc}")
@@ -151,7 +153,8 @@ class NvmlProbe:
 
     def query_gpu_inventory(self) -> Sequence[Mapping[str, object]]:
         rows = []
-        for i in range(self.device_count()):
+        n = self.device_count()
+        for i in (range(n) if self.devices is None else [d for d in self.devices if 0 <= d < n]):
             h = self._handle(i)
             row: dict[str, object] = {"device_id": i}
             buf = ctypes.create_string_buffer(96)
@@ -311,10 +314,14 @@ def fabric_links_from_matrix(gpu_ids: set[int], lines: Sequence[str]) -> tuple[F
 class CudaNvmlTopologyProvider(TopologyProvider):
     def __init__(self, probe: CudaTopologyProbe | None = None, *, cache_max_age_seconds: float = 30.0,
                  now: Callable[[], float] | None = None, sysfs_root: str | None = "/sys",
-                 fabric_probe: CudaTopologyProbe | None = None) -> None:
+                 fabric_probe: CudaTopologyProbe | None = None,
+                 devices: Sequence[int] | None = None) -> None:
+        """``devices`` limits discovery to those GPU indices: a daemon that
+        may only use part of a shared node queries nothing about the rest."""
+        self._devices = None if devices is None else frozenset(int(d) for d in devices)
         if probe is None:
             try:
-                probe = NvmlProbe()
+                probe = NvmlProbe(devices=devices)
             except TopologyDiscoveryError:
                 probe = NvidiaSmiProbe()
         self._probe = probe
@@ -331,6 +338,8 @@ class CudaNvmlTopologyProvider(TopologyProvider):
                 and now - self._cached.discovered_at <= self._max_age:
             return self._cached
         rows = list(self._probe.query_gpu_inventory())
+        if self._devices is not None:
+            rows = [r for r in rows if int(r.get("device_id", r.get("index", -1))) in self._devices]
         if not rows:
             raise TopologyDiscoveryError("cuda-nvml topology discovery found no GPUs")
         gpus = tuple(_gpu_record(r) for r in rows)

@@ -13,6 +13,8 @@ reservation and relay quota was released (turbobus/verification.py:74-424,
 
 from __future__ import annotations
 
+from .planner_types import assignment_bytes, assignment_chunk_count
+
 import argparse
 import json
 import multiprocessing
@@ -133,9 +135,8 @@ def _plan_split(plan: Mapping[str, object], kind: str) -> tuple[int, int]:
     b = c = 0
     for a in (plan.get("assignments") or ()):
         if str(a.get("path", {}).get("kind", "")).lower() == kind:
-            for ch in a.get("chunks") or ():
-                b += int(ch["bytes"])
-                c += 1
+            b += assignment_bytes(a)
+            c += assignment_chunk_count(a)
     return b, c
 
 

@@ -11,6 +11,8 @@ label ``pool_h2d``/``relay_d2h``/... and per-lane measured stats.
 
 from __future__ import annotations
 
+from ..planner_types import assignment_chunks
+
 import threading
 from typing import Any
 
@@ -46,7 +48,7 @@ def scoped_plan(request: WorkerTransferRequest, target: int) -> dict[str, Any]:
             p["relay_device"] = -1
         p["enabled"] = True
         chunks = [{"src_offset": int(c["src_offset"]), "dst_offset": int(c["dst_offset"]), "bytes": int(c["bytes"])}
-                  for c in a.get("chunks", ()) or ()]
+                  for c in assignment_chunks(a)]
         if not chunks:
             continue
         n = sum(c["bytes"] for c in chunks)

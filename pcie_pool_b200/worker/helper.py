@@ -14,6 +14,8 @@ plan (direct and relay lanes) on the worker's persistent engine.
 
 from __future__ import annotations
 
+from ..planner_types import assignment_chunks
+
 from dataclasses import asdict, dataclass, field
 from enum import Enum
 from collections.abc import Mapping
@@ -58,9 +60,11 @@ def _assignments(plan: Mapping[str, Any]):
 
 
 def _chunks(a: Mapping[str, Any]):
-    for c in a.get("chunks", ()) or ():
-        if not isinstance(c, Mapping):
-            raise ValueError("daemon plan chunk must be an object")
+    try:
+        chunks = assignment_chunks(a)
+    except ValueError as exc:
+        raise ValueError(f"daemon plan chunk is invalid: {exc}") from None
+    for c in chunks:
         yield {"src_offset": int(c["src_offset"]), "dst_offset": int(c["dst_offset"]), "bytes": int(c["bytes"])}
 
 

@@ -11,6 +11,7 @@ from pcie_pool_b200 import TransferIntent, TransferStatusState, TurboBusClient
 from pcie_pool_b200.daemon import InProcessDaemonClient, IntentExecutor, TurboBusDaemon
 from pcie_pool_b200.mock import MockDataPlane, MockWorld, chunk_lane_map
 from pcie_pool_b200.topology import StaticTopologyProvider
+from pcie_pool_b200.planner_types import assignment_chunks
 
 MiB = 1 << 20
 
@@ -86,7 +87,7 @@ def test_plan_assigns_each_chunk_to_exactly_one_lane(node):
     resp = dc.plan_transfer(sid, 256 * MiB, 4 * MiB)
     assert resp.ok, resp.error
     plan = resp.payload["plan"]
-    offs = [c["src_offset"] for a in plan["assignments"] for c in a["chunks"]]
+    offs = [c["src_offset"] for a in plan["assignments"] for c in assignment_chunks(a)]
     assert sorted(offs) == list(range(0, 256 * MiB, 4 * MiB))
     assert len({a["path"]["relay_device"] for a in plan["assignments"]}) == 4
 

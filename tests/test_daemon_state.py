@@ -14,6 +14,7 @@ from pcie_pool_b200.daemon import InProcessDaemonClient, TurboBusDaemon
 from pcie_pool_b200.schema import PeerIdentity, TransferIntent, WorkerTransferAuthorizationRequest
 from pcie_pool_b200.topology import StaticTopologyProvider
 from pcie_pool_b200.transfer import TransferRequest
+from pcie_pool_b200.planner_types import assignment_chunks
 
 MiB = 1 << 20
 
@@ -133,7 +134,7 @@ def test_pool_plan_covers_every_byte_and_leases_each_relay():
     r = plan(d, sid)
     assert r.ok, r.error
     p = r.payload
-    chunks = [c for a in p["plan"]["assignments"] for c in a["chunks"]]
+    chunks = [c for a in p["plan"]["assignments"] for c in assignment_chunks(a)]
     assert sum(c["bytes"] for c in chunks) == 64 * MiB
     assert sorted(t["relay_gpu"] for t in p["lease_tokens"]) == [1, 2, 3]
     assert p["plan_generation"] == 1 and p["transfer_id"]
@@ -154,7 +155,7 @@ def test_session_chunk_quota_bounds_relay_chunks():
     sid = setup_job(d, inflight=2)
     r = plan(d, sid, total=256 * MiB, chunk=16 * MiB)
     assert r.ok
-    relay_chunks = sum(len(a["chunks"]) for a in r.payload["plan"]["assignments"] if a["path"]["kind"] == "relay")
+    relay_chunks = sum(len(assignment_chunks(a)) for a in r.payload["plan"]["assignments"] if a["path"]["kind"] == "relay")
     assert relay_chunks <= 2 or not r.payload["lease_tokens"]
 
 

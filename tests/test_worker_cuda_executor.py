@@ -23,6 +23,7 @@ from pcie_pool_b200.schema import WorkerTransferAuthorizationRequest
 from pcie_pool_b200.transfer import TransferRequest
 from pcie_pool_b200.worker.cuda_executor import CudaWorkerExecutor, scoped_plan
 from pcie_pool_b200.worker.helper import WorkerTransferState
+from pcie_pool_b200.planner_types import assignment_chunks
 
 
 @pytest.fixture
@@ -57,7 +58,7 @@ def plan_split(p) -> dict[int, int]:
     out: dict[int, int] = {}
     for a in p["plan"]["assignments"]:
         dev = 0 if a["path"]["kind"] == "direct" else a["path"]["relay_device"]
-        out[dev] = out.get(dev, 0) + sum(c["bytes"] for c in a["chunks"])
+        out[dev] = out.get(dev, 0) + sum(c["bytes"] for c in assignment_chunks(a))
     return out
 
 

@@ -18,6 +18,7 @@ import pytest
 from test_worker_lifecycle import MiB, N, Rig
 
 from pcie_pool_b200.daemon import InProcessDaemonClient
+from pcie_pool_b200.planner_types import assignment_chunks
 from pcie_pool_b200.schema import BufferRegistration, DaemonResponse, WorkerTransferAuthorizationRequest
 from pcie_pool_b200.transfer import TransferRequest
 from pcie_pool_b200.worker import (WorkerDataPlaneResourceBinder, WorkerServiceEndpoint,
@@ -51,7 +52,7 @@ def authorized(rig, **over):
 def relay_chunks(plan, relay=None):
     """(src, dst, bytes) of the plan's relay chunks, optionally of one relay."""
     return [triple(c) for a in plan["assignments"] if a["path"]["kind"] == "relay"
-            and (relay is None or a["path"]["relay_device"] == relay) for c in a["chunks"]]
+            and (relay is None or a["path"]["relay_device"] == relay) for c in assignment_chunks(a)]
 
 
 def triple(c):
@@ -210,10 +211,20 @@ def _first_relay_path(plan):
     return next(a for a in plan["assignments"] if a["path"]["kind"] == "relay")
 
 
+def _move_first_chunk(plan, key, value):
+    """Point the first relay chunk (or chunk run) somewhere else; daemon plans
+    carry compact chunk runs [src, dst, bytes, chunk]."""
+    a = _first_relay_path(plan)
+    if a.get("chunk_runs"):
+        a["chunk_runs"][0][0 if key == "src_offset" else 1] = value
+    else:
+        a["chunks"][0][key] = value
+
+
 @pytest.mark.parametrize("edit,msg", [
     (lambda pl: pl.update(assignments=[]), "relay path"),
-    (lambda pl: _first_relay_path(pl)["chunks"][0].update(dst_offset=N), "exceeds dst buffer size"),
-    (lambda pl: _first_relay_path(pl)["chunks"][0].update(src_offset=N), "exceeds src buffer size"),
+    (lambda pl: _move_first_chunk(pl, "dst_offset", N), "exceeds dst buffer size"),
+    (lambda pl: _move_first_chunk(pl, "src_offset", N), "exceeds src buffer size"),
     (lambda pl: pl.update(total_bytes=pl["total_bytes"] + MiB), "total"),
     (lambda pl: [a["path"].update(target_device=3) for a in pl["assignments"]], "target"),
     (lambda pl: _first_relay_path(pl)["path"].update(enabled=False), "disabled"),

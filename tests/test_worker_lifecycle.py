@@ -17,6 +17,7 @@ import pytest
 from pcie_pool_b200.client import CudaIpcDeviceBuffer, SharedPinnedCpuBuffer
 from pcie_pool_b200.daemon import InProcessDaemonClient, TurboBusDaemon
 from pcie_pool_b200.mock import FaultPlan, MockCudaBackend, MockDataPlane, MockWorkerExecutor, MockWorld
+from pcie_pool_b200.planner_types import assignment_chunks
 from pcie_pool_b200.schema import DaemonResponse, WorkerTransferAuthorizationRequest
 from pcie_pool_b200.topology import StaticTopologyProvider
 from pcie_pool_b200.transfer import TransferRequest
@@ -104,7 +105,7 @@ def test_complete_lifecycle_moves_bytes_reports_and_releases(rig):
     lc = rig.service.handle_lifecycle(req)
     assert lc.final_state == "complete" and lc.error is None
     assert lc.result.bytes_completed == N and rig.status(p["transfer_id"]) == "complete"
-    relay_ranges = [c for a in p["plan"]["assignments"] if a["path"]["kind"] == "relay" for c in a["chunks"]]
+    relay_ranges = [c for a in p["plan"]["assignments"] if a["path"]["kind"] == "relay" for c in assignment_chunks(a)]
     for c in relay_ranges:  # every relayed range landed
         s, b = c["dst_offset"], c["bytes"]
         assert np.array_equal(rig.dev_arr[s:s + b], rig.host.numpy()[c["src_offset"]:c["src_offset"] + b])
