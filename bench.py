@@ -47,6 +47,7 @@ def parse_args(argv=None):
     p.add_argument("--no-checksum", action="store_true", help="skip the fused per-chunk checksum")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--json-out", default="")
+    p.add_argument("--reference-e2e-child", action="store_true", help=argparse.SUPPRESS)
     return p.parse_args(argv)
 
 
@@ -250,11 +251,12 @@ def reference_e2e(args, ref_root: Path, host_np, dev, profile, relays) -> dict:
     cpu = None
     try:
         procs.append(subprocess.Popen(
-            # --allow-missing-fabric: the reference's own switch for a node
-            # whose discovery reports no GPU-GPU links (a 1-GPU run)
+            # the reference's own switches for a node whose discovery reports
+            # no GPU-GPU links or PCIe paths (its parser misses them on some
+            # boxes); they only relax its startup check
             [sys.executable, "-m", "turbobus.daemon", "--target-gpu", "0", "--min-relays", "0",
-             "--max-inflight-chunks-per-relay", "4096", "--socket-path", dsock]
-            + ([] if relays else ["--allow-missing-fabric"]), env=env))
+             "--max-inflight-chunks-per-relay", "4096", "--socket-path", dsock,
+             "--allow-missing-fabric", "--allow-missing-pcie"], env=env))
         wait_sock(dsock, procs[-1], "daemon")
         procs.append(subprocess.Popen(
             [sys.executable, "-m", "turbobus.worker", "--daemon-socket-path", dsock, "--socket-path", wsock],
@@ -400,17 +402,74 @@ def run_reference(args, dist: Dist) -> dict:
                            for r in profile.relays],
             },
         }
-        del rt
+        del rt, host_t, dev
+        torch.cuda.empty_cache()
         if not args.no_e2e and args.direction == "h2d":
-            try:
-                out["e2e"] = reference_e2e(args, ref_root, host_t.numpy(), dev, profile, relays)
-            except Exception as exc:  # noqa: BLE001 - reported in the JSON line
-                out["e2e"] = {"error": f"{type(exc).__name__}: {exc}"}
+            out["e2e"] = reference_e2e_isolated(args, ref_root)
     return out
+
+
+def reference_e2e_isolated(args, ref_root: Path) -> dict:
+    """Run ``reference_e2e`` in a child process (``faulthandler`` on): a
+    crash inside the reference's own stack then costs only the e2e figure,
+    reported with the child's exit status and the tail of its stack dump."""
+    import subprocess
+    import tempfile
+
+    fd, out_path = tempfile.mkstemp(prefix="ref-e2e-", suffix=".json")
+    os.close(fd)
+    cmd = [sys.executable, "-X", "faulthandler", str(ROOT / "bench.py"), "--impl", "reference",
+           "--reference-e2e-child", "--gpus", str(args.gpus), "--steps", str(args.steps), "--warmup",
+           str(args.warmup), "--bytes", str(args.bytes), "--chunk", str(args.chunk), "--json-out", out_path]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "LOCAL_WORLD_SIZE",
+                                                             "GROUP_RANK", "ROLE_RANK", "TORCHELASTIC_RUN_ID")}
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=1200, env=env)
+        text = Path(out_path).read_text() if os.path.getsize(out_path) else ""
+    except subprocess.TimeoutExpired:
+        return {"error": "reference e2e child timed out after 1200 s"}
+    finally:
+        try:
+            os.unlink(out_path)
+        except OSError:
+            pass
+    if r.returncode == 0 and text.strip():
+        return json.loads(text)
+    tail = [l for l in (r.stderr or "").splitlines() if l.strip()][-12:]
+    return {"error": f"reference e2e child exited with status {r.returncode}", "stderr_tail": tail}
+
+
+def reference_e2e_child(args) -> int:
+    """Child side of ``reference_e2e_isolated`` (one process, cuda:0)."""
+    ref_root = ROOT / "baseline" / "_ref"
+    sys.path.insert(0, str(ref_root))
+    import torch
+    from turbobus import runtime_engine
+    from turbobus.runtime_engine import RuntimeOptions
+
+    native = runtime_engine._turbobus
+    torch.cuda.set_device(0)
+    n = args.bytes
+    host_t = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    fill_random(host_t.numpy(), seed=1234)
+    dev = torch.empty(n, dtype=torch.uint8, device="cuda:0")
+    relays = list(range(1, args.gpus))
+    rt = native.Runtime(RuntimeOptions(chunk_bytes=args.chunk).to_native())
+    rt.init(0, relays)
+    profile = rt.profile(256 << 20, False)
+    try:
+        res = reference_e2e(args, ref_root, host_t.numpy(), dev, profile, relays)
+    except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+        res = {"error": f"{type(exc).__name__}: {exc}"}
+    del rt
+    Path(args.json_out).write_text(json.dumps(res))
+    return 0
 
 
 def main(argv=None) -> int:
     args = parse_args(argv)
+    if args.reference_e2e_child:
+        return reference_e2e_child(args)
     dist = Dist()
     if args.impl == "reference":
         res = run_reference(args, dist)

@@ -158,14 +158,17 @@ class TurboBusCPUBackingPool:
     pinned uint8 region of ``layers x lanes x blocks`` units; ``views`` are the
     per-layer slices (the reference's one-tensor-per-layer layout)."""
 
-    def __init__(self) -> None:
+    def __init__(self, shared: bool = False) -> None:
         self._free: dict[tuple, list[Any]] = {}
+        # shared: backings live in shared page-locked memory so a daemon
+        # process can map them (its data plane moves the bytes)
+        self.shared = bool(shared)
 
     def acquire(self, block_count: int, kv_caches: list[Any]) -> tuple[Any, bool]:
         sig = _signature(block_count, kv_caches)
         if self._free.get(sig):
             return self._free[sig].pop(), True
-        return self._allocate(block_count, kv_caches), False
+        return self._allocate(block_count, kv_caches, self.shared), False
 
     def release(self, block_count: int, kv_caches: list[Any], cpu_backings) -> None:
         self._free.setdefault(_signature(block_count, kv_caches), []).append(cpu_backings)
@@ -175,16 +178,23 @@ class TurboBusCPUBackingPool:
         self.release(prefix.block_count, kv_caches, prefix.cpu_backings)
 
     @staticmethod
-    def _allocate(block_count: int, kv_caches: list[Any]):
+    def _allocate(block_count: int, kv_caches: list[Any], shared: bool = False):
         import torch
 
         per = [max(1, block_count * _lanes_per_layer(kv)) * _unit_bytes(kv) for kv in kv_caches]
-        whole = torch.empty(sum(per), dtype=torch.uint8, pin_memory=torch.cuda.is_available())
+        shm = None
+        if shared:
+            from ..client import SharedPinnedCpuBuffer
+
+            shm = SharedPinnedCpuBuffer.allocate(f"kv-backing-{id(per)}", "vllm-kv", sum(per))
+            whole = torch.from_numpy(shm.numpy())
+        else:
+            whole = torch.empty(sum(per), dtype=torch.uint8, pin_memory=torch.cuda.is_available())
         views, off = [], 0
         for n in per:
             views.append(whole[off:off + n])
             off += n
-        return {"tensor": whole, "views": views}
+        return {"tensor": whole, "views": views, "shm": shm}
 
 
 class TurboBusConnectorMetadata(KVConnectorMetadata):
@@ -397,19 +407,50 @@ class TurboBusConnector(KVConnectorBase_V1, SupportsHMA):
         return [kv for _, kv in self.state.kv_caches.items()]
 
     def _engine_offloader(self):
+        """The fused KV data path, driven through the node daemon: each save
+        or restore is one intent with a gather / scatter landing spec, so the
+        relays it uses come from the daemon's leases.  With
+        ``turbobus.daemon_socket_path`` the daemon is the node's daemon
+        process (KV caches exported by CUDA IPC, backings in shared memory);
+        without it the worker runs a daemon of its own over the target and
+        ``turbobus.relay_gpus`` (same scheduler, leases and executor)."""
         if self._offloader is None:
-            from ..parallel.balance import LaneBalancer
-            from ..parallel.engine import PoolEngine
-            from .kv_offload import PagedKVOffloader
+            from .kv_offload import DaemonKVOffloader
 
             kvs = self._kv_list()
             target = int(kvs[0].device.index)
-            devs = [target, *[r for r in self.config.relay_gpus if r != target]]
-            eng = PoolEngine(devs, slot_bytes=max(self.config.chunk_bytes, 1 << 20), slots=3)
+            relays = [r for r in self.config.relay_gpus if r != target]
+            dc, client = self._node_daemon(target, relays)
+            sess = dc.register_session(target, relays, max_inflight_chunks=1 << 16)
+            if not sess.ok:
+                raise RuntimeError(f"daemon session registration failed: {sess.error}")
+            sid = sess.payload["session"]["session_id"]
+            r = dc.register_job(self.job_id, session_id=sid)
+            if not r.ok:
+                raise RuntimeError(f"daemon job registration failed: {r.error}")
             upc = max(1, self.config.chunk_bytes // _unit_bytes(kvs[0]))
-            self._offloader = PagedKVOffloader(eng, kvs, target, devs[1:], units_per_chunk=upc,
-                                               balancer=LaneBalancer())
+            self._offloader = DaemonKVOffloader(client, dc, session_id=sid, job_id=self.job_id, kv_caches=kvs,
+                                                units_per_chunk=upc, prefix=f"{self.job_id}-kv")
         return self._offloader
+
+    def _node_daemon(self, target: int, relays: list[int]):
+        from ..api import TurboBusClient
+
+        path = self.config.daemon_socket_path
+        if path and os.path.exists(path):
+            from ..daemon import TurboBusDaemonClient
+
+            dc = TurboBusDaemonClient(path, persistent=True)
+            self._backing_pool.shared = True
+            return dc, TurboBusClient(daemon=dc)
+        from ..e2e import build_inprocess_node, nominal_profile
+        from ..parallel.engine import PoolEngine
+
+        devs = [target, *relays]
+        eng = PoolEngine(devs, slot_bytes=max(self.config.chunk_bytes, 1 << 20), slots=3)
+        daemon, dc = build_inprocess_node(eng, devs, target, nominal_profile(target, relays) if relays else None)
+        self._node = daemon
+        return dc, TurboBusClient(daemon=dc)
 
     # ---- worker side: caches -----------------------------------------------------------------
     def register_kv_caches(self, kv_caches: dict[str, Any]) -> None:
@@ -557,9 +598,8 @@ class TurboBusConnector(KVConnectorBase_V1, SupportsHMA):
         n = min(len(r.block_ids), saved.block_count)
         ids = list(r.block_ids[:n])
         if saved.data_path == "engine":
-            host = saved.host["tensor"]
-            stats = self._engine_offloader().restore(ids, host.data_ptr(), host.numel(),
-                                                     span_blocks=saved.block_count)
+            host = saved.host.get("shm") or saved.host["tensor"]
+            stats = self._engine_offloader().restore(ids, host, span_blocks=saved.block_count)
             cuda_ms, nbytes = stats.cuda_ms, stats.bytes
         else:
             refs = make_vllm_layer_range_refs_from_ids(r.request_id, ids, self._kv_list())
@@ -610,11 +650,13 @@ class TurboBusConnector(KVConnectorBase_V1, SupportsHMA):
     def _save(self, r: TurboBusRequestMetadata) -> None:
         t0 = time.perf_counter()
         kvs = self._kv_list()
-        backing, reused = self._backing_pool.acquire(r.block_count, kvs)
         path = self.config.data_path
-        if path == "engine":
-            host = backing["tensor"]
-            st = self._engine_offloader().save(list(r.block_ids), host.data_ptr(), host.numel())
+        # the data path first: a daemon process needs shared backings
+        off = self._engine_offloader() if path == "engine" else None
+        backing, reused = self._backing_pool.acquire(r.block_count, kvs)
+        if off is not None:
+            host = backing.get("shm") or backing["tensor"]
+            st = off.save(list(r.block_ids), host)
             nbytes, cuda_ms, receipts, fallback = st.bytes, st.cuda_ms, "", ""
             ranges = st.units
         else:

@@ -71,7 +71,11 @@ class IntentExecutor:
         try:
             if src is None or dst is None:
                 raise RuntimeError("ticket buffers are no longer registered")
-            res = self.data_plane.execute(ticket, src, dst, intent)
+            extra = daemon.landing_buffers(intent) if hasattr(daemon, "landing_buffers") else {}
+            if extra:
+                res = self.data_plane.execute(ticket, src, dst, intent, buffers=extra)
+            else:
+                res = self.data_plane.execute(ticket, src, dst, intent)
         except Exception as exc:  # noqa: BLE001 - every data-plane error fails the transfer
             res = ExecutionResult(ok=False, bytes_completed=0,
                                   error=f"{type(exc).__name__}: {exc}",
@@ -155,8 +159,9 @@ class EngineDataPlane:
 
     # -- execution ------------------------------------------------------------------------------
     def execute(self, ticket: ExecutionTicket, src: BufferRegistration, dst: BufferRegistration,
-                intent: TransferIntent | None) -> ExecutionResult:
+                intent: TransferIntent | None, buffers: dict | None = None) -> ExecutionResult:
         from ..parallel.engine import D2H, H2D, Lane, lanes_from_plan
+        from .landing import LandingSpec, annotate_lanes, fp8_table, unit_addresses
 
         h2d = ticket.direction == "h2d"
         host_buf, dev_buf = (src, dst) if h2d else (dst, src)
@@ -166,13 +171,33 @@ class EngineDataPlane:
         lanes = lanes_from_plan(ticket.plan, target)
         eng = self.engine
         direction = H2D if h2d else D2H
+        # fused landing op named by the intent (validated by the daemon)
+        spec = LandingSpec.from_metadata(intent.metadata) if intent is not None else None
+        op_kw: dict = {}
+        if spec is not None and spec.op != "copy":
+            from .._native import native
+
+            C = native()
+            annotate_lanes(spec, lanes, h2d)
+            if spec.units_op:
+                regs = dict(buffers or {})
+                regs.setdefault(dev_buf.buffer_id, dev_buf)
+                missing = [b for b in spec.buffer_ids() if b not in regs]
+                if missing:
+                    raise RuntimeError(f"landing buffers are no longer registered: {missing}")
+                op_kw = {"op": C.OP_SCATTER_UNITS if h2d else C.OP_GATHER_UNITS, "unit_bytes": spec.unit_bytes,
+                         "unit_addrs": unit_addresses(spec, lambda b: self.device_pointer(regs[b]))}
+            else:
+                op_kw = {"op": C.OP_FP8_QUANT, "tensors": fp8_table(spec, dev_ptr)}
+            if spec.ctas_per_lane:
+                op_kw["ctas_per_lane"] = spec.ctas_per_lane
 
         def run(ls, drop=-1):
             kw = {"debug_drop_publish": drop} if drop >= 0 else {}
             if drop >= 0 and self.failover_timeout_s:
                 kw["timeout_s"] = self.failover_timeout_s
             return eng.run(direction, target, host_ptr, host_buf.size_bytes, dev_ptr, dev_buf.size_bytes, ls,
-                           checksum=self.checksum, **kw)
+                           checksum=self.checksum, **op_kw, **kw)
 
         drop, self.debug_drop_publish = self.debug_drop_publish, -1
         r = run(lanes, drop)

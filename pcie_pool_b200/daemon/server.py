@@ -43,6 +43,7 @@ from ..schema import (BufferRegistration, CleanupRequest, DaemonRequest, DaemonR
 from ..planner_types import assignment_bytes, assignment_chunk_count, assignment_has_chunks, assignment_spans
 from ..topology import TopologyProvider
 from .audit import build_audit_record
+from .landing import LandingSpec, validate_landing
 from .wire import reserve_socket
 
 ADMITTED = "admitted"
@@ -449,8 +450,15 @@ class TurboBusDaemon:
             return fail("intent must be a TransferIntent")
         try:
             chunk = intent_chunk_bytes(intent)
+            spec = LandingSpec.from_metadata(intent.metadata)
         except (TypeError, ValueError) as exc:
             return fail(str(exc))
+        if spec is not None and spec.op != "copy":
+            with self._lock:
+                try:
+                    self._validate_landing(intent, spec, chunk, peer_identity)
+                except ValueError as exc:
+                    return fail(str(exc))
         with self._lock:
             existing = self._st.intent_transfer.get(intent.intent_id)
             if existing is not None:
@@ -499,6 +507,37 @@ class TurboBusDaemon:
             if ticket is not None:
                 self._dispatch(tid, ticket)
             return resp
+
+    def _validate_landing(self, intent: TransferIntent, spec: LandingSpec, chunk: int, peer) -> None:
+        """A fused-op intent may only touch buffers its job registered: the
+        spec's kv buffers are checked for ownership (authenticated peer) and
+        every unit / tensor it addresses for bounds (daemon/landing.py)."""
+        S = self._st
+        h2d = intent.direction == "h2d"
+        host_id, dev_id = ((intent.source_buffer_id, intent.destination_buffer_id) if h2d
+                           else (intent.destination_buffer_id, intent.source_buffer_id))
+        host, dev = S.buffers.get(host_id), S.buffers.get(dev_id)
+        if host is None or dev is None:
+            raise ValueError("unknown buffer")
+        for bid in spec.buffer_ids():
+            self._peer_owns_buffer(bid, peer)
+        validate_landing(spec, direction=intent.direction, job_id=intent.job_id, device_buffer=dev,
+                         host_buffer=host, ranges=intent.ranges, total_bytes=intent.total_bytes,
+                         chunk_bytes=chunk, buffers=S.buffers)
+
+    def landing_buffers(self, intent: TransferIntent | None) -> dict[str, BufferRegistration]:
+        """Registrations of the extra device buffers a fused-op intent names
+        (the executor resolves their addresses)."""
+        if intent is None:
+            return {}
+        try:
+            spec = LandingSpec.from_metadata(intent.metadata)
+        except ValueError:
+            return {}
+        if spec is None:
+            return {}
+        with self._lock:
+            return {b: self._st.buffers[b] for b in spec.buffer_ids() if b in self._st.buffers}
 
     def wait_transfer_receipt(self, intent_id: str, timeout_seconds: float | None = None) -> DaemonResponse:
         iid = str(intent_id)

@@ -43,6 +43,16 @@ def build_inprocess_node(engine, devices, target: int = 0, profile: dict | None 
     return daemon, InProcessDaemonClient(daemon)
 
 
+def nominal_profile(target: int, relays, lane_gibps: float = 50.0, p2p_gibps: float = 700.0) -> dict:
+    """An even profile (every lane the same rate) for a daemon that has not
+    probed its links yet: the planner then splits evenly across the direct
+    lane and the relays; a probed profile replaces it."""
+    return {"target_device": int(target), "direct_h2d_bw_gbps": lane_gibps, "direct_d2h_bw_gbps": lane_gibps,
+            "relays": [{"relay_device": int(r), "target_device": int(target), "h2d_bw_gbps": lane_gibps,
+                        "d2h_bw_gbps": lane_gibps, "p2p_bw_gbps": p2p_gibps, "effective_bw_gbps": lane_gibps,
+                        "effective_d2h_bw_gbps": lane_gibps, "p2p_enabled": True} for r in relays]}
+
+
 def public_api_pooled_load(args, eng, host, dev, profile: dict | None = None, depth: int = 2) -> dict[str, Any]:
     import torch
 

@@ -10,8 +10,6 @@ on the lane the plan chose.
 
 from __future__ import annotations
 
-from ..planner_types import assignment_chunks
-
 import ctypes
 import threading
 import time
@@ -21,6 +19,7 @@ from typing import Any, Callable
 import numpy as np
 
 from ..daemon.executor import ExecutionResult
+from ..planner_types import assignment_chunks
 from ..schema import BufferRegistration, ExecutionTicket, TransferIntent
 from ..utils.checksum import checksum_bytes
 
@@ -81,7 +80,9 @@ class MockDataPlane:
         self._lock = threading.Lock()
 
     def execute(self, ticket: ExecutionTicket, src: BufferRegistration, dst: BufferRegistration,
-                intent: TransferIntent | None) -> ExecutionResult:
+                intent: TransferIntent | None, buffers: dict | None = None) -> ExecutionResult:
+        from ..daemon.landing import LandingSpec
+
         if src.address is None or dst.address is None:
             raise MockLaneError("mock data plane needs in-process buffer addresses")
         plan = ticket.plan
@@ -91,13 +92,18 @@ class MockDataPlane:
             dev = int(p["target_device"]) if p["kind"] == "direct" else int(p["relay_device"])
             lanes.append((dev, p["kind"], [(int(c["src_offset"]), int(c["dst_offset"]), int(c["bytes"]))
                                             for c in assignment_chunks(asg)]))
+        spec = LandingSpec.from_metadata(intent.metadata) if intent is not None else None
+        landing = None
+        if spec is not None and spec.op != "copy":
+            landing = _MockLanding(spec, ticket.direction == "h2d", src, dst, dict(buffers or {}))
         return self.run_lanes(ticket.direction, int(src.address), int(src.size_bytes),
                               int(dst.address), int(dst.size_bytes), lanes,
-                              transfer_id=str(ticket.metadata.get("transfer_id", ticket.ticket_id)))
+                              transfer_id=str(ticket.metadata.get("transfer_id", ticket.ticket_id)),
+                              landing=landing)
 
     def run_lanes(self, direction: str, src: int, src_bytes: int, dst: int, dst_bytes: int,
                   lanes: list[tuple[int, str, list[tuple[int, int, int]]]],
-                  transfer_id: str = "") -> ExecutionResult:
+                  transfer_id: str = "", landing: "_MockLanding | None" = None) -> ExecutionResult:
         f = self.faults
         results: dict[int, dict[str, Any]] = {}
         errors: list[str] = []
@@ -107,6 +113,17 @@ class MockDataPlane:
             t0 = time.perf_counter()
             moved = 0
             for k, (so, do, n) in enumerate(chunks):
+                if landing is not None:
+                    try:
+                        landing.move(so, do, n)
+                    except (ValueError, IndexError) as exc:
+                        errors.append(f"lane {dev}: chunk {k}: {exc}")
+                        return
+                    moved += n
+                    with self._lock:
+                        self.trace.append({"transfer_id": transfer_id, "lane": dev, "kind": kind,
+                                           "src_offset": so, "dst_offset": do, "bytes": n, "op": landing.spec.op})
+                    continue
                 if so < 0 or do < 0 or so + n > src_bytes or do + n > dst_bytes:
                     errors.append(f"lane {dev}: chunk {k} out of bounds")
                     return
@@ -154,6 +171,51 @@ class MockDataPlane:
         if errors:
             return ExecutionResult(ok=False, bytes_completed=total, error="; ".join(errors), measured=measured)
         return ExecutionResult(ok=True, bytes_completed=total, measured=measured)
+
+
+class _MockLanding:
+    """The fused landing ops on host memory, chunk by chunk, with the same
+    addressing rules as the GPU kernels: unit scatter / gather through the
+    KV layout and bf16 -> e4m3 block quantisation (the OCP oracle)."""
+
+    def __init__(self, spec, h2d: bool, src: BufferRegistration, dst: BufferRegistration,
+                 buffers: dict) -> None:
+        from ..daemon.landing import unit_addresses
+
+        self.spec, self.h2d = spec, h2d
+        self.host, self.dev = (src, dst) if h2d else (dst, src)
+        buffers.setdefault(self.dev.buffer_id, self.dev)
+        if spec.units_op:
+            self.units = unit_addresses(spec, lambda b: int(buffers[b].address))
+
+    def move(self, so: int, do: int, n: int) -> None:
+        spec = self.spec
+        hbase = int(self.host.address)
+        if spec.units_op:
+            u = spec.unit_bytes
+            host_off, pos = (so, do) if self.h2d else (do, so)
+            if pos % u or n % u:
+                raise ValueError("chunk is not a whole number of units")
+            for k in range(n // u):
+                ua = int(self.units[pos // u + k])
+                h = hbase + host_off + k * u
+                if self.h2d:
+                    ctypes.memmove(ua, h, u)
+                else:
+                    ctypes.memmove(h, ua, u)
+            return
+        from ..utils.fp8 import block_quant
+
+        ts = sorted(spec.tensors, key=lambda t: t.host_offset)
+        t = next(t for t in reversed(ts) if t.host_offset <= so)
+        rb = 2 * t.cols
+        row0, rows = (so - t.host_offset) // rb, n // rb
+        raw = np.ctypeslib.as_array((ctypes.c_uint16 * (n // 2)).from_address(hbase + so)).copy()
+        x = (raw.astype(np.uint32) << 16).view(np.float32).reshape(rows, t.cols)
+        q, sc = block_quant(x)
+        dbase = int(self.dev.address)
+        ctypes.memmove(dbase + t.q_offset + row0 * t.cols, q.ctypes.data, q.nbytes)
+        ctypes.memmove(dbase + t.scales_offset + (row0 // 128) * (t.cols // 128) * 4, sc.ctypes.data, sc.nbytes)
 
 
 def chunk_lane_map(trace: list[dict[str, Any]]) -> dict[int, int]:

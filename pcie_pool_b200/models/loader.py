@@ -54,6 +54,24 @@ def _assign(sizes: np.ndarray, weights: Sequence[float] | None, nlanes: int) -> 
     return idx
 
 
+def fp8_chunks(manifest: WeightManifest, chunk_bytes: int):
+    """(src_off, rows_start, nbytes, tensor_index) of every fp8 chunk: each
+    matrix cut on 128-row tiles into pieces of at most ``chunk_bytes``."""
+    src, row0, nbytes, tidx = [], [], [], []
+    for ti, t in enumerate(manifest.matrices()):
+        rows, cols = t.shape
+        rb = cols * 2
+        step = max(1, int(chunk_bytes) // (128 * rb)) * 128
+        for r in range(0, rows, step):
+            n = min(step, rows - r)
+            src.append(t.offset + r * rb)
+            row0.append(r)
+            nbytes.append(n * rb)
+            tidx.append(ti)
+    return (np.array(src, np.int64), np.array(row0, np.int64), np.array(nbytes, np.int64),
+            np.array(tidx, np.int64))
+
+
 class PooledWeightLoader:
     def __init__(self, engine, target: int, relays: Sequence[int] = (), *, chunk_bytes: int = 16 << 20,
                  balancer=None, lane_weights: Sequence[float] | None = None, checksum: bool = True,
@@ -137,21 +155,7 @@ class PooledWeightLoader:
     # ---- fp8 -----------------------------------------------------------------------------------
     def fp8_plan(self, manifest: WeightManifest):
         """(src_off, rows_start, nbytes, tensor_index) of every fp8 chunk."""
-        src, row0, nbytes, tidx = [], [], [], []
-        for ti, t in enumerate(manifest.matrices()):
-            rows, cols = t.shape
-            rb = cols * 2
-            tile = 128 * rb
-            k = max(1, self.chunk_bytes // tile)
-            step = k * 128
-            for r in range(0, rows, step):
-                n = min(step, rows - r)
-                src.append(t.offset + r * rb)
-                row0.append(r)
-                nbytes.append(n * rb)
-                tidx.append(ti)
-        return (np.array(src, np.int64), np.array(row0, np.int64), np.array(nbytes, np.int64),
-                np.array(tidx, np.int64))
+        return fp8_chunks(manifest, self.chunk_bytes)
 
     def load_fp8(self, host_ptr: int, host_bytes: int, manifest: WeightManifest) -> LoadedWeights:
         """Matrices land as e4m3 codes + fp32 scales [ceil(R/128), C/128];
@@ -215,4 +219,160 @@ class PooledWeightLoader:
                              storage=[qbuf, vbuf])
 
 
-__all__ = ["LoadStats", "LoadedWeights", "PooledWeightLoader"]
+class DaemonWeightLoader:
+    """Pooled weight loading as daemon intents.
+
+    The same two loads as ``PooledWeightLoader`` -- a packed bf16 image, or
+    matrices landing as fp8 e4m3 + fp32 per-128x128-block scales quantised in
+    the landing kernel -- but each is an intent to the node daemon, so the
+    relays it uses come from the daemon's leases and fairness rules (the
+    reference's ``ModelWeightLoader`` submits the same kind of intent,
+    turbobus/adapters/model_loading.py).  The fp8 intent carries a landing
+    spec (daemon/landing.py) naming every matrix's output inside ONE device
+    buffer of codes and scales; its ranges are pre-cut on 128-row tiles.
+    Host images are page-locked tensors (daemon in this process) or
+    ``SharedPinnedCpuBuffer`` (daemon process); device buffers are registered
+    by address or CUDA IPC accordingly."""
+
+    def __init__(self, client, daemon_client, *, session_id: str, job_id: str, target: int,
+                 chunk_bytes: int = 16 << 20, prefix: str = "weights", fp8_ctas_per_lane: int = 12,
+                 timeout_s: float = 600.0) -> None:
+        from ..daemon.client import InProcessDaemonClient
+
+        self.client, self.dc = client, daemon_client
+        self.session_id, self.job_id, self.target = str(session_id), str(job_id), int(target)
+        self.chunk_bytes = int(chunk_bytes)
+        self.prefix = str(prefix)
+        self.fp8_ctas_per_lane = int(fp8_ctas_per_lane)
+        self.timeout_s = float(timeout_s)
+        self.in_process = isinstance(daemon_client, InProcessDaemonClient)
+        self._n = 0
+        self._keep: list = []
+
+    def _ok(self, r) -> None:
+        if not r.ok:
+            raise RuntimeError(r.error or "daemon request failed")
+
+    def _register_host(self, host) -> tuple[str, int]:
+        from ..client import SharedPinnedCpuBuffer
+
+        self._n += 1
+        bid = f"{self.prefix}-host{self._n}"
+        if isinstance(host, SharedPinnedCpuBuffer):
+            reg = host.buffer_registration()
+            self._ok(self.dc.register_buffer(bid, self.job_id, reg.kind, reg.size_bytes, handle_type=reg.handle_type,
+                                             metadata=dict(reg.metadata), pinned=True))
+            size = reg.size_bytes
+        else:
+            if not self.in_process:
+                raise ValueError("a daemon process needs a SharedPinnedCpuBuffer host image")
+            size = host.numel() * host.element_size()
+            self._ok(self.dc.register_buffer(bid, self.job_id, "cpu_pinned", size, address=int(host.data_ptr()),
+                                             pinned=True))
+        self._keep.append(host)
+        return bid, size
+
+    def _register_device(self, t) -> str:
+        self._n += 1
+        bid = f"{self.prefix}-dev{self._n}"
+        if self.in_process:
+            self._ok(self.dc.register_buffer(bid, self.job_id, "gpu", t.numel() * t.element_size(),
+                                             device_index=self.target, address=int(t.data_ptr())))
+        else:
+            from ..client import CudaIpcDeviceBuffer
+
+            buf = CudaIpcDeviceBuffer.from_tensor(bid, self.job_id, t)
+            self._ok(buf.register_with_daemon(self.dc))
+            self._keep.append(buf)
+        return bid
+
+    def _transfer(self, src: str, dst: str, ranges, chunk: int, landing=None):
+        from .. import TransferIntent, TransferStatusState
+
+        self._n += 1
+        meta = {"chunk_bytes": int(chunk)}
+        if landing is not None:
+            meta["landing"] = landing
+        total = sum(int(r["bytes"]) for r in ranges)
+        it = TransferIntent(f"{self.prefix}-load{self._n}", self.job_id, self.session_id, src, dst, "h2d", total,
+                            tuple(ranges), workload_kind="model_weights", metadata=meta)
+        r = self.client.transfer(it, timeout_seconds=self.timeout_s)
+        if r.state is not TransferStatusState.COMPLETE:
+            raise RuntimeError(f"weight load failed: {r.error}")
+        meas = (r.metadata or {}).get("measured", {}) or {}
+        return r, float(meas.get("cuda_ms", 0.0) or 0.0)
+
+    def load_bf16(self, host, manifest: WeightManifest, device_buffer=None) -> LoadedWeights:
+        import time
+
+        import torch
+
+        total = manifest.total_bytes
+        hid, hsize = self._register_host(host)
+        if hsize < total:
+            raise ValueError("host image is smaller than the manifest")
+        dev = torch.device("cuda", self.target)
+        buf = device_buffer if device_buffer is not None else torch.empty(total, dtype=torch.uint8, device=dev)
+        did = self._register_device(buf)
+        t0 = time.perf_counter()
+        r, cuda_ms = self._transfer(hid, did, ({"src_offset": 0, "dst_offset": 0, "bytes": total},), self.chunk_bytes)
+        wall = (time.perf_counter() - t0) * 1e3
+        views = {t.name: buf[t.offset:t.offset + t.nbytes].view(torch.bfloat16).view(*t.shape)
+                 for t in manifest.tensors}
+        lanes = [(p.get("relay_device"), p.get("bytes"), round(float(p.get("cuda_ms", 0.0)), 3))
+                 for p in (r.path_stats or ())]
+        return LoadedWeights(views, {}, LoadStats(total, cuda_ms, wall, 1, lanes), storage=[buf])
+
+    def load_fp8(self, host, manifest: WeightManifest) -> LoadedWeights:
+        import time
+
+        import torch
+
+        mats = manifest.matrices()
+        if self.chunk_bytes < 128 * 2 * max(t.shape[1] for t in mats):
+            raise ValueError("chunk_bytes must hold at least one 128-row tile of the widest matrix")
+        hid, _ = self._register_host(host)
+        dev = torch.device("cuda", self.target)
+        q_total = sum(t.numel for t in mats)
+        s_base = -(-q_total // 256) * 256
+        s_total = sum(-(-t.shape[0] // 128) * (t.shape[1] // 128) * 4 for t in mats)
+        out = torch.empty(s_base + s_total, dtype=torch.uint8, device=dev)
+        table, qviews, sviews = [], {}, {}
+        qo, so = 0, s_base
+        for t in mats:
+            rows, cols = t.shape
+            ns = -(-rows // 128) * (cols // 128) * 4
+            table.append({"host_offset": t.offset, "rows": rows, "cols": cols, "q_offset": qo, "scales_offset": so})
+            qviews[t.name] = out[qo:qo + t.numel].view(rows, cols)
+            sviews[t.name] = out[so:so + ns].view(torch.float32).view(-(-rows // 128), cols // 128)
+            qo += t.numel
+            so += ns
+        did = self._register_device(out)
+        src, _row0, nbytes, _tidx = fp8_chunks(manifest, self.chunk_bytes)
+        ranges = [{"src_offset": int(a), "dst_offset": int(a), "bytes": int(n)} for a, n in zip(src, nbytes)]
+        landing = {"op": "fp8_quant", "tensors": table, "ctas_per_lane": self.fp8_ctas_per_lane}
+        t0 = time.perf_counter()
+        r, cuda_ms = self._transfer(hid, did, ranges, int(nbytes.max()), landing)
+        moved, transfers = int(nbytes.sum()), 1
+        vecs = manifest.vectors()
+        storage = [out]
+        if vecs:
+            vbuf = torch.empty(max(16, sum(t.nbytes for t in vecs)), dtype=torch.uint8, device=dev)
+            vid = self._register_device(vbuf)
+            vr, off = [], 0
+            for t in vecs:
+                vr.append({"src_offset": t.offset, "dst_offset": off, "bytes": t.nbytes})
+                qviews[t.name] = vbuf[off:off + t.nbytes].view(torch.bfloat16).view(*t.shape)
+                off += t.nbytes
+            _rv, ms2 = self._transfer(hid, vid, vr, self.chunk_bytes)
+            cuda_ms += ms2
+            moved += off
+            transfers += 1
+            storage.append(vbuf)
+        wall = (time.perf_counter() - t0) * 1e3
+        lanes = [(p.get("relay_device"), p.get("bytes"), round(float(p.get("cuda_ms", 0.0)), 3))
+                 for p in (r.path_stats or ())]
+        return LoadedWeights(qviews, sviews, LoadStats(moved, cuda_ms, wall, transfers, lanes), storage=storage)
+
+
+__all__ = ["DaemonWeightLoader", "LoadStats", "LoadedWeights", "PooledWeightLoader", "fp8_chunks"]
