@@ -44,6 +44,9 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=1, help="untimed passes over all requests")
     p.add_argument("--chunk", type=int, default=4 << 20, help="bytes per pooled chunk (whole block-lanes)")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--via", choices=["engine", "daemon"], default="engine",
+                   help="ours: drive the engine directly, or submit every save / restore as a daemon intent "
+                        "(fused gather / scatter landing spec, relays from leases)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--json-out", default="")
     return p.parse_args(argv)
@@ -105,34 +108,51 @@ def run_ours(a) -> dict:
     devices = list(range(a.gpus))
     eng = PoolEngine(devices, slot_bytes=a.chunk, slots=3, ctas_per_lane=4, timeout_s=30.0)
     lane_set, _weights, balancer, profile = calibrate(eng, 0, devices, w.req_bytes, a.chunk)
-    off = PagedKVOffloader(eng, w.caches, 0, [d for d in lane_set if d != 0], units_per_chunk=a.chunk // w.unit,
-                           checksum=True, balancer=balancer)
-    hosts = [PinnedHostBuffer(w.req_bytes, fill=None) for _ in range(a.requests)]
+    relays = [d for d in lane_set if d != 0]
+    if a.via == "daemon":
+        from .. import TurboBusClient
+        from ..adapters.kv_offload import DaemonKVOffloader
+        from ..e2e import build_inprocess_node, nominal_profile
+
+        prof = profile if profile is not None else (nominal_profile(0, relays) if relays else None)
+        _daemon, dc = build_inprocess_node(eng, list(lane_set), 0, prof)
+        sid = dc.register_session(0, relays, max_inflight_chunks=1 << 16).payload["session"]["session_id"]
+        dc.register_job("kv-bench", session_id=sid)
+        off = DaemonKVOffloader(TurboBusClient(daemon=dc), dc, session_id=sid, job_id="kv-bench",
+                                kv_caches=w.caches, units_per_chunk=a.chunk // w.unit)
+        hosts = [torch.empty(w.req_bytes, dtype=torch.uint8, pin_memory=True) for _ in range(a.requests)]
+        save = lambda r: off.save(list(w.src[r]), hosts[r])  # noqa: E731
+        load = lambda r: off.restore(list(w.dst[r]), hosts[r])  # noqa: E731
+    else:
+        off = PagedKVOffloader(eng, w.caches, 0, relays, units_per_chunk=a.chunk // w.unit, checksum=True,
+                               balancer=balancer)
+        hosts = [PinnedHostBuffer(w.req_bytes, fill=None) for _ in range(a.requests)]
+        save = lambda r: off.save(list(w.src[r]), hosts[r].ptr, w.req_bytes)  # noqa: E731
+        load = lambda r: off.restore(list(w.dst[r]), hosts[r].ptr, w.req_bytes)  # noqa: E731
     save_ms, load_ms, save_dev, load_dev = [], [], [], []
     try:
         for _ in range(a.warmup):
             for r in range(a.requests):
-                off.save(list(w.src[r]), hosts[r].ptr, w.req_bytes)
-                off.restore(list(w.dst[r]), hosts[r].ptr, w.req_bytes)
+                save(r)
+                load(r)
         torch.cuda.synchronize()
         clocks = ClockSampler(a.gpus).start()
         for _ in range(a.steps):
             for r in range(a.requests):
                 st = {}
-                save_ms.append(_timed(lambda: st.setdefault("s", off.save(list(w.src[r]), hosts[r].ptr,
-                                                                            w.req_bytes))))
+                save_ms.append(_timed(lambda: st.setdefault("s", save(r))))
                 save_dev.append(st["s"].cuda_ms)
             for r in range(a.requests):
                 st = {}
-                load_ms.append(_timed(lambda: st.setdefault("l", off.restore(list(w.dst[r]), hosts[r].ptr,
-                                                                              w.req_bytes))))
+                load_ms.append(_timed(lambda: st.setdefault("l", load(r))))
                 load_dev.append(st["l"].cuda_ms)
         clk = clocks.stop()
         verified = w.verify()
         last_lanes = st["l"].lanes
     finally:
         for h in hosts:
-            h.release()
+            if hasattr(h, "release"):
+                h.release()
     return {"reload_ms": load_ms, "offload_ms": save_ms, "reload_dev_ms": load_dev, "offload_dev_ms": save_dev,
             "verified": verified, "clocks": clk, "lane_set": lane_set, "lanes": last_lanes,
             "req_bytes": w.req_bytes, "units_per_request": w.req_bytes // w.unit,
@@ -225,6 +245,7 @@ def main(argv=None) -> int:
     p50 = _pct(res["reload_ms"], 0.5)
     line = {"metric": "vLLM KV reload p50 (per 32k-token request, permuted block table)", "value": round(p50, 3),
             "unit": "ms", "higher_is_better": False, "n_gpus": a.gpus, "impl": a.impl,
+            "via": a.via if a.impl == "ours" else "reference runtime",
             "reload_p50_ms": round(p50, 3), "reload_p99_ms": round(_pct(res["reload_ms"], 0.99), 3),
             "offload_p50_ms": round(_pct(res["offload_ms"], 0.5), 3),
             "offload_p99_ms": round(_pct(res["offload_ms"], 0.99), 3),

@@ -36,6 +36,9 @@ def parse_args(argv=None):
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--chunk", type=int, default=16 << 20)
     p.add_argument("--api", action="store_true", help="also time the bf16 load through the public API")
+    p.add_argument("--via", choices=["engine", "daemon"], default="engine",
+                   help="ours: drive the engine directly, or submit each load as a daemon intent "
+                        "(fp8: landing spec with the tensor table; relays from leases)")
     p.add_argument("--layers", type=int, default=0, help="override the layer count (smaller smoke runs)")
     p.add_argument("--json-out", default="")
     return p.parse_args(argv)
@@ -106,10 +109,27 @@ def run_ours(a) -> dict:
     host = _host_image(manifest)
     eng = PoolEngine(devices, slot_bytes=a.chunk, slots=3, ctas_per_lane=4, timeout_s=30.0)
     lane_set, weights, balancer, profile = calibrate(eng, 0, devices, total, a.chunk)
-    loader = PooledWeightLoader(eng, 0, [d for d in lane_set if d != 0], chunk_bytes=a.chunk, balancer=balancer)
+    relays = [d for d in lane_set if d != 0]
+    loader = PooledWeightLoader(eng, 0, relays, chunk_bytes=a.chunk, balancer=balancer)
     dst = torch.empty(total, dtype=torch.uint8, device="cuda:0") if a.variant == "bf16" else None
+    if a.via == "daemon":
+        from .. import TurboBusClient
+        from ..e2e import build_inprocess_node, nominal_profile
+        from ..models.loader import DaemonWeightLoader
+
+        prof = profile if profile is not None else (nominal_profile(0, relays) if relays else None)
+        _daemon, dc = build_inprocess_node(eng, list(lane_set), 0, prof)
+        sid = dc.register_session(0, relays, max_inflight_chunks=1 << 16).payload["session"]["session_id"]
+        dc.register_job("llama-load", session_id=sid)
+        dloader = DaemonWeightLoader(TurboBusClient(daemon=dc), dc, session_id=sid, job_id="llama-load", target=0,
+                                     chunk_bytes=a.chunk)
+        host_t = torch.from_numpy(host.numpy())  # the same page-locked image, as a tensor
 
     def load():
+        if a.via == "daemon":
+            if a.variant == "bf16":
+                return dloader.load_bf16(host_t, manifest, device_buffer=dst)
+            return dloader.load_fp8(host_t, manifest)
         if a.variant == "bf16":
             return loader.load_bf16(host.ptr, total, manifest, device_buffer=dst)
         return loader.load_fp8(host.ptr, total, manifest)
@@ -257,6 +277,7 @@ def main(argv=None) -> int:
     line = {"metric": "Llama-3-8B-shape weight load into GPU0", "value": round(ms / 1e3, 4), "unit": "s",
             "higher_is_better": False, "gb_per_s": round(res["bytes"] / 1e9 / (ms / 1e3), 3),
             "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "impl": a.impl, "variant": a.variant,
+            "via": a.via if a.impl == "ours" else "reference runtime",
             "verified": res.get("verified"), "clocks": res.get("clocks"),
             "config": {"model": _manifest(a.layers).config.name, "params": _manifest(a.layers).param_count,
                        "image_bytes": res["bytes"], "chunk_bytes": a.chunk, "target_gpu": 0,
