@@ -44,6 +44,9 @@ def parse_args(argv=None):
     p.add_argument("--coalesce", type=int, default=64 << 20,
                    help="largest merged copy-engine transfer on the direct lane (bytes)")
     p.add_argument("--direction", choices=["h2d", "d2h"], default="h2d")
+    p.add_argument("--lane-order", choices=["spread", "index"], default="spread",
+                   help="ours: GPU0 plus N-1 relays spread over PCIe uplinks (socket, root complex, switch) "
+                        "among the visible GPUs, or simply GPUs 0..N-1")
     p.add_argument("--no-checksum", action="store_true", help="skip the fused per-chunk checksum")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--json-out", default="")
@@ -54,10 +57,16 @@ def parse_args(argv=None):
 # ---- distributed plumbing -------------------------------------------------------------
 
 class Dist:
-    def __init__(self):
+    """One rank per GPU of the lane set: rank r runs on ``lane_set[r]`` (the
+    lane set is computed identically on every rank from the topology), so
+    exactly the N GPUs that carry lanes are active."""
+
+    def __init__(self, lane_set=None):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.device = int(lane_set[self.local_rank]) if lane_set and self.local_rank < len(lane_set) \
+            else self.local_rank
         self.pg = None
         if self.world > 1:
             import datetime
@@ -65,16 +74,16 @@ class Dist:
             import torch
             import torch.distributed as dist
 
-            torch.cuda.set_device(self.local_rank)
+            torch.cuda.set_device(self.device)
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                    device_id=torch.device("cuda", self.local_rank))
+                                    device_id=torch.device("cuda", self.device))
             self.pg = dist
 
     def barrier(self):
         if self.pg is not None:
             import torch
 
-            self.pg.barrier(device_ids=[self.local_rank])
+            self.pg.barrier(device_ids=[self.device])
             torch.cuda.synchronize()
 
     def max(self, value: float) -> float:
@@ -82,7 +91,7 @@ class Dist:
             return value
         import torch
 
-        t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{self.local_rank}")
+        t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{self.device}")
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
@@ -108,7 +117,7 @@ def run_ours(args, dist: Dist) -> dict:
     from pcie_pool_b200.utils.host_memory import PinnedHostBuffer
 
     N = args.gpus
-    devices = list(range(N))
+    devices = list(args.lane_set)
     n = args.bytes
     out: dict = {}
     if dist.rank == 0:
@@ -158,7 +167,7 @@ def run_ours(args, dist: Dist) -> dict:
     dist.barrier()
     res = None
     elapsed_ms = 0.0
-    clocks = ClockSampler(N)
+    clocks = ClockSampler(devices)
     if dist.rank == 0:
         torch.cuda.synchronize()
         clocks.start()
@@ -189,6 +198,8 @@ def run_ours(args, dist: Dist) -> dict:
             "gpu_launches": kernel_per_step * args.steps,
             "transfer_cuda_ms": res.cuda_ms,
             "lane_set": list(lane_set),
+            "gpus_bound": list(devices),
+            "lane_choice": args.lane_info,
             "probe": None if profile is None else profile.get("concurrent"),
         }
         if not args.no_e2e and direction == H2D:
@@ -470,7 +481,13 @@ def main(argv=None) -> int:
     args = parse_args(argv)
     if args.reference_e2e_child:
         return reference_e2e_child(args)
-    dist = Dist()
+    if args.impl == "ours" and args.lane_order == "spread":
+        from pcie_pool_b200.topology.cuda_nvml import cuda_lane_set
+
+        args.lane_set, args.lane_info = cuda_lane_set(args.gpus)
+    else:
+        args.lane_set, args.lane_info = list(range(args.gpus)), {"rule": "GPUs 0..N-1"}
+    dist = Dist(args.lane_set)
     if args.impl == "reference":
         res = run_reference(args, dist)
     else:
@@ -502,7 +519,7 @@ def main(argv=None) -> int:
                     "transfer_bytes": args.bytes,
                     "chunk_bytes": args.chunk, "coalesce_bytes": args.coalesce,
                     "target_gpu": 0,
-                    "relay_gpus": list(range(1, N)),
+                    "relay_gpus": list(args.lane_set[1:]),
                     "parallelism": f"direct+{N - 1}relay",
                     "l2": "inputs larger than L2 (each step moves a fresh 4 GiB stream)",
                 },
@@ -519,6 +536,8 @@ def main(argv=None) -> int:
             else:
                 line["impl"] = "ours"
                 line["lane_set"] = res.get("lane_set")
+                line["gpus_bound"] = res.get("gpus_bound")
+                line["lane_choice"] = res.get("lane_choice")
                 line["probe"] = res.get("probe")
                 if "e2e" in res:
                     line["e2e"] = res["e2e"]

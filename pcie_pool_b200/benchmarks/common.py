@@ -22,8 +22,10 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpus: int):
-        self.gpus = gpus
+    def __init__(self, gpus):
+        """``gpus``: a GPU count (indices 0..gpus-1) or the indices sampled."""
+        self.devices = set(range(gpus)) if isinstance(gpus, int) else {int(g) for g in gpus}
+        self.gpus = len(self.devices)
         self.proc = None
         self.lines: list[str] = []
         self._t = None
@@ -63,7 +65,7 @@ class ClockSampler:
                 idx = int(parts[0])
             except ValueError:
                 continue
-            if idx >= self.gpus:
+            if idx not in self.devices:
                 continue
             try:
                 sm.append(float(parts[1]))

@@ -206,7 +206,25 @@ class TurboBusDaemon:
                 return fail(TOPOLOGY_UNAVAILABLE)
             inv = self._topology.snapshot()
             cands = tuple(sorted(self._quotas)) if requested_relays is None else tuple(norm_relays(requested_relays))
-            return ok(relay_discovery=self._discovery(inv, None if target_gpu is None else int(target_gpu), cands))
+            disc = self._discovery(inv, None if target_gpu is None else int(target_gpu), cands)
+            if target_gpu is not None:
+                # every eligible relay, in the order that spreads lanes over
+                # sockets, root complexes and switches (take a prefix)
+                disc["recommended_relays"] = inv.spread_relays(int(target_gpu),
+                                                               [g for g in cands if g in self._quotas], len(cands))
+            return ok(relay_discovery=disc)
+
+    def choose_relays(self, target_gpu: int, count: int, candidates: Iterable[int] | None = None) -> list[int]:
+        """``count`` relays for lanes into ``target_gpu``, spread over PCIe
+        uplinks (topology: socket, root complex, switch), among the relays
+        this daemon lends."""
+        with self._lock:
+            if self._topology is None:
+                raise ValueError(TOPOLOGY_UNAVAILABLE)
+            inv = self._topology.snapshot()
+            cands = sorted(self._quotas) if candidates is None else [g for g in norm_relays(candidates)
+                                                                     if g in self._quotas]
+            return inv.spread_relays(int(target_gpu), cands, int(count))
 
     # ---- sessions / jobs / buffers -----------------------------------------------------
     def register_session(self, target_gpu: int, requested_relays: Iterable[int],

@@ -168,6 +168,28 @@ class DaemonResourceInventory:
             out[p.device_id] = ids.setdefault(key, len(ids))
         return out
 
+    def uplink_keys(self, device: int) -> tuple[str | None, str | None, str | None]:
+        """(socket, root complex, top switch) of a GPU's PCIe path, the three
+        levels at which lanes share upstream bandwidth; None where unknown."""
+        p = self.pcie_path(int(device))
+        if p is None:
+            return (None, None, None)
+        sock = None if p.numa_node is None else f"numa{p.numa_node}"
+        return (sock, p.root_complex, p.switch_hierarchy[0] if p.switch_hierarchy else None)
+
+    def spread_relays(self, target_device: int, candidates: Iterable[int], count: int) -> list[int]:
+        """Pick ``count`` relays from eligible ``candidates`` for lanes into
+        ``target_device`` so the lane set (target included) shares as little
+        upstream PCIe as possible: greedily the candidate whose socket, then
+        root complex, then top switch carries the fewest lanes chosen so far
+        (ties: lower index).  Lanes behind one root port or socket share its
+        bandwidth, so spreading them raises the aggregate (on an 8-GPU node
+        whose GPUs 0-3 share a socket, 4 lanes as {0, 4, 1, 5} rather than
+        {0, 1, 2, 3}).  The reference picks relays by index and isolated
+        per-link bandwidth (turbobus/scheduler/daemon.py:222-281)."""
+        pool = list(self.eligible_relay_devices(int(target_device), candidates))
+        return spread_by_keys(int(target_device), pool, count, self.uplink_keys)
+
     def eligible_relay_devices(self, target_device: int, requested_relays: Iterable[int]) -> tuple[int, ...]:
         return tuple(e["relay_gpu"] for e in
                      self.relay_eligibility(target_device, requested_relays)["eligible_relays"])
@@ -222,16 +244,45 @@ class StaticTopologyProvider(TopologyProvider):
         self.invalidations += 1
 
 
+def spread_by_keys(target: int, pool: Iterable[int], count: int, keys_of) -> list[int]:
+    """Greedy uplink spreading (see ``DaemonResourceInventory.spread_relays``)
+    over any device numbering: ``keys_of(dev)`` gives its (socket, root
+    complex, top switch) keys."""
+    pool = list(pool)
+    load: list[dict[str, int]] = [{}, {}, {}]
+
+    def add(dev: int) -> None:
+        for lvl, key in enumerate(keys_of(dev)):
+            if key is not None:
+                load[lvl][key] = load[lvl].get(key, 0) + 1
+
+    def cost(dev: int):
+        return tuple(load[lvl].get(k, 0) if k is not None else 0 for lvl, k in enumerate(keys_of(dev))) + (dev,)
+
+    add(int(target))
+    out: list[int] = []
+    while pool and len(out) < max(0, int(count)):
+        best = min(pool, key=cost)
+        pool.remove(best)
+        out.append(best)
+        add(best)
+    return out
+
+
 def synthetic_inventory(gpu_count: int, *, fabric: str = "nvswitch", source: str = "synthetic",
-                        gen: int = 5, width: int = 16, gpus_per_switch: int = 1) -> DaemonResourceInventory:
+                        gen: int = 5, width: int = 16, gpus_per_switch: int = 1,
+                        gpus_per_root: int | None = None) -> DaemonResourceInventory:
     """An HGX-like node: every GPU on its own Gen5 x16 link (or
-    ``gpus_per_switch`` GPUs per switch), all pairs joined by the fabric."""
+    ``gpus_per_switch`` GPUs per switch), all pairs joined by the fabric; the
+    first half of the GPUs on socket (NUMA node) 0, the rest on 1, and
+    ``gpus_per_root`` GPUs per root complex (default: one per switch)."""
+    per_root = gpus_per_root or gpus_per_switch
     gpus = tuple(GpuInventoryRecord(i, backend="cuda", vendor="nvidia", uuid=f"GPU-synthetic-{i}",
                                     pci_bus_id=f"0000:{0x10 * (i + 1):02x}:00.0",
                                     numa_node=0 if i < max(1, gpu_count // 2) else 1,
                                     memory_bytes=183359 << 20) for i in range(gpu_count))
     paths = tuple(PciePathRecord(i, numa_node=g.numa_node,
-                                 root_complex=f"0000:{0x10 * (i // gpus_per_switch + 1):02x}",
+                                 root_complex=f"0000:{0x10 * (i // per_root + 1):02x}",
                                  link_generation=gen, link_width=width,
                                  bandwidth_gbps=round(pcie_gbps(gen, width) or 0.0, 3),
                                  switch_hierarchy=(f"switch{i // gpus_per_switch}",),
@@ -258,4 +309,4 @@ def pcie_gbps(gen: int | None, width: int | None) -> float | None:
 
 __all__ = ["DaemonResourceInventory", "FabricLinkRecord", "GpuInventoryRecord", "PCIE_GBPS_PER_LANE",
            "PCIE_GTPS", "PciePathRecord", "StaticTopologyProvider", "TopologyProvider", "pcie_gbps",
-           "synthetic_inventory"]
+           "spread_by_keys", "synthetic_inventory"]

@@ -462,3 +462,57 @@ def _root_complex(bus_id: str | None) -> str | None:
 
 __all__ = ["CudaNvmlTopologyProvider", "CudaTopologyProbe", "NvidiaSmiProbe", "NvmlProbe",
            "TopologyDiscoveryError", "fabric_capability", "fabric_links_from_matrix", "pcie_tree"]
+
+
+def _bdf(s: str | None) -> tuple[int, int, int] | None:
+    """(domain, bus, device) of a PCI address like ``00000000:18:00.0``."""
+    if not s:
+        return None
+    try:
+        dom, bus, rest = str(s).strip().lower().split(":")
+        return int(dom, 16), int(bus, 16), int(rest.split(".")[0], 16)
+    except ValueError:
+        return None
+
+
+def cuda_lane_set(n: int, target: int = 0, provider: "CudaNvmlTopologyProvider | None" = None,
+                  bus_ids: dict[int, tuple[int, int, int]] | None = None) -> tuple[list[int], dict]:
+    """CUDA device indices of ``target`` plus ``n - 1`` relays among the
+    visible GPUs, spread over PCIe uplinks (socket, root complex, switch)
+    with the daemon's rule.  Topology comes from NVML and sysfs and CUDA
+    indices are matched to it by PCI address, so no CUDA context is created
+    on any GPU.  Falls back to ``target, 0, 1, ...`` when discovery fails."""
+    from . import spread_by_keys
+
+    info: dict = {"rule": "spread over socket, root complex, switch"}
+    if bus_ids is None:
+        import torch
+
+        bus_ids = {}
+        for i in range(torch.cuda.device_count()):
+            p = torch.cuda.get_device_properties(i)
+            bus_ids[i] = (int(p.pci_domain_id), int(p.pci_bus_id), int(p.pci_device_id))
+    cands = [i for i in sorted(bus_ids) if i != int(target)]
+    fallback = [int(target)] + cands[:max(0, n - 1)]
+    if n <= 1:
+        return [int(target)], {**info, "reason": "single lane"}
+    try:
+        inv = (provider or CudaNvmlTopologyProvider()).snapshot()
+    except Exception as exc:  # noqa: BLE001 - any discovery failure keeps the index order
+        return fallback, {**info, "fallback": f"topology unavailable: {exc}"}
+    nvml_of = {}
+    by_bdf = {_bdf(g.pci_bus_id): g.device_id for g in inv.gpus}
+    for i, b in bus_ids.items():
+        if b in by_bdf:
+            nvml_of[i] = by_bdf[b]
+    if int(target) not in nvml_of:
+        return fallback, {**info, "fallback": "target GPU not found in the topology"}
+
+    def keys(i: int):
+        return inv.uplink_keys(nvml_of[i]) if i in nvml_of else (None, None, None)
+
+    relays = spread_by_keys(int(target), [c for c in cands if c in nvml_of], n - 1, keys)
+    if len(relays) < n - 1:
+        relays += [c for c in cands if c not in relays][:n - 1 - len(relays)]
+    info["uplinks"] = {str(i): list(keys(i)) for i in [int(target), *relays]}
+    return [int(target), *relays], info

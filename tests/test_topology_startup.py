@@ -231,3 +231,30 @@ def test_daemon_cli_builds_the_startup_config():
     assert (c.max_inflight_chunks_per_relay, c.execute, c.profile_store_path) == (64, True, "/tmp/p.json")
     with pytest.raises(SystemExit):
         build_parser().parse_args([])
+
+
+def test_relays_spread_across_sockets_and_root_complexes():
+    """Lanes into GPU0 take relays on the other socket first, then on root
+    complexes (and switches) no chosen lane uses yet."""
+    from pcie_pool_b200.topology import synthetic_inventory
+
+    inv = synthetic_inventory(8)  # GPUs 0-3 on socket 0, 4-7 on socket 1, one root complex each
+    assert inv.spread_relays(0, range(8), 1) == [4]
+    assert inv.spread_relays(0, range(8), 3) == [4, 1, 5]
+    assert sorted(inv.spread_relays(0, range(8), 7)) == [1, 2, 3, 4, 5, 6, 7]
+    # two GPUs per switch, four per root complex: the switch partner of GPU0 comes last on its socket
+    inv2 = synthetic_inventory(8, gpus_per_switch=2, gpus_per_root=4)
+    assert inv2.spread_relays(0, range(8), 3) == [4, 2, 6]
+    # only eligible candidates are chosen
+    assert inv.spread_relays(0, [1, 2, 3], 2) == [1, 2]
+
+
+def test_daemon_recommends_relays_spread_over_uplinks():
+    from pcie_pool_b200.daemon import InProcessDaemonClient, TurboBusDaemon
+    from pcie_pool_b200.topology import StaticTopologyProvider, synthetic_inventory
+
+    d = TurboBusDaemon(range(1, 8), topology_provider=StaticTopologyProvider(synthetic_inventory(8)))
+    r = InProcessDaemonClient(d).discover_relays(0)
+    assert r.ok and r.payload["relay_discovery"]["recommended_relays"][:3] == [4, 1, 5]
+    assert d.choose_relays(0, 3) == [4, 1, 5]
+    assert d.choose_relays(0, 2, candidates=[1, 2, 3]) == [1, 2]
