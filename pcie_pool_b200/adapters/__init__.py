@@ -9,6 +9,7 @@ from .inference import (FrameworkKVSlot, FrameworkKVSlotAdapter, InferenceKVSlot
                         make_contiguous_kv_slots)
 from .kv_offload import KVTransferStats, PagedKVOffloader
 from .model_loading import ModelLoader, ModelWeightLoader
+from .streamed_optimizer import StepStats, StreamedAdamW
 from .training_offload import TrainingOffloadManager, TrainingOffloadStore
 from .vllm import (VllmKVBlockRef, VllmKVGroup, VllmKVSlotAdapter, block_bytes_from_vllm_kv_tensor,
                    block_table_units, make_vllm_block_refs_from_ids, make_vllm_layer_block_refs_from_ids,
@@ -25,7 +26,7 @@ __all__ = [
     "ReceiptTransferHandle", "TrainingOffloadManager", "TrainingOffloadStore", "TurboBusConnector",
     "TurboBusConnectorConfig", "TurboBusConnectorMetadata", "TurboBusRequestMetadata", "TurboBusSavedPrefix",
     "VllmAllocationEvent", "VllmIntegrationState", "VllmKVBlockRef", "VllmKVGroup", "VllmKVSlotAdapter",
-    "VllmTurboBusIntegration", "block_bytes_from_vllm_kv_tensor", "block_table_units", "clear_connector_events",
+    "StepStats", "StreamedAdamW", "VllmTurboBusIntegration", "block_bytes_from_vllm_kv_tensor", "block_table_units", "clear_connector_events",
     "clear_saved_prefixes", "extract_vllm_block_ids", "get_connector_events", "get_saved_prefix",
     "make_contiguous_kv_slots", "make_vllm_block_refs_from_ids", "make_vllm_layer_block_refs_from_ids",
     "make_vllm_layer_groups_from_kv_caches", "make_vllm_layer_range_refs_from_ids", "vllm_block_name",

@@ -42,6 +42,9 @@ PYBIND11_MODULE(_C, m) {
   m.attr("OP_FP8_QUANT") = static_cast<int>(kOpFp8Quant);
   m.attr("OP_SCATTER_RANGES") = static_cast<int>(kOpScatterRanges);
   m.attr("OP_GATHER_RANGES") = static_cast<int>(kOpGatherRanges);
+  m.attr("OP_ADAMW") = static_cast<int>(kOpAdamW);
+  m.attr("ADAM_TILE_PARAMS") = kAdamTileParams;
+  m.attr("ADAM_TILE_BYTES") = kAdamTileBytes;
   m.attr("TILE_BYTES") = kTileBytes;
   m.attr("BUILD_ARCH") = "sm_100a";
 
@@ -172,6 +175,19 @@ PYBIND11_MODULE(_C, m) {
           py::arg("src_off"), py::arg("dst_off"), py::arg("bytes"), py::arg("unit0") = py::none(),
           py::arg("tensor") = py::none(), py::arg("count") = py::none());
 
+  py::class_<AdamStepSpec>(m, "AdamStepSpec")
+      .def(py::init<>())
+      .def_readwrite("grads", &AdamStepSpec::grads)
+      .def_readwrite("params", &AdamStepSpec::params)
+      .def_readwrite("nparams", &AdamStepSpec::nparams)
+      .def_readwrite("lr", &AdamStepSpec::lr)
+      .def_readwrite("beta1", &AdamStepSpec::beta1)
+      .def_readwrite("beta2", &AdamStepSpec::beta2)
+      .def_readwrite("eps", &AdamStepSpec::eps)
+      .def_readwrite("weight_decay", &AdamStepSpec::weight_decay)
+      .def_readwrite("grad_scale", &AdamStepSpec::grad_scale)
+      .def_readwrite("step", &AdamStepSpec::step);
+
   py::class_<QuantTensorSpec>(m, "QuantTensorSpec")
       .def(py::init<>())
       .def_readwrite("q", &QuantTensorSpec::q)
@@ -198,6 +214,7 @@ PYBIND11_MODULE(_C, m) {
       .def_readwrite("timeout_s", &TransferSpec::timeout_s)
       .def_readwrite("unit_bytes", &TransferSpec::unit_bytes)
       .def_readwrite("tensors", &TransferSpec::tensors)
+      .def_readwrite("adam", &TransferSpec::adam)
       .def("set_unit_addrs",
            [](TransferSpec& s, py::array_t<uint64_t, py::array::c_style | py::array::forcecast> a) {
              s.unit_addrs = to_vec<uint64_t>(a);

@@ -1,6 +1,7 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <stdexcept>
 #include <thread>
@@ -11,15 +12,22 @@ namespace ppb {
 
 namespace {
 
-// Mailbox layout: per direction four 32-bit counters (relay ready, relay
-// free, landing ready, landing free), each on its own 128-byte line.
+// Mailbox layout: per direction six 32-bit counters (relay ready, relay
+// free, landing ready, landing free, relay done, landing done), each on its
+// own 128-byte line.  "done" is only used by round trips (kOpAdamW): the
+// kernel publishes a processed chunk and the copy-out stream frees the slot.
 constexpr int kCounterStride = 128 / 4;
 constexpr int kRelayReady = 0;
 constexpr int kRelayFree = 1;
 constexpr int kLandReady = 2;
 constexpr int kLandFree = 3;
-constexpr size_t kMailboxBytes = 128 * 8;
-uint32_t* counter(uint32_t* mbox, int dir, int which) { return mbox + (dir * 4 + which) * kCounterStride; }
+constexpr int kRelayDone = 4;
+constexpr int kLandDone = 5;
+constexpr int kCountersPerDir = 6;
+constexpr size_t kMailboxBytes = 128 * 2 * kCountersPerDir;
+uint32_t* counter(uint32_t* mbox, int dir, int which) {
+  return mbox + (dir * kCountersPerDir + which) * kCounterStride;
+}
 
 // Of the lane-kernel CTAs that can be resident on one GPU, landing kernels
 // (H2D; fp8 quantisation wants many CTAs) get two thirds and push kernels
@@ -69,10 +77,14 @@ struct PoolEngine::Pending {
     bool kernel = false;     // processed by the lane kernel
     bool staged = false;     // goes through a staging ring
     bool in_place = false;   // kernel reads/writes data at its final place
+    bool roundtrip = false;  // kOpAdamW: chunks return to the host after the kernel
     Ring* ring = nullptr;
     cudaStream_t stream = nullptr;
+    cudaStream_t out = nullptr;  // round trip: the copy-out (device->host) stream
     Dev* d = nullptr;
     cudaEvent_t t0 = nullptr, t1 = nullptr;
+    cudaEvent_t t_in = nullptr;   // round trip: end of the copy-in leg
+    cudaEvent_t t_out = nullptr;  // round trip: end of the copy-out leg
     uint64_t seq0 = 0;       // ring->issued before this lane's first chunk
     uint64_t bytes = 0;
     uint64_t chunks = 0;
@@ -138,6 +150,8 @@ PoolEngine::PoolEngine(const std::vector<int>& devices, const EngineOptions& opt
       D->relay[dir].freec = counter(D->mbox, dir, kRelayFree);
       D->land[dir].ready = counter(D->mbox, dir, kLandReady);
       D->land[dir].freec = counter(D->mbox, dir, kLandFree);
+      D->relay[dir].donec = counter(D->mbox, dir, kRelayDone);
+      D->land[dir].donec = counter(D->mbox, dir, kLandDone);
     }
     // Keep freed stream-ordered allocations cached in the pool.
     cudaMemPool_t pool;
@@ -329,6 +343,7 @@ void PoolEngine::reset_rings(Pending& P) {
     DeviceGuard g(P.ring_devices[i]);
     cudaMemset(r->ready, 0, 4);
     cudaMemset(r->freec, 0, 4);
+    cudaMemset(r->donec, 0, 4);
     cudaDeviceSynchronize();
     r->issued = 0;
     r->poisoned = false;
@@ -356,6 +371,14 @@ void validate_spec(const TransferSpec& s, uint64_t slot_bytes, size_t slots) {
     case kOpGatherUnits:
     case kOpGatherRanges:
       if (h2d) throw std::invalid_argument("gather ops push data: D2H only");
+      break;
+    case kOpAdamW:
+      if (!h2d) throw std::invalid_argument("the streamed optimizer step is an H2D round trip");
+      if (s.adam.nparams == 0 || s.adam.grads == 0 || s.adam.params == 0 || s.adam.grads % 16 != 0 ||
+          s.adam.params % 16 != 0)
+        throw std::invalid_argument("adamw needs 16-byte aligned grads and params and nparams > 0");
+      if (s.adam.step < 1) throw std::invalid_argument("adamw step must be >= 1");
+      if (s.host_ptr % 16 != 0) throw std::invalid_argument("adamw state image must be 16-byte aligned");
       break;
     default:
       throw std::invalid_argument("unknown lane op");
@@ -404,6 +427,15 @@ void validate_spec(const TransferSpec& s, uint64_t slot_bytes, size_t slots) {
           sum += s.range_bytes[c.unit0 + k];
         }
         if (sum != c.bytes) throw std::invalid_argument("chunk bytes must equal its ranges");
+      }
+      if (s.op == kOpAdamW) {
+        const uint64_t tiles = (s.adam.nparams + kAdamTileParams - 1) / kAdamTileParams;
+        if (c.bytes % kAdamTileBytes != 0 || c.src_off % 16 != 0)
+          throw std::invalid_argument("adamw chunks must be whole 16-byte aligned state tiles");
+        if (uint64_t(c.unit0) + c.bytes / kAdamTileBytes > tiles)
+          throw std::invalid_argument("adamw chunk tiles exceed the parameter count");
+        if (c.src_off != uint64_t(c.unit0) * kAdamTileBytes)
+          throw std::invalid_argument("adamw chunk offset must match its first tile");
       }
       if (s.op == kOpFp8Quant) {
         if (c.tensor >= s.tensors.size()) throw std::invalid_argument("fp8 tensor index out of range");
@@ -455,6 +487,8 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
       R.ring = &T.land[0];  // counters only: CE publishes, the kernel verifies in place
     }
     R.stream = R.d->copy[s.direction];
+    R.roundtrip = s.op == kOpAdamW;
+    if (R.roundtrip) R.out = R.d->copy[1];
     for (const auto& c : L.chunks) R.bytes += c.bytes;
     R.chunks = L.chunks.size();
     P.bytes += R.bytes;
@@ -526,7 +560,9 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
       LaneDesc d{};
       d.ring = R.staged ? R.ring->base : nullptr;
       d.ready = R.ring ? R.ring->ready : nullptr;
-      d.freec = R.ring ? R.ring->freec : nullptr;
+      // a round trip's slots are freed by its copy-out stream, not the kernel
+      d.freec = R.ring && !R.roundtrip ? R.ring->freec : nullptr;
+      d.donec = R.roundtrip ? R.ring->donec : nullptr;
       d.slot_bytes = options_.slot_bytes;
       d.slots = static_cast<uint32_t>(options_.slots);
       d.chunk_begin = static_cast<uint32_t>(chunks_d.size());
@@ -589,6 +625,10 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
   for (auto& R : P.lanes) {
     R.t0 = take_event(*R.d);
     R.t1 = take_event(*R.d);
+    if (R.roundtrip) {
+      R.t_in = take_event(*R.d);
+      R.t_out = take_event(*R.d);
+    }
   }
 
   cudaStream_t tmain = T.main[s.direction];
@@ -607,6 +647,7 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     DeviceGuard lg(R.device);
     PPB_CUDA(cudaStreamWaitEvent(R.stream, P.start, 0));
     PPB_CUDA(cudaEventRecord(R.t0, R.stream));
+    if (R.roundtrip) PPB_CUDA(cudaStreamWaitEvent(R.out, P.start, 0));
   }
 
   // Pipelined (default): the kernel is queued before any copy-engine work so a
@@ -655,6 +696,16 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     kp.status = reinterpret_cast<int*>(dsc + o_status);
     kp.timeout_ns = static_cast<uint64_t>(P.timeout_s * 1e9);
     kp.trace = s.trace ? reinterpret_cast<unsigned long long*>(dsc + o_trace) : nullptr;
+    if (s.op == kOpAdamW) {
+      const auto& a = s.adam;
+      const double bc1 = 1.0 - std::pow(static_cast<double>(a.beta1), a.step);
+      const double bc2 = 1.0 - std::pow(static_cast<double>(a.beta2), a.step);
+      kp.grads = reinterpret_cast<const uint16_t*>(a.grads);
+      kp.params_out = reinterpret_cast<uint16_t*>(a.params);
+      kp.nparams = a.nparams;
+      kp.adam = AdamCoeffs{a.lr, a.beta1, a.beta2, a.eps, a.weight_decay, a.grad_scale,
+                           static_cast<float>(a.lr / bc1), static_cast<float>(1.0 / std::sqrt(bc2))};
+    }
     // Launch before any copy-engine work is queued: if the launch fails no
     // relay stream is left waiting for a kernel that never runs.
     const cudaError_t lrc = h2d ? launch_land(kp, static_cast<int>(cta), tkern)
@@ -736,6 +787,13 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
           stream_wait_geq(R.stream, R.ring->freec, seq - static_cast<uint32_t>(options_.slots), false);
           PPB_CUDA(cudaMemcpyAsync(slot, host + c.src_off, c.bytes, cudaMemcpyHostToDevice, R.stream));
           if (publish) stream_write(R.stream, R.ring->ready, seq);
+          if (R.roundtrip) {
+            // copy-out leg: once the kernel has updated the chunk in the slot
+            stream_wait_geq(R.out, R.ring->donec, seq, R.d->can_flush_remote_writes);
+            PPB_CUDA(cudaMemcpyAsync(const_cast<uint8_t*>(host) + c.src_off, slot, c.bytes,
+                                     cudaMemcpyDeviceToHost, R.out));
+            stream_write(R.out, R.ring->freec, seq);
+          }
         } else {
           PPB_CUDA(cudaMemcpyAsync(devp + c.dst_off, host + c.src_off, c.bytes, cudaMemcpyHostToDevice, R.stream));
           if (R.in_place && publish) stream_write(R.stream, R.ring->ready, seq);
@@ -755,11 +813,17 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
 
   for (auto& R : P.lanes) {
     DeviceGuard lg(R.device);
+    if (R.roundtrip) {
+      // the lane ends when its copy-out leg ends
+      PPB_CUDA(cudaEventRecord(R.t_in, R.stream));
+      PPB_CUDA(cudaEventRecord(R.t_out, R.out));
+      PPB_CUDA(cudaStreamWaitEvent(R.stream, R.t_out, 0));
+    }
     PPB_CUDA(cudaEventRecord(R.t1, R.stream));
   }
   if (kernel_after_copies && P.has_kernel) {
     DeviceGuard kg(s.target);
-    for (auto& R : P.lanes) PPB_CUDA(cudaStreamWaitEvent(tkern, R.t1, 0));
+    for (auto& R : P.lanes) PPB_CUDA(cudaStreamWaitEvent(tkern, R.roundtrip ? R.t_in : R.t1, 0));
     launch_kernel();
   }
   PPB_CUDA(cudaSetDevice(s.target));
@@ -827,6 +891,7 @@ TransferResult PoolEngine::wait(uint64_t id, double host_timeout_s) {
       if (cudaStreamCreateWithFlags(&rs, cudaStreamNonBlocking) == cudaSuccess) {
         cudaMemcpyAsync(r->ready, &v, 4, cudaMemcpyHostToDevice, rs);
         cudaMemcpyAsync(r->freec, &v, 4, cudaMemcpyHostToDevice, rs);
+        cudaMemcpyAsync(r->donec, &v, 4, cudaMemcpyHostToDevice, rs);
         cudaStreamSynchronize(rs);
         cudaStreamDestroy(rs);
       }
@@ -912,6 +977,8 @@ TransferResult PoolEngine::wait(uint64_t id, double host_timeout_s) {
   for (auto& R : P.lanes) {
     give_event(*R.d, R.t0);
     give_event(*R.d, R.t1);
+    give_event(*R.d, R.t_in);
+    give_event(*R.d, R.t_out);
   }
   if (done || cudaEventQuery(stop) == cudaSuccess) {
     give_scratch(T, P.scratch);

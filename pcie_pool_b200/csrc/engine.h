@@ -68,6 +68,20 @@ struct QuantTensorSpec {
   uint32_t cols = 0;
 };
 
+// Streamed optimizer step (op kOpAdamW): device tensors and hyper-parameters.
+struct AdamStepSpec {
+  uint64_t grads = 0;    // bf16 gradients on the target, nparams elements
+  uint64_t params = 0;   // bf16 parameters written on the target, nparams elements
+  uint64_t nparams = 0;
+  float lr = 1e-3f;
+  float beta1 = 0.9f;
+  float beta2 = 0.999f;
+  float eps = 1e-8f;
+  float weight_decay = 0.0f;
+  float grad_scale = 1.0f;
+  int step = 1;          // 1-based step count (bias correction)
+};
+
 struct TransferSpec {
   int direction = 0;     // 0 = H2D, 1 = D2H
   int target = 0;
@@ -95,6 +109,7 @@ struct TransferSpec {
   std::vector<uint32_t> range_bytes;
   std::vector<uint64_t> range_pos;    // start of each range inside its chunk stream
   std::vector<QuantTensorSpec> tensors;
+  AdamStepSpec adam;                  // kOpAdamW: host_ptr is the fp32 state image
 };
 
 struct LaneStats {
@@ -151,6 +166,7 @@ class PoolEngine {
     uint8_t* base = nullptr;
     uint32_t* ready = nullptr;
     uint32_t* freec = nullptr;
+    uint32_t* donec = nullptr;  // round trips: kernel -> copy-out
     uint64_t issued = 0;       // chunks ever published through this ring
     int last_dir = -1;
     int last_target = -1;
@@ -164,7 +180,7 @@ class PoolEngine {
     cudaStream_t main[2] = {nullptr, nullptr};
     cudaStream_t kern[2] = {nullptr, nullptr};
     cudaStream_t copy[2] = {nullptr, nullptr};
-    uint32_t* mbox = nullptr;  // 8 counters, each on its own 128-byte line
+    uint32_t* mbox = nullptr;  // 12 counters, each on its own 128-byte line
     Ring relay[2], land[2];
     std::vector<cudaEvent_t> free_events;
     // Lane-kernel scratch (descriptor tables, checksums, status, arrival

@@ -8,6 +8,7 @@
 
 #include "device_utils.cuh"
 #include "native_ops.h"
+#include "adamw.cuh"
 
 namespace ppb {
 namespace {
@@ -135,14 +136,11 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(float* __restrict__ mas
                                                          float lr, float b1, float b2, float eps,
                                                          float wd, float gscale, float step_size,
                                                          float inv_sqrt_bc2) {
+  const AdamCoeffs c{lr, b1, b2, eps, wd, gscale, step_size, inv_sqrt_bc2};
   const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
   for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n; i += stride) {
-    const float gr = __bfloat162float(g[i]) * gscale;
-    float p = master[i] * (1.0f - lr * wd);
-    const float mi = b1 * m[i] + (1.0f - b1) * gr;
-    const float vi = b2 * v[i] + (1.0f - b2) * gr * gr;
-    const float denom = sqrtf(vi) * inv_sqrt_bc2 + eps;
-    p -= step_size * (mi / denom);
+    float mi = m[i], vi = v[i];
+    const float p = adamw_update(mi, vi, master[i], __bfloat162float(g[i]), c);
     m[i] = mi;
     v[i] = vi;
     master[i] = p;

@@ -59,6 +59,7 @@ __global__ void noalloc_prepare(unsigned char* s, const uint8_t* src, uint64_t s
     L.cta_count = ctas;
     L.in_place = 0;
     L.slots = nchunks;
+    L.donec = nullptr;  // not a round trip
     *reinterpret_cast<LaneDesc*>(s + kOffLane) = L;
     *reinterpret_cast<uint32_t*>(s + kOffReady) = 1u;  // every chunk is published (seq 1)
     int* st = reinterpret_cast<int*>(s + kOffStatus);

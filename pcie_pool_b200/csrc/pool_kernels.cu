@@ -72,10 +72,15 @@ __device__ void copy_generic(const uint8_t* src, uint8_t* dst, uint64_t n, uint6
 // Pipelined bulk-copy loop over the tiles j, j+G, j+2G, ... of one chunk.
 // `q` is the CTA's running tile counter: stage = q % kStages and the mbarrier
 // phase parity = (q / kStages) & 1.  Returns false on a copy timeout.
-template <class Geom>
+struct NoXform {
+  static constexpr bool kActive = false;
+  __device__ void operator()(uint8_t*, const Tile&, uint32_t) const {}
+};
+
+template <class Geom, class Xform = NoXform>
 __device__ bool run_tiles(const Geom& geom, uint32_t ntiles, uint32_t j, uint32_t G, bool store,
                           bool do_csum, uint32_t& q, uint64_t* bars, uint8_t* smem,
-                          Csum& cs, uint64_t timeout_ns) {
+                          Csum& cs, uint64_t timeout_ns, const Xform& xform = Xform{}) {
   const uint32_t my_n = ntiles > j ? (ntiles - j + G - 1) / G : 0;
   if (my_n == 0) return true;
   const uint32_t base = q;
@@ -105,6 +110,12 @@ __device__ bool run_tiles(const Geom& geom, uint32_t ntiles, uint32_t j, uint32_
       const uint32_t nv = t.n >> 4;
       const uint64_t w0 = t.pos >> 2;
       for (uint32_t i = threadIdx.x; i < nv; i += blockDim.x) csum_vec(cs, v[i], w0 + 4ull * i);
+    }
+    if constexpr (Xform::kActive) {
+      if (do_csum) __syncthreads();  // the checksum reads the tile as it arrived
+      xform(stage, t, j + k * G);
+      // generic-proxy writes of the stage become visible to the bulk store
+      fence_proxy_async_smem();
     }
     __syncthreads();  // every reader is done with this stage
     if (threadIdx.x == 0) {
@@ -180,6 +191,71 @@ struct RangeGeom {
     uint8_t* ra = reinterpret_cast<uint8_t*>(range_addr[k]);
     if (scatter) return Tile{stream_src + pos, ra, pos, n};
     return Tile{ra, stream_dst ? stream_dst + pos : nullptr, pos, n};
+  }
+};
+
+// Streamed optimizer: tile k of a chunk is updated in its staging slot.
+struct AdamGeom {
+  uint8_t* slot;
+  __device__ Tile operator()(uint32_t k) const {
+    const uint32_t off = k * kAdamTileBytes;
+    return Tile{slot + off, slot + off, off, kAdamTileBytes};
+  }
+};
+
+// AdamW on one staged tile: [master | exp_avg | exp_avg_sq] fp32 in shared
+// memory, bf16 gradient read from global memory, updated state written back
+// into the stage (the bulk store returns it to the slot) and the bf16
+// parameter written to global memory.  Thread t owns parameters 4t..4t+3 and
+// 1024+4t..1024+4t+3 of the tile (float4 / 8-byte vector accesses).
+struct AdamXform {
+  static constexpr bool kActive = true;
+  const uint16_t* grads;
+  uint16_t* params;
+  uint64_t nparams;
+  uint32_t tile0;  // first tile of the chunk
+  AdamCoeffs c;
+  __device__ void operator()(uint8_t* stage, const Tile&, uint32_t k) const {
+    float* M = reinterpret_cast<float*>(stage);
+    float* A = M + kAdamTileParams;
+    float* V = A + kAdamTileParams;
+    const uint64_t base = uint64_t(tile0 + k) * kAdamTileParams;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const uint32_t i0 = r * (kAdamTileParams / 2) + 4u * threadIdx.x;
+      const uint64_t gi = base + i0;
+      if (gi >= nparams) continue;
+      if (gi + 4 <= nparams) {
+        const uint2 graw = *reinterpret_cast<const uint2*>(grads + gi);
+        const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&graw);
+        const float2 g01 = __bfloat1622float2(gh[0]);
+        const float2 g23 = __bfloat1622float2(gh[1]);
+        float4 m = *reinterpret_cast<float4*>(M + i0);
+        float4 a = *reinterpret_cast<float4*>(A + i0);
+        float4 v = *reinterpret_cast<float4*>(V + i0);
+        m.x = adamw_update(a.x, v.x, m.x, g01.x, c);
+        m.y = adamw_update(a.y, v.y, m.y, g01.y, c);
+        m.z = adamw_update(a.z, v.z, m.z, g23.x, c);
+        m.w = adamw_update(a.w, v.w, m.w, g23.y, c);
+        *reinterpret_cast<float4*>(M + i0) = m;
+        *reinterpret_cast<float4*>(A + i0) = a;
+        *reinterpret_cast<float4*>(V + i0) = v;
+        __nv_bfloat162 p01 = __floats2bfloat162_rn(m.x, m.y);
+        __nv_bfloat162 p23 = __floats2bfloat162_rn(m.z, m.w);
+        uint2 praw;
+        praw.x = *reinterpret_cast<uint32_t*>(&p01);
+        praw.y = *reinterpret_cast<uint32_t*>(&p23);
+        *reinterpret_cast<uint2*>(params + gi) = praw;
+      } else {
+        for (uint32_t e = 0; e < 4 && gi + e < nparams; ++e) {
+          const float g = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(grads + gi + e));
+          const float p = adamw_update(A[i0 + e], V[i0 + e], M[i0 + e], g, c);
+          M[i0 + e] = p;
+          const __nv_bfloat16 pb = __float2bfloat16_rn(p);
+          params[gi + e] = *reinterpret_cast<const uint16_t*>(&pb);
+        }
+      }
+    }
   }
 };
 
@@ -328,8 +404,10 @@ __global__ void __launch_bounds__(kLaneThreads, 1) land_kernel(const LaneKernelP
     if (!s_ok) {
       if (threadIdx.x == 0) {
         record_error(p.status, kStatusReadyTimeout, lane, static_cast<int>(cidx), int(c.seq));
-        // Unblock the producer for every remaining chunk of this lane.
+        // Unblock the producer (and a round trip's copy-out) for every
+        // remaining chunk of this lane.
         if (L.freec) st_release_sys(L.freec, c.seq + 0x40000000u);
+        if (L.donec) st_release_sys(L.donec, c.seq + 0x40000000u);
       }
       return;
     }
@@ -358,18 +436,33 @@ __global__ void __launch_bounds__(kLaneThreads, 1) land_kernel(const LaneKernelP
       case kOpFp8Quant:
         ok = land_fp8_chunk(p, c, src, j, G, do_csum, cs, fred);
         break;
+      case kOpAdamW:
+        ok = !L.in_place &&
+             run_tiles(AdamGeom{const_cast<uint8_t*>(src)}, c.bytes / kAdamTileBytes, j, G, true, do_csum,
+                       q, bars, smem, cs, p.timeout_ns,
+                       AdamXform{p.grads, p.params_out, p.nparams, c.unit0, p.adam});
+        break;
       default:
         ok = false;
     }
     if (!ok) {
       if (threadIdx.x == 0) {
-        record_error(p.status, p.op > kOpScatterRanges ? kStatusBadArgument : kStatusCopyTimeout,
-                     lane, static_cast<int>(cidx), int(c.seq));
+        const bool timed_out = p.op <= kOpScatterRanges || p.op == kOpAdamW;
+        record_error(p.status, timed_out ? kStatusCopyTimeout : kStatusBadArgument, lane,
+                     static_cast<int>(cidx), int(c.seq));
         if (L.freec) st_release_sys(L.freec, c.seq + 0x40000000u);
+        if (L.donec) st_release_sys(L.donec, c.seq + 0x40000000u);
       }
       return;
     }
     if (do_csum) csum_block_commit(cs, p.csum + 2ull * cidx, red);
+    if (L.donec && threadIdx.x == 0) {
+      // round trip: the updated tiles must sit in the slot before the
+      // copy-out stream is told to read them
+      bulk_wait_all<0>();
+      fence_proxy_async_global();
+      fence_sys();
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
       const uint32_t old = G > 1 ? atom_add_acq_rel_gpu(p.done + cidx, 1u) : 0u;
@@ -378,7 +471,11 @@ __global__ void __launch_bounds__(kLaneThreads, 1) land_kernel(const LaneKernelP
           p.trace[uint64_t(kTraceWords) * cidx + 2] = globaltimer_ns();
           p.trace[uint64_t(kTraceWords) * cidx + 3] = G;
         }
-        if (L.freec) st_release_sys(L.freec, c.seq);
+        if (L.donec) {
+          st_release_sys(L.donec, c.seq);
+        } else if (L.freec) {
+          st_release_sys(L.freec, c.seq);
+        }
       }
     }
   }

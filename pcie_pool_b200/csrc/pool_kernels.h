@@ -19,6 +19,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "adamw.cuh"
+
 namespace ppb {
 
 enum LaneOp : uint32_t {
@@ -28,7 +30,16 @@ enum LaneOp : uint32_t {
   kOpFp8Quant = 3,      // H2D: bf16 rows -> fp8 e4m3 + fp32 per-128x128 scales
   kOpScatterRanges = 4, // H2D: variable ranges -> range_addr (unpack)
   kOpGatherRanges = 5,  // D2H: variable ranges -> contiguous (pack)
+  kOpAdamW = 6,         // H2D round trip: fp32 optimizer-state tiles are updated in
+                        // their staging slot with the local bf16 grads (bf16 params
+                        // out), then copied back to the host (streamed optimizer step)
 };
+
+// Streamed-optimizer state layout, host and slot: tiles of kAdamTileParams
+// parameters, each [master | exp_avg | exp_avg_sq] as fp32 (24 KiB, one
+// shared-memory stage).  Parameter i lives in tile i / kAdamTileParams.
+constexpr uint32_t kAdamTileParams = 2048;
+constexpr uint32_t kAdamTileBytes = 3u * 4u * kAdamTileParams;
 
 enum StatusCode : int {
   kStatusOk = 0,
@@ -50,6 +61,9 @@ struct LaneDesc {
   uint32_t cta_count;
   uint32_t in_place;      // 1: no staging, the data sits at its final place
   uint32_t slots;
+  // Round trip (kOpAdamW): the kernel publishes a processed chunk here for the
+  // copy-out stream, which frees the slot itself (freec is then unused).
+  uint32_t* donec;
 };
 
 struct ChunkDesc {
@@ -94,6 +108,11 @@ struct LaneKernelParams {
   // published / push: slot free), chunk done (last CTA of the lane group),
   // CTAs that finished the chunk}.
   unsigned long long* trace;
+  // kOpAdamW: local bf16 gradients in, bf16 parameters out (nparams each)
+  const uint16_t* grads;
+  uint16_t* params_out;
+  uint64_t nparams;
+  AdamCoeffs adam;
 };
 
 constexpr int kTraceWords = 4;

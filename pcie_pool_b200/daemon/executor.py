@@ -179,7 +179,16 @@ class EngineDataPlane:
 
             C = native()
             annotate_lanes(spec, lanes, h2d)
-            if spec.units_op:
+            if spec.op == "adamw":
+                a = spec.adam_params
+                regs = dict(buffers or {})
+                if a["grads_buffer"] not in regs:
+                    raise RuntimeError("adamw grads buffer is no longer registered")
+                adam = {k: a[k] for k in ("lr", "beta1", "beta2", "eps", "weight_decay", "grad_scale", "step")}
+                adam.update(grads=self.device_pointer(regs[a["grads_buffer"]]), params=dev_ptr,
+                            nparams=int(a["nparams"]))
+                op_kw = {"op": C.OP_ADAMW, "adam": adam}
+            elif spec.units_op:
                 regs = dict(buffers or {})
                 regs.setdefault(dev_buf.buffer_id, dev_buf)
                 missing = [b for b in spec.buffer_ids() if b not in regs]
@@ -204,7 +213,9 @@ class EngineDataPlane:
         failover = None
         lane_stats = list(r.lanes)
         checksums = None if r.checksums is None else np.array(r.checksums, dtype=np.uint64, copy=True)
-        if not r.ok and self.failover and len(lanes) > 1 and 0 <= r.error_lane < len(lanes):
+        # an optimizer round trip is not idempotent: its lanes are never re-run
+        idempotent = spec is None or spec.op != "adamw"
+        if not r.ok and self.failover and idempotent and len(lanes) > 1 and 0 <= r.error_lane < len(lanes):
             # Lane failover: the chunks of the lane that failed are moved again
             # over a surviving lane (the direct lane when it survived).  Every
             # op here is a pure data movement, so chunks of the failed lane

@@ -11,6 +11,11 @@ in the same pass, under the same plan, leases and ticket as any intent:
   into one host-contiguous region;
 * ``fp8_quant`` (H2D): bf16 matrices land as fp8 e4m3 codes plus one fp32
   scale per 128x128 block, quantised in the landing kernel;
+* ``adamw`` (H2D round trip): the host range is fp32 optimizer state in
+  24 KiB tiles ``[master | exp_avg | exp_avg_sq]`` x 2048 parameters; each
+  tile is updated on the GPU with the bf16 gradients of a registered buffer,
+  the intent's device buffer receives the bf16 parameters, and the tile
+  returns to the host (adapters/streamed_optimizer.py);
 * ``copy``: the plain op (the default without a spec).
 
 The reference has no such path: its KV connector and model loader submit
@@ -46,8 +51,11 @@ from collections.abc import Mapping
 from dataclasses import dataclass, field
 from typing import Any, Sequence
 
-OPS = ("copy", "scatter_units", "gather_units", "fp8_quant")
+OPS = ("copy", "scatter_units", "gather_units", "fp8_quant", "adamw")
 TILE_ROWS = 128
+ADAM_TILE_PARAMS = 2048
+ADAM_TILE_BYTES = 3 * 4 * ADAM_TILE_PARAMS
+ADAM_KEYS = ("lr", "beta1", "beta2", "eps", "weight_decay", "grad_scale", "step")
 
 
 @dataclass(frozen=True)
@@ -92,6 +100,9 @@ class LandingSpec:
     kv: KVUnits | None = None
     tensors: tuple[Fp8Tensor, ...] = field(default_factory=tuple)
     ctas_per_lane: int = 0
+    # adamw: {"grads_buffer", "nparams", "lr", "beta1", "beta2", "eps",
+    # "weight_decay", "grad_scale", "step"}
+    adam: tuple[tuple[str, Any], ...] = ()
 
     # ---- wire form ------------------------------------------------------------------
     @classmethod
@@ -124,8 +135,22 @@ class LandingSpec:
                                          int(t["q_offset"]), int(t["scales_offset"])))
             except (KeyError, TypeError, ValueError) as exc:
                 raise ValueError(f"landing fp8 tensor is incomplete: {exc}") from None
+        adam = ()
+        if d.get("adam") is not None:
+            a = d["adam"]
+            if not isinstance(a, Mapping):
+                raise ValueError("landing adam parameters must be an object")
+            try:
+                vals = {"grads_buffer": str(a["grads_buffer"]), "nparams": int(a["nparams"]),
+                        "step": int(a.get("step", 1))}
+                for k in ADAM_KEYS[:-1]:
+                    vals[k] = float(a.get(k, {"lr": 1e-3, "beta1": 0.9, "beta2": 0.999, "eps": 1e-8,
+                                              "weight_decay": 0.0, "grad_scale": 1.0}[k]))
+            except (KeyError, TypeError, ValueError) as exc:
+                raise ValueError(f"landing adam parameters are incomplete: {exc}") from None
+            adam = tuple(sorted(vals.items()))
         return cls(op=op, unit_bytes=int(d.get("unit_bytes", 0) or 0), kv=kv, tensors=tuple(tensors),
-                   ctas_per_lane=int(d.get("ctas_per_lane", 0) or 0))
+                   ctas_per_lane=int(d.get("ctas_per_lane", 0) or 0), adam=adam)
 
     def to_metadata(self) -> dict[str, Any]:
         d: dict[str, Any] = {"op": self.op}
@@ -140,13 +165,21 @@ class LandingSpec:
                              "q_offset": t.q_offset, "scales_offset": t.scales_offset} for t in self.tensors]
         if self.ctas_per_lane:
             d["ctas_per_lane"] = self.ctas_per_lane
+        if self.adam:
+            d["adam"] = dict(self.adam)
         return d
+
+    @property
+    def adam_params(self) -> dict[str, Any]:
+        return dict(self.adam)
 
     @property
     def units_op(self) -> bool:
         return self.op in ("scatter_units", "gather_units")
 
     def buffer_ids(self) -> tuple[str, ...]:
+        if self.op == "adamw" and self.adam:
+            return (str(self.adam_params["grads_buffer"]),)
         return self.kv.buffers if self.kv is not None else ()
 
 
@@ -163,6 +196,8 @@ def validate_landing(spec: LandingSpec, *, direction: str, job_id: str, device_b
         raise ValueError(f"landing op {spec.op} lands data: h2d only")
     if spec.op == "gather_units" and h2d:
         raise ValueError("landing op gather_units pushes data: d2h only")
+    if spec.op == "adamw" and not h2d:
+        raise ValueError("landing op adamw is an h2d round trip")
     if spec.ctas_per_lane < 0 or spec.ctas_per_lane > 64:
         raise ValueError("landing ctas_per_lane must be between 0 and 64")
     rs = list(ranges) if ranges is not None else [{"src_offset": 0, "dst_offset": 0, "bytes": int(total_bytes)}]
@@ -172,6 +207,9 @@ def validate_landing(spec: LandingSpec, *, direction: str, job_id: str, device_b
     elif spec.op == "fp8_quant":
         _validate_fp8(spec, device_buffer=device_buffer, host_buffer=host_buffer, ranges=rs,
                       chunk_bytes=chunk_bytes)
+    elif spec.op == "adamw":
+        _validate_adam(spec, job_id=job_id, device_buffer=device_buffer, host_buffer=host_buffer, ranges=rs,
+                       chunk_bytes=chunk_bytes, buffers=buffers)
 
 
 def _validate_units(spec, *, job_id, device_buffer, ranges, h2d, chunk_bytes, buffers) -> None:
@@ -242,6 +280,33 @@ def _validate_fp8(spec, *, device_buffer, host_buffer, ranges, chunk_bytes) -> N
             raise ValueError("fp8 landing ranges must be whole 128-row tiles of one tensor")
 
 
+def _validate_adam(spec, *, job_id, device_buffer, host_buffer, ranges, chunk_bytes, buffers) -> None:
+    a = spec.adam_params
+    if not a:
+        raise ValueError("adamw landing needs its adam parameters")
+    n = int(a["nparams"])
+    if n <= 0 or int(a["step"]) < 1:
+        raise ValueError("adamw needs nparams > 0 and step >= 1")
+    g = buffers.get(a["grads_buffer"])
+    if g is None:
+        raise ValueError(f"adamw grads buffer {a['grads_buffer']} is not registered")
+    if g.job_id != job_id:
+        raise ValueError("adamw grads buffer belongs to another job")
+    if g.device_index != device_buffer.device_index or str(g.kind).lower() != str(device_buffer.kind).lower():
+        raise ValueError("adamw grads buffer is not on the intent's device")
+    if int(g.size_bytes) < 2 * n or int(device_buffer.size_bytes) < 2 * n:
+        raise ValueError("adamw grads and params buffers must hold nparams bf16 values")
+    tiles = -(-n // ADAM_TILE_PARAMS)
+    if int(host_buffer.size_bytes) < tiles * ADAM_TILE_BYTES:
+        raise ValueError("adamw host state is smaller than the tiled optimizer state")
+    if chunk_bytes % ADAM_TILE_BYTES:
+        raise ValueError("adamw chunk_bytes must be a whole number of 24 KiB state tiles")
+    for r in ranges:
+        s, d, b = int(r["src_offset"]), int(r["dst_offset"]), int(r["bytes"])
+        if s != d or s % ADAM_TILE_BYTES or b % ADAM_TILE_BYTES or s + b > tiles * ADAM_TILE_BYTES:
+            raise ValueError("adamw ranges must be whole state tiles with dst_offset == src_offset")
+
+
 # ---- executor side ------------------------------------------------------------------------
 
 def unit_addresses(spec: LandingSpec, base_of) -> "Any":
@@ -269,6 +334,9 @@ def annotate_lanes(spec: LandingSpec, lanes, h2d: bool) -> None:
         for L in lanes:
             pos = L.dst_off if h2d else L.src_off
             L.unit0 = (pos // u).astype(np.uint32)
+    elif spec.op == "adamw":
+        for L in lanes:
+            L.unit0 = (L.src_off // np.uint64(ADAM_TILE_BYTES)).astype(np.uint32)
     elif spec.op == "fp8_quant":
         order = sorted(range(len(spec.tensors)), key=lambda i: spec.tensors[i].host_offset)
         starts = np.array([spec.tensors[i].host_offset for i in order], dtype=np.int64)

@@ -187,10 +187,15 @@ class _MockLanding:
         buffers.setdefault(self.dev.buffer_id, self.dev)
         if spec.units_op:
             self.units = unit_addresses(spec, lambda b: int(buffers[b].address))
+        if spec.op == "adamw":
+            self.grads = int(buffers[spec.adam_params["grads_buffer"]].address)
 
     def move(self, so: int, do: int, n: int) -> None:
         spec = self.spec
         hbase = int(self.host.address)
+        if spec.op == "adamw":
+            self._adamw(hbase, so, n)
+            return
         if spec.units_op:
             u = spec.unit_bytes
             host_off, pos = (so, do) if self.h2d else (do, so)
@@ -216,6 +221,39 @@ class _MockLanding:
         dbase = int(self.dev.address)
         ctypes.memmove(dbase + t.q_offset + row0 * t.cols, q.ctypes.data, q.nbytes)
         ctypes.memmove(dbase + t.scales_offset + (row0 // 128) * (t.cols // 128) * 4, sc.ctypes.data, sc.nbytes)
+
+
+    def _adamw(self, hbase: int, so: int, n: int) -> None:
+        """The kernel's AdamW (float32, same operation order) on host tiles."""
+        from ..daemon.landing import ADAM_TILE_BYTES, ADAM_TILE_PARAMS
+
+        a = self.spec.adam_params
+        f32 = np.float32
+        lr, b1, b2, eps, wd, gs = (f32(a[k]) for k in ("lr", "beta1", "beta2", "eps", "weight_decay", "grad_scale"))
+        t = int(a["step"])
+        step_size = f32(float(a["lr"]) / (1.0 - float(a["beta1"]) ** t))
+        inv_sqrt_bc2 = f32(1.0 / np.sqrt(1.0 - float(a["beta2"]) ** t))
+        nparams = int(a["nparams"])
+        tiles = n // ADAM_TILE_BYTES
+        st = np.ctypeslib.as_array((ctypes.c_float * (n // 4)).from_address(hbase + so)).reshape(tiles, 3,
+                                                                                               ADAM_TILE_PARAMS)
+        p0 = so // ADAM_TILE_BYTES * ADAM_TILE_PARAMS
+        cnt = max(0, min(tiles * ADAM_TILE_PARAMS, nparams - p0))
+        graw = np.ctypeslib.as_array((ctypes.c_uint16 * cnt).from_address(self.grads + 2 * p0))
+        g = (graw.astype(np.uint32) << 16).view(np.float32) * gs
+        flat = st.transpose(1, 0, 2).reshape(3, -1)[:, :cnt].copy()
+        mast, m, v = flat
+        p = mast * (f32(1.0) - lr * wd)
+        m = b1 * m + (f32(1.0) - b1) * g
+        v = b2 * v + (f32(1.0) - b2) * g * g
+        p = p - step_size * (m / (np.sqrt(v) * inv_sqrt_bc2 + eps))
+        full = st.transpose(1, 0, 2).reshape(3, -1).copy()
+        full[0, :cnt], full[1, :cnt], full[2, :cnt] = p, m, v
+        st[:] = full.reshape(3, tiles, ADAM_TILE_PARAMS).transpose(1, 0, 2)
+        bits = p.astype(np.float32).view(np.uint32)
+        rounded = ((bits + np.uint32(0x7FFF) + ((bits >> 16) & np.uint32(1))) >> 16).astype(np.uint16)
+        out = np.ctypeslib.as_array((ctypes.c_uint16 * cnt).from_address(int(self.dev.address) + 2 * p0))
+        out[:] = rounded
 
 
 def chunk_lane_map(trace: list[dict[str, Any]]) -> dict[int, int]:

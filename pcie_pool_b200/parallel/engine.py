@@ -130,6 +130,7 @@ class PoolEngine:
                unit_bytes: int = 0, unit_addrs: np.ndarray | None = None,
                ranges: tuple[np.ndarray, np.ndarray, np.ndarray] | None = None,
                tensors: Sequence[tuple[int, int, int, int]] = (),
+               adam: Mapping | None = None,
                debug_drop_publish: int = -1, trace: bool = False) -> int:
         C = self._C
         spec = C.TransferSpec()
@@ -161,6 +162,11 @@ class PoolEngine:
             t.q, t.scales, t.rows, t.cols = int(q), int(scales), int(rows), int(cols)
             qts.append(t)
         spec.tensors = qts
+        if adam is not None:
+            a = C.AdamStepSpec()
+            for k, v in adam.items():
+                setattr(a, k, v)
+            spec.adam = a
         nl = []
         for lane in lanes:
             ls = C.LaneSpec()
