@@ -16,6 +16,14 @@ their links.  Reported: step time (wall, all transfers of all active jobs),
 per-job time and Jain's fairness index over per-job throughput, relay share,
 and the daemon's state afterwards (no reservation or quota may leak).
 
+``--optimizer streamed-adamw`` (ours): every step is the optimizer step
+itself -- per GPU shard one AdamW round-trip intent: the fp32 master weights
+and Adam moments stream host -> GPU over the direct and leased relay lanes,
+the landing kernel updates them with the shard's local bf16 gradients and
+writes the bf16 parameters in place, and the state streams back (12 bytes per
+parameter each way; adapters/streamed_optimizer.py).  A slice of every shard
+is checked against torch.optim.AdamW.
+
 ``--impl reference``: the same transfers through the reference's own
 runtime, one warm ``Runtime`` per GPU with every other GPU as a relay
 candidate and plans from its own planner; there is no arbitration between
@@ -43,6 +51,8 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=1)
     p.add_argument("--chunk", type=int, default=16 << 20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--optimizer", choices=["none", "streamed-adamw"], default="none",
+                   help="ours: run the AdamW step on the offload path instead of plain grads/params moves")
     p.add_argument("--json-out", default="")
     return p.parse_args(argv)
 
@@ -170,6 +180,8 @@ def run_ours(a) -> dict:
     client = TurboBusClient(daemon=dc)
     active = gpus[:(a.active_jobs or a.jobs) * a.gpus_per_job]
     rng = ({"src_offset": 0, "dst_offset": 0, "bytes": T.n},)
+    if a.optimizer == "streamed-adamw":
+        return _run_streamed_adamw(a, T, dc, client, sessions, active, gpus)
     counter = iter(range(1 << 30))
     pool = ThreadPoolExecutor(max_workers=2 * len(active))
 
@@ -222,6 +234,79 @@ def run_ours(a) -> dict:
            "relay_share": round(relay_b / max(1, total_b), 4), "verified": verified,
            "leaked_quota_chunks": leaked, "open_reservations": len(desc["reservations"]),
            "shard_bytes": T.n, "active_gpus": active}
+    T.release()
+    return out
+
+
+ADAM_KW = dict(lr=1e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+CHECK_PARAMS = 64 * 2048
+
+
+def _run_streamed_adamw(a, T, dc, client, sessions, active, gpus) -> dict:
+    import torch
+
+    from ..adapters.streamed_optimizer import TILE_BYTES, StreamedAdamW
+
+    opts, p0 = {}, {}
+    for g in active:
+        # start from the host image of the parameters (the device copy is uninitialised)
+        T.dev_params[g].copy_(torch.from_numpy(T.host_params[g].numpy()))
+        torch.cuda.synchronize(g)
+        params = T.dev_params[g].view(torch.bfloat16)
+        p0[g] = params[:CHECK_PARAMS].cpu().clone()
+        opts[g] = StreamedAdamW(params, client=client, daemon_client=dc, session_id=sessions[g],
+                                job_id=shard_job(T.job_of[g], g), chunk_bytes=max(TILE_BYTES, a.chunk // TILE_BYTES
+                                                                                   * TILE_BYTES),
+                                prefix=f"opt{g}", **ADAM_KW)
+    pool = ThreadPoolExecutor(max_workers=len(active))
+    grads = {g: T.dev_grads[g].view(torch.bfloat16) for g in active}
+
+    def one(g):
+        t0 = time.perf_counter()
+        st = opts[g].step(grads[g])
+        return g, time.perf_counter() - t0, st
+
+    def step():
+        t0 = time.perf_counter()
+        res = [f.result() for f in [pool.submit(one, g) for g in active]]
+        return time.perf_counter() - t0, res
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(len(gpus)).start()
+    steps = [step() for _ in range(a.steps)]
+    clk = clocks.stop()
+    pool.shutdown()
+    desc = dc.describe().payload
+    leaked = {k: q["active_chunks"] for k, q in desc["relay_quotas"].items() if q["active_chunks"]}
+    per_job, relay_b, total_b, dev_ms = {}, 0, 0, []
+    for _dt, res in steps:
+        for g, secs, st in res:
+            j = T.job_of[g]
+            per_job[j] = max(per_job.get(j, 0.0), secs)
+            dev_ms.append(st.cuda_ms)
+            for dev, nb, _ms in st.lanes:
+                total_b += int(nb or 0)
+                relay_b += int(nb or 0) if dev not in (-1, None) else 0
+    # a slice of every shard against torch.optim.AdamW (same gradient every step)
+    verified = True
+    nsteps = a.warmup + a.steps
+    for g in active:
+        ref = torch.nn.Parameter(p0[g].float())
+        o = torch.optim.AdamW([ref], **ADAM_KW)
+        gr = grads[g][:CHECK_PARAMS].float().cpu()
+        for _ in range(nsteps):
+            ref.grad = gr
+            o.step()
+        got = opts[g].state()["master"][:CHECK_PARAMS]
+        verified &= bool(torch.allclose(got, ref.detach(), rtol=1e-5, atol=1e-7))
+    out = {"step_s": [round(dt, 4) for dt, _ in steps], "per_job_s": per_job, "clocks": clk,
+           "relay_share": round(relay_b / max(1, total_b), 4), "verified": verified,
+           "leaked_quota_chunks": leaked, "open_reservations": len(desc["reservations"]),
+           "shard_bytes": opts[active[0]].tiles * TILE_BYTES, "active_gpus": active,
+           "optimizer": "streamed-adamw", "params_per_gpu": opts[active[0]].nparams,
+           "step_device_ms_median": round(statistics.median(dev_ms), 3)}
     T.release()
     return out
 
@@ -310,13 +395,18 @@ def main(argv=None) -> int:
     step = statistics.median(res["step_s"])
     nbytes = 2 * res["shard_bytes"] * len(res["active_gpus"])
     per_job = res["per_job_s"]
-    line = {"metric": "multi-tenant training offload step (bf16 grads D2H + params H2D, all jobs)",
+    metric = ("multi-tenant training offload step (bf16 grads D2H + params H2D, all jobs)"
+              if res.get("optimizer") is None else
+              "multi-tenant streamed AdamW step (fp32 state H2D + D2H, fused update, all jobs)")
+    line = {"metric": metric,
             "value": round(step * 1e3, 2), "unit": "ms", "higher_is_better": False, "impl": a.impl,
             "n_gpus": len(res["active_gpus"]), "steps": a.steps, "warmup": a.warmup,
             "aggregate_gb_per_s": round(nbytes / 1e9 / step, 2), "per_job_ms": {f"job{k}": round(v * 1e3, 1)
                                                                                 for k, v in per_job.items()},
             "jain_fairness": round(jain([1.0 / v for v in per_job.values()]), 4),
             "relay_share": res.get("relay_share"), "verified": res["verified"], "clocks": res["clocks"],
+            "optimizer": res.get("optimizer", "none"), "params_per_gpu": res.get("params_per_gpu"),
+            "step_device_ms_median": res.get("step_device_ms_median"),
             "leaked_quota_chunks": res.get("leaked_quota_chunks"), "open_reservations": res.get("open_reservations"),
             "config": {"model": f"decoder-7b ({a.layers} layers) data-parallel x{a.gpus_per_job}",
                        "jobs": a.jobs, "gpus_per_job": a.gpus_per_job, "active_jobs": a.active_jobs or a.jobs,
