@@ -1,36 +1,38 @@
-"""Observation hooks for a running vLLM (V1) process.
+"""Observe a running vLLM (V1) process without taking anything over.
 
-``VllmTurboBusIntegration.install()`` wraps ``GPUModelRunner.initialize_kv_cache``
-(to see the KV tensors) and ``KVCacheManager.allocate_slots`` (to see each
-request's block ids); vLLM keeps owning scheduling and KV allocation.  The
-observed tensors and ids feed the KV slot adapter (intent path) or the
-paged-KV offloader (engine path).  API as turbobus/adapters/vllm_integration.py.
+Two vLLM methods are wrapped so that their results are also reported here:
+``GPUModelRunner.initialize_kv_cache`` (the KV tensors, once they exist) and
+``KVCacheManager.allocate_slots`` (every request's block ids, as vLLM hands
+them out).  vLLM keeps scheduling and allocating; this module only records
+what it sees and turns a request's blocks into the KV slot adapter's block
+references.  The public surface (class names, methods, the
+``_turbobus_integration`` class attribute) follows the reference's module
+turbobus/adapters/vllm_integration.py so existing deployments keep working.
 """
 
 from __future__ import annotations
 
 import functools
 from dataclasses import dataclass, field
+from itertools import zip_longest
 from typing import Callable, Iterable
 
 from ..offload_store import AdapterTransferContext, TransferIntentClient
 from .vllm import (VllmKVBlockRef, VllmKVSlotAdapter, block_bytes_from_vllm_kv_tensor,
                    make_vllm_layer_block_refs_from_ids, make_vllm_layer_groups_from_kv_caches)
 
+_HOOK_ATTR = "_turbobus_integration"
 
-def _dedup(ids: Iterable[int]) -> tuple[int, ...]:
-    seen: set[int] = set()
-    out = []
-    for b in ids:
-        if b not in seen:
-            seen.add(b)
-            out.append(b)
-    return tuple(out)
+
+def _unique(ids: Iterable[int]) -> tuple[int, ...]:
+    """Ids in first-seen order, each once."""
+    return tuple(dict.fromkeys(ids))
 
 
 @dataclass(frozen=True)
 class VllmAllocationEvent:
-    """Block ids vLLM allocated for one request, per KV cache group."""
+    """Everything vLLM has allocated to one request so far, per KV cache
+    group; ``event_count`` counts the allocations folded in."""
 
     request_id: str
     block_ids_by_group: tuple[tuple[int, ...], ...]
@@ -38,18 +40,15 @@ class VllmAllocationEvent:
 
     @property
     def block_ids(self) -> tuple[int, ...]:
-        return _dedup(b for g in self.block_ids_by_group for b in g)
+        return _unique(b for group in self.block_ids_by_group for b in group)
 
     def merge(self, other: "VllmAllocationEvent") -> "VllmAllocationEvent":
+        """Fold a later allocation of the same request into this one."""
         if other.request_id != self.request_id:
-            raise ValueError("cannot merge allocation events for different requests")
-        n = max(len(self.block_ids_by_group), len(other.block_ids_by_group))
-
-        def grp(ev, i):
-            return ev.block_ids_by_group[i] if i < len(ev.block_ids_by_group) else ()
-
-        return VllmAllocationEvent(self.request_id, tuple(_dedup((*grp(self, i), *grp(other, i))) for i in range(n)),
-                                   event_count=self.event_count + other.event_count)
+            raise ValueError(f"allocation events of {self.request_id!r} and {other.request_id!r} do not merge")
+        groups = tuple(_unique((*mine, *theirs)) for mine, theirs in
+                       zip_longest(self.block_ids_by_group, other.block_ids_by_group, fillvalue=()))
+        return VllmAllocationEvent(self.request_id, groups, self.event_count + other.event_count)
 
 
 AllocationCallback = Callable[["VllmTurboBusIntegration", object, object, VllmAllocationEvent], None]
@@ -63,6 +62,27 @@ class VllmIntegrationState:
     adapter: VllmKVSlotAdapter | None = None
 
 
+def _wrap_once(cls, method: str, report: Callable) -> None:
+    """Replace ``cls.method`` (once) by a wrapper that calls the original and
+    then ``report(integration, instance, args, kwargs, result)`` when an
+    integration is attached to the instance's class."""
+    saved = f"_turbobus_original_{method}"
+    if hasattr(cls, saved):
+        return
+    original = getattr(cls, method)
+    setattr(cls, saved, original)
+
+    @functools.wraps(original)
+    def hooked(obj, *args, **kwargs):
+        result = original(obj, *args, **kwargs)
+        integration = getattr(type(obj), _HOOK_ATTR, None)
+        if integration is not None:
+            report(integration, obj, args, kwargs, result)
+        return result
+
+    setattr(cls, method, hooked)
+
+
 class VllmTurboBusIntegration:
     def __init__(self, client: TransferIntentClient, transfer_context: AdapterTransferContext,
                  cpu_backings: Iterable | None = None) -> None:
@@ -72,155 +92,133 @@ class VllmTurboBusIntegration:
         self._cpu_backings = None if cpu_backings is None else list(cpu_backings)
         self._callback: AllocationCallback | None = None
 
+    # ---- hooking ------------------------------------------------------------------------
     def install(self) -> None:
-        from vllm.v1.core import kv_cache_manager as manager_module
-        from vllm.v1.worker import gpu_model_runner as runner_module
+        from vllm.v1.core import kv_cache_manager
+        from vllm.v1.worker import gpu_model_runner
 
-        self.install_on_classes(runner_module.GPUModelRunner, manager_module.KVCacheManager)
+        self.install_on_classes(gpu_model_runner.GPUModelRunner, kv_cache_manager.KVCacheManager)
 
     def install_on_classes(self, runner_cls, manager_cls) -> None:
-        """Wrap the two hook points once per class (idempotent)."""
-        runner_cls._turbobus_integration = self
-        manager_cls._turbobus_integration = self
-        if not hasattr(runner_cls, "_turbobus_original_initialize_kv_cache"):
-            orig_init = runner_cls.initialize_kv_cache
-            runner_cls._turbobus_original_initialize_kv_cache = orig_init
+        """Attach to these two classes; repeated installs wrap nothing twice."""
+        for cls in (runner_cls, manager_cls):
+            setattr(cls, _HOOK_ATTR, self)
+        _wrap_once(runner_cls, "initialize_kv_cache",
+                   lambda integ, runner, args, kw, _r: integ.bind_runner(runner, args[0] if args else
+                                                                        kw.get("kv_cache_config")))
+        _wrap_once(manager_cls, "allocate_slots",
+                   lambda integ, _mgr, args, kw, blocks: integ.handle_allocation(
+                       args[0] if args else kw.get("request"), blocks))
 
-            @functools.wraps(orig_init)
-            def initialize_kv_cache(runner, kv_cache_config, *a, **kw):
-                out = orig_init(runner, kv_cache_config, *a, **kw)
-                integ = getattr(type(runner), "_turbobus_integration", None)
-                if integ is not None:
-                    integ.bind_runner(runner, kv_cache_config)
-                return out
-
-            runner_cls.initialize_kv_cache = initialize_kv_cache
-        if not hasattr(manager_cls, "_turbobus_original_allocate_slots"):
-            orig_alloc = manager_cls.allocate_slots
-            manager_cls._turbobus_original_allocate_slots = orig_alloc
-
-            @functools.wraps(orig_alloc)
-            def allocate_slots(manager, request, *a, **kw):
-                out = orig_alloc(manager, request, *a, **kw)
-                integ = getattr(type(manager), "_turbobus_integration", None)
-                if integ is not None:
-                    integ.handle_allocation(request, out)
-                return out
-
-            manager_cls.allocate_slots = allocate_slots
-
+    # ---- what vLLM reports --------------------------------------------------------------------
     def bind_runner(self, runner, kv_cache_config=None) -> None:
-        self.bind_kv_caches(list(getattr(runner, "kv_caches", []) or []), kv_cache_config)
+        self.bind_kv_caches(list(getattr(runner, "kv_caches", None) or ()), kv_cache_config)
 
     def bind_kv_caches(self, kv_caches: Iterable, kv_cache_config=None) -> None:
         self.state.kv_cache_config = kv_cache_config
         self.state.kv_caches = list(kv_caches)
-        self._refresh()
+        self._rebuild_adapter()
 
-    def set_cpu_backings(self, cpu_backings: Iterable) -> None:
-        self._cpu_backings = list(cpu_backings)
-        self._refresh()
+    def record_allocation(self, request, blocks) -> VllmAllocationEvent | None:
+        groups = extract_vllm_block_ids(blocks)
+        if not groups:
+            return None
+        rid = str(getattr(request, "request_id", "unknown"))
+        event = VllmAllocationEvent(rid, groups)
+        if rid in self.state.allocations:
+            event = self.state.allocations[rid].merge(event)
+        self.state.allocations[rid] = event
+        return event
+
+    def handle_allocation(self, request, blocks) -> VllmAllocationEvent | None:
+        event = self.record_allocation(request, blocks)
+        if event is not None and self._callback is not None:
+            self._callback(self, request, blocks, event)
+        return event
 
     def set_allocation_callback(self, callback: AllocationCallback | None) -> None:
         self._callback = callback
 
+    # ---- CPU side and transfers -----------------------------------------------------------------
+    def set_cpu_backings(self, cpu_backings: Iterable) -> None:
+        self._cpu_backings = list(cpu_backings)
+        self._rebuild_adapter()
+
     def allocate_cpu_backings(self, slots_per_layer: int, *, pin_memory: bool = True) -> list:
+        """One page-locked CPU backing per KV tensor, ``slots_per_layer`` units each."""
         import torch
 
-        b = [torch.empty(slots_per_layer * block_bytes_from_vllm_kv_tensor(kv), dtype=torch.uint8,
-                         pin_memory=pin_memory) for kv in self.state.kv_caches]
-        self.set_cpu_backings(b)
-        return b
-
-    def record_allocation(self, request, blocks) -> VllmAllocationEvent | None:
-        rid = str(getattr(request, "request_id", "unknown"))
-        groups = extract_vllm_block_ids(blocks)
-        if not groups:
-            return None
-        ev = VllmAllocationEvent(rid, groups)
-        prev = self.state.allocations.get(rid)
-        if prev is not None:
-            ev = prev.merge(ev)
-        self.state.allocations[rid] = ev
-        return ev
-
-    def handle_allocation(self, request, blocks) -> VllmAllocationEvent | None:
-        ev = self.record_allocation(request, blocks)
-        if ev is not None and self._callback is not None:
-            self._callback(self, request, blocks, ev)
-        return ev
+        backings = [torch.empty(int(slots_per_layer) * block_bytes_from_vllm_kv_tensor(kv), dtype=torch.uint8,
+                                pin_memory=pin_memory) for kv in self.state.kv_caches]
+        self.set_cpu_backings(backings)
+        return backings
 
     def block_ids_for_request(self, request_id: str) -> tuple[int, ...]:
         return self.state.allocations[str(request_id)].block_ids
 
     def make_refs_for_request(self, request_id: str, *, cpu_slot_start: int = 0) -> list[VllmKVBlockRef]:
         return make_vllm_layer_block_refs_from_ids(str(request_id), self.block_ids_for_request(request_id),
-                                                   layer_count=len(self.state.kv_caches),
-                                                   cpu_slot_start=cpu_slot_start)
+                                                   layer_count=len(self.state.kv_caches), cpu_slot_start=cpu_slot_start)
 
     def restore_request_prefix(self, request_id: str, *, cpu_slot_start: int = 0) -> list:
-        return self.require_adapter().restore_prefix(self.make_refs_for_request(request_id, cpu_slot_start=cpu_slot_start))
+        refs = self.make_refs_for_request(request_id, cpu_slot_start=cpu_slot_start)
+        return self.require_adapter().restore_prefix(refs)
 
     def save_request_prefix(self, request_id: str, *, cpu_slot_start: int = 0) -> list:
-        return self.require_adapter().save_prefix(self.make_refs_for_request(request_id, cpu_slot_start=cpu_slot_start))
+        refs = self.make_refs_for_request(request_id, cpu_slot_start=cpu_slot_start)
+        return self.require_adapter().save_prefix(refs)
 
-    def _refresh(self) -> None:
-        if not self.state.kv_caches or self._cpu_backings is None:
+    def _rebuild_adapter(self) -> None:
+        caches, backings = self.state.kv_caches, self._cpu_backings
+        if not caches or backings is None:
             self.state.adapter = None
             return
-        if len(self._cpu_backings) != len(self.state.kv_caches):
-            raise ValueError("cpu_backings must match the number of vLLM KV cache tensors")
+        if len(backings) != len(caches):
+            raise ValueError(f"{len(backings)} CPU backings for {len(caches)} vLLM KV cache tensors")
         self.state.adapter = VllmKVSlotAdapter(self.client, self.transfer_context,
-                                               make_vllm_layer_groups_from_kv_caches(self._cpu_backings,
-                                                                                     self.state.kv_caches))
+                                               make_vllm_layer_groups_from_kv_caches(backings, caches))
 
     def require_adapter(self) -> VllmKVSlotAdapter:
         if self.state.adapter is None:
-            raise RuntimeError("vLLM KV caches and CPU backings must be bound before restore/save")
+            raise RuntimeError("bind the vLLM KV caches and the CPU backings before saving or restoring")
         return self.state.adapter
 
     _require_adapter = require_adapter
 
 
 def extract_vllm_block_ids(blocks) -> tuple[tuple[int, ...], ...]:
-    """Block ids from a vLLM ``KVCacheBlocks`` (or ids / groups of ids)."""
+    """Block ids from a vLLM ``KVCacheBlocks`` (or plain ids / id groups)."""
     if blocks is None:
         return ()
-    get = getattr(blocks, "get_block_ids", None)
-    if get is None:
-        raw = getattr(blocks, "block_ids", blocks)
-    else:
-        try:
-            raw = get(allow_none=True)
-        except TypeError:
-            raw = get()
-    return normalize_block_id_groups(raw)
+    getter = getattr(blocks, "get_block_ids", None)
+    if getter is None:
+        return normalize_block_id_groups(getattr(blocks, "block_ids", blocks))
+    try:
+        return normalize_block_id_groups(getter(allow_none=True))
+    except TypeError:  # older vLLM: no allow_none
+        return normalize_block_id_groups(getter())
+
+
+def _block_id(b) -> int:
+    return int(getattr(b, "block_id", b))
 
 
 def normalize_block_id_groups(raw) -> tuple[tuple[int, ...], ...]:
-    if raw is None:
-        return ()
-    if isinstance(raw, (tuple, list)):
-        if all(isinstance(x, int) or x is None for x in raw):
-            ids = tuple(int(x) for x in raw if x is not None)
-            return (ids,) if ids else ()
-        groups = []
-        for g in raw:
-            if g is None:
-                continue
-            if isinstance(g, int):
-                groups.append((int(g),))
-                continue
-            ids = []
-            for b in g:
-                if b is None:
-                    continue
-                ids.append(int(getattr(b, "block_id", b)))
-            groups.append(tuple(ids))
-        return tuple(groups)
+    """``ids``, ``[ids, ...]`` or ``[[block, ...], ...]`` -> tuple of id groups
+    (``None`` entries dropped; a flat list is one group)."""
     if isinstance(raw, int):
-        return ((int(raw),),)
-    return ()
+        return ((raw,),)
+    if not isinstance(raw, (tuple, list)):
+        return ()
+    if all(x is None or isinstance(x, int) for x in raw):
+        flat = tuple(int(x) for x in raw if x is not None)
+        return (flat,) if flat else ()
+    groups = []
+    for g in raw:
+        if g is None:
+            continue
+        groups.append((int(g),) if isinstance(g, int) else tuple(_block_id(b) for b in g if b is not None))
+    return tuple(groups)
 
 
 __all__ = ["AllocationCallback", "VllmAllocationEvent", "VllmIntegrationState", "VllmTurboBusIntegration",

@@ -1,55 +1,34 @@
-"""Cross-process buffers.
+"""Buffers an application shares with the node's data plane.
 
-``SharedPinnedCpuBuffer``: POSIX shared memory that the owner and the data
-plane both map and page-lock (``cudaHostRegister``, portable + mapped), so the
-daemon's executor can DMA from the application's host memory without a copy.
-``CudaIpcDeviceBuffer``: a device allocation exported with a legacy CUDA IPC
-handle (64 bytes, hex on the wire).  Same API as the reference
-(turbobus/client.py:57-352).
+``SharedPinnedCpuBuffer`` is a window into a POSIX shared-memory segment.
+The application creates (owns) the segment; the daemon's executor or a
+worker maps the same segment by name and page-locks its own mapping, so the
+copy engines move the application's bytes with no intermediate copy.
+``CudaIpcDeviceBuffer`` describes a device allocation exported through a
+legacy CUDA IPC handle (64 bytes, hex on the wire) plus the buffer's offset
+inside that allocation.
+
+Public names, constructors and registration metadata keys match the
+reference's client module (turbobus/client.py:57-352) so applications and
+daemons of either project interoperate; the implementation is this
+project's own: one ``_Segment`` per mapping owns the shared memory and its
+base address, a buffer is a bounds-checked window onto it, and CUDA
+page-locking is a separate, reversible record.
 """
 
 from __future__ import annotations
 
-import ctypes
 import os
 import threading
 import uuid
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from multiprocessing import resource_tracker, shared_memory
 from typing import Any
 
 from .schema import BufferRegistration, DaemonResponse
 
-_OWNED_NAMES: set[str] = set()
-_ATTACH_LOCK = threading.Lock()
-
-
-def _shm_name(prefix: str) -> str:
-    clean = "".join(c if c.isalnum() or c in "_-" else "_" for c in str(prefix)).strip("_") or "pcie_pool"
-    return f"{clean}_{uuid.uuid4().hex}"
-
-
-def _tracker_name(shm: shared_memory.SharedMemory) -> str:
-    name = getattr(shm, "_name", None) or str(shm.name)
-    return name if (os.name != "posix" or name.startswith("/")) else f"/{name}"
-
-
-def _open_borrowed(name: str) -> shared_memory.SharedMemory:
-    """Map someone else's segment without making this process its owner."""
-    try:
-        return shared_memory.SharedMemory(name=name, create=False, track=False)
-    except TypeError:  # Python < 3.13 has no ``track``
-        # Attaching would register the name with the resource tracker, which
-        # processes started by ``multiprocessing`` share with their parent; a
-        # register + unregister pair here would drop the owner's registration.
-        # Skip the registration for the duration of the attach instead.
-        with _ATTACH_LOCK:
-            saved = resource_tracker.register
-            resource_tracker.register = lambda *_a, **_k: None
-            try:
-                return shared_memory.SharedMemory(name=name, create=False)
-            finally:
-                resource_tracker.register = saved
+SHARED_HANDLE = "shared_pinned_cpu"
+IPC_HANDLE = "cuda_ipc_device"
 
 
 def default_backend():
@@ -58,156 +37,226 @@ def default_backend():
     return default_cuda_backend
 
 
-@dataclass
-class SharedPinnedCpuBuffer:
-    buffer_id: str
-    job_id: str
-    size_bytes: int
-    shared_memory_name: str
-    shared_memory_size_bytes: int
-    _shared_memory: shared_memory.SharedMemory = field(repr=False, compare=False)
-    offset_bytes: int = 0
-    owner: bool = False
-    _cuda_registered: bool = field(default=False, init=False, repr=False)
-    _cuda_backend: Any | None = field(default=None, init=False, repr=False)
-    _cuda_registered_address: int | None = field(default=None, init=False, repr=False)
-    _closed: bool = field(default=False, init=False, repr=False)
-    _unlinked: bool = field(default=False, init=False, repr=False)
+# ---- shared-memory segments -------------------------------------------------------------
 
+class _Segment:
+    """One mapping of a shared-memory segment and its base address.
+
+    The creator owns the name (it unlinks it); a process that attaches to a
+    segment it did not create maps it without registering the name with the
+    ``multiprocessing`` resource tracker, which a spawned daemon shares with
+    its parent and which would otherwise unlink the owner's segment."""
+
+    _attach_lock = threading.Lock()
+
+    def __init__(self, shm: shared_memory.SharedMemory, owner: bool) -> None:
+        import numpy as np
+
+        self.shm = shm
+        self.owner = owner
+        self.size = len(shm.buf)
+        self.base = int(np.frombuffer(shm.buf, dtype=np.uint8).ctypes.data) if self.size else 0
+        self.mapped = True
+        self.unlinked = False
+
+    @classmethod
+    def create(cls, prefix: str, size: int) -> "_Segment":
+        stem = "".join(c if c.isalnum() or c in "_-" else "_" for c in str(prefix)).strip("_") or "pcie_pool"
+        return cls(shared_memory.SharedMemory(name=f"{stem}_{uuid.uuid4().hex}", create=True, size=size), True)
+
+    @classmethod
+    def attach(cls, name: str) -> "_Segment":
+        try:
+            return cls(shared_memory.SharedMemory(name=name, create=False, track=False), False)
+        except TypeError:  # Python < 3.13: no ``track``; suppress the registration while attaching
+            with cls._attach_lock:
+                keep = resource_tracker.register
+                resource_tracker.register = lambda *_a, **_k: None
+                try:
+                    return cls(shared_memory.SharedMemory(name=name, create=False), False)
+                finally:
+                    resource_tracker.register = keep
+
+    @property
+    def name(self) -> str:
+        return str(self.shm.name)
+
+    def unmap(self) -> None:
+        if self.mapped:
+            self.shm.close()
+            self.mapped = False
+
+    def unlink(self) -> None:
+        if not self.unlinked:
+            self.shm.unlink()
+            self.unlinked = True
+
+
+def validate_backing(offset: int, size: int, declared: int, mapped: int) -> None:
+    """A registration may only name bytes that exist: its window must fit the
+    size the owner declared, and the declared size must fit what was mapped."""
+    end = int(offset) + int(size)
+    if end > int(declared):
+        raise ValueError(f"shared_pinned_cpu window ends at byte {end}, past the declared "
+                         f"segment size {int(declared)}")
+    if int(declared) > int(mapped) or end > int(mapped):
+        raise ValueError(f"shared_pinned_cpu backing maps {int(mapped)} bytes, fewer than the "
+                         f"{max(end, int(declared))} the registration needs")
+
+
+check_backing = validate_backing
+
+
+@dataclass
+class _Pinning:
+    backend: Any
+    address: int
+
+
+# ---- shared pinned host buffer ---------------------------------------------------------------
+
+class SharedPinnedCpuBuffer:
+    """``size_bytes`` bytes at ``offset_bytes`` of a shared-memory segment."""
+
+    def __init__(self, buffer_id: str, job_id: str, segment: _Segment, offset_bytes: int, size_bytes: int,
+                 declared_bytes: int | None = None) -> None:
+        self.buffer_id = str(buffer_id)
+        self.job_id = str(job_id)
+        self._seg = segment
+        self.offset_bytes = int(offset_bytes)
+        self.size_bytes = int(size_bytes)
+        self.shared_memory_size_bytes = int(segment.size if declared_bytes is None else declared_bytes)
+        self._pin: _Pinning | None = None
+
+    # -- construction --------------------------------------------------------------------
     @classmethod
     def allocate(cls, buffer_id: str, job_id: str, size_bytes: int, *,
                  name_prefix: str = "pcie_pool") -> "SharedPinnedCpuBuffer":
-        size_bytes = int(size_bytes)
-        if size_bytes <= 0:
-            raise ValueError("size_bytes must be positive")
-        shm = shared_memory.SharedMemory(name=_shm_name(name_prefix), create=True, size=size_bytes)
-        _OWNED_NAMES.add(_tracker_name(shm))
-        return cls(buffer_id=str(buffer_id), job_id=str(job_id), size_bytes=size_bytes,
-                   shared_memory_name=shm.name, shared_memory_size_bytes=size_bytes, owner=True,
-                   _shared_memory=shm)
+        """Create a new segment of ``size_bytes`` owned by this process."""
+        n = int(size_bytes)
+        if n <= 0:
+            raise ValueError(f"a shared buffer needs a positive size, got {n}")
+        return cls(buffer_id, job_id, _Segment.create(name_prefix, n), 0, n)
 
     @classmethod
     def open_from_registration(cls, registration: BufferRegistration) -> "SharedPinnedCpuBuffer":
+        """Map the segment a registration names (this process does not own it)."""
         if not isinstance(registration, BufferRegistration):
             raise TypeError("registration must be a BufferRegistration")
-        if registration.handle_type != "shared_pinned_cpu":
-            raise ValueError("registration must be a shared_pinned_cpu buffer")
+        if registration.handle_type != SHARED_HANDLE:
+            raise ValueError(f"registration {registration.buffer_id} is a {registration.handle_type} buffer, "
+                             f"not {SHARED_HANDLE}")
         md = registration.metadata
-        if "shared_memory_size_bytes" not in md:
-            raise ValueError("shared_pinned_cpu metadata requires shared_memory_size_bytes")
-        name, off, declared = str(md["shared_memory_name"]), int(md["offset_bytes"]), int(md["shared_memory_size_bytes"])
-        shm = _open_borrowed(name)
+        for key in ("shared_memory_name", "offset_bytes", "shared_memory_size_bytes"):
+            if key not in md:
+                raise ValueError(f"{SHARED_HANDLE} registration lacks metadata {key!r}")
+        seg = _Segment.attach(str(md["shared_memory_name"]))
         try:
-            check_backing(off, registration.size_bytes, declared, len(shm.buf))
-        except Exception:
-            shm.close()
+            validate_backing(int(md["offset_bytes"]), registration.size_bytes, int(md["shared_memory_size_bytes"]),
+                             seg.size)
+        except ValueError:
+            seg.unmap()
             raise
-        return cls(buffer_id=registration.buffer_id, job_id=registration.job_id,
-                   size_bytes=registration.size_bytes, shared_memory_name=name,
-                   shared_memory_size_bytes=declared, offset_bytes=off, owner=False, _shared_memory=shm)
+        return cls(registration.buffer_id, registration.job_id, seg, int(md["offset_bytes"]),
+                   registration.size_bytes, int(md["shared_memory_size_bytes"]))
+
+    # -- identity ----------------------------------------------------------------------------
+    @property
+    def shared_memory_name(self) -> str:
+        return self._seg.name
+
+    @property
+    def owner(self) -> bool:
+        return self._seg.owner
+
+    @property
+    def closed(self) -> bool:
+        return not self._seg.mapped
 
     @property
     def metadata(self) -> dict[str, object]:
         return {"shared_memory_name": self.shared_memory_name, "offset_bytes": self.offset_bytes,
                 "shared_memory_size_bytes": self.shared_memory_size_bytes}
 
-    @property
-    def view(self) -> memoryview:
-        if self._closed:
-            raise RuntimeError("shared CPU buffer is closed")
-        return self._shared_memory.buf[self.offset_bytes:self.offset_bytes + self.size_bytes]
-
-    @property
-    def address(self) -> int:
-        v = self.view
-        c = ctypes.c_char.from_buffer(v)
-        try:
-            return ctypes.addressof(c)
-        finally:
-            del c
-            v.release()
-
-    @property
-    def closed(self) -> bool:
-        return self._closed
-
-    @property
-    def cuda_registered(self) -> bool:
-        return self._cuda_registered
-
-    def numpy(self):
-        import numpy as np
-
-        return np.frombuffer(self._shared_memory.buf, dtype=np.uint8, count=self.size_bytes,
-                             offset=self.offset_bytes)
-
-    def write(self, data, offset: int = 0) -> None:
-        payload = bytes(data)
-        offset = int(offset)
-        if offset < 0:
-            raise ValueError("offset must be non-negative")
-        if offset + len(payload) > self.size_bytes:
-            raise ValueError("write exceeds shared CPU buffer")
-        v = self.view
-        try:
-            v[offset:offset + len(payload)] = payload
-        finally:
-            v.release()
-
-    def read(self, size: int | None = None, offset: int = 0) -> bytes:
-        offset = int(offset)
-        if offset < 0:
-            raise ValueError("offset must be non-negative")
-        n = self.size_bytes - offset if size is None else int(size)
-        if n < 0:
-            raise ValueError("size must be non-negative")
-        if offset + n > self.size_bytes:
-            raise ValueError("read exceeds shared CPU buffer")
-        v = self.view
-        try:
-            return bytes(v[offset:offset + n])
-        finally:
-            v.release()
-
     def buffer_registration(self) -> BufferRegistration:
         return BufferRegistration(buffer_id=self.buffer_id, job_id=self.job_id, kind="cpu_pinned",
-                                  size_bytes=self.size_bytes, pinned=True, handle_type="shared_pinned_cpu",
+                                  size_bytes=self.size_bytes, pinned=True, handle_type=SHARED_HANDLE,
                                   metadata=self.metadata)
 
     def register_with_daemon(self, daemon_client) -> DaemonResponse:
-        return daemon_client.register_buffer(buffer_id=self.buffer_id, job_id=self.job_id, kind="cpu_pinned",
-                                             size_bytes=self.size_bytes, pinned=True,
-                                             handle_type="shared_pinned_cpu", metadata=self.metadata)
+        r = self.buffer_registration()
+        return daemon_client.register_buffer(buffer_id=r.buffer_id, job_id=r.job_id, kind=r.kind,
+                                             size_bytes=r.size_bytes, pinned=True, handle_type=r.handle_type,
+                                             metadata=dict(r.metadata))
+
+    # -- data ----------------------------------------------------------------------------------
+    def _live(self) -> _Segment:
+        if not self._seg.mapped:
+            raise RuntimeError(f"shared buffer {self.buffer_id} is closed")
+        return self._seg
+
+    @property
+    def address(self) -> int:
+        """Address of the window's first byte in this process."""
+        return self._live().base + self.offset_bytes
+
+    @property
+    def view(self) -> memoryview:
+        return self._live().shm.buf[self.offset_bytes:self.offset_bytes + self.size_bytes]
+
+    def numpy(self):
+        """The window as a writable uint8 array (no copy)."""
+        import numpy as np
+
+        return np.frombuffer(self._live().shm.buf, dtype=np.uint8, count=self.size_bytes, offset=self.offset_bytes)
+
+    def _span(self, offset: int, n: int) -> slice:
+        o, n = int(offset), int(n)
+        if o < 0 or n < 0 or o + n > self.size_bytes:
+            raise ValueError(f"bytes [{o}, {o + n}) fall outside shared buffer {self.buffer_id} "
+                             f"of {self.size_bytes} bytes")
+        return slice(o, o + n)
+
+    def write(self, data, offset: int = 0) -> None:
+        import numpy as np
+
+        src = np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8)
+        self.numpy()[self._span(offset, src.size)] = src
+
+    def read(self, size: int | None = None, offset: int = 0) -> bytes:
+        n = self.size_bytes - int(offset) if size is None else int(size)
+        return self.numpy()[self._span(offset, n)].tobytes()
+
+    # -- page-locking for CUDA ----------------------------------------------------------------
+    @property
+    def cuda_registered(self) -> bool:
+        return self._pin is not None
 
     def register_for_cuda(self, backend=None) -> None:
-        if self._cuda_registered:
-            return
-        backend = backend or default_backend()
-        addr = self.address
-        backend.register_host_memory(addr, self.size_bytes)
-        self._cuda_backend, self._cuda_registered_address, self._cuda_registered = backend, addr, True
+        if self._pin is None:
+            b = backend or default_backend()
+            addr = self.address
+            b.register_host_memory(addr, self.size_bytes)
+            self._pin = _Pinning(b, addr)
 
     def unregister_from_cuda(self) -> None:
-        if not self._cuda_registered:
-            return
-        (self._cuda_backend or default_backend()).unregister_host_memory(self._cuda_registered_address)
-        self._cuda_backend, self._cuda_registered_address, self._cuda_registered = None, None, False
+        pin, self._pin = self._pin, None
+        if pin is not None:
+            pin.backend.unregister_host_memory(pin.address)
 
+    # -- lifetime ---------------------------------------------------------------------------------
     def close(self) -> None:
-        if self._closed:
-            return
-        self.unregister_from_cuda()
-        self._shared_memory.close()
-        self._closed = True
+        """Drop this process's mapping (CUDA page-locking first)."""
+        if self._seg.mapped:
+            self.unregister_from_cuda()
+            self._seg.unmap()
 
     def unlink(self) -> None:
-        if self._unlinked:
-            return
-        self._shared_memory.unlink()
-        _OWNED_NAMES.discard(_tracker_name(self._shared_memory))
-        self._unlinked = True
+        """Remove the segment's name (the memory lives until every mapping closes)."""
+        self._seg.unlink()
 
     def release(self) -> None:
+        """Close; the owner also unlinks."""
         try:
             self.close()
         finally:
@@ -220,8 +269,14 @@ class SharedPinnedCpuBuffer:
     def __exit__(self, *exc) -> None:
         self.release()
 
+    def __repr__(self) -> str:
+        return (f"SharedPinnedCpuBuffer({self.buffer_id!r}, job={self.job_id!r}, segment={self.shared_memory_name!r}, "
+                f"offset={self.offset_bytes}, size={self.size_bytes}, owner={self.owner})")
+
 
 class SharedPinnedCpuBufferAllocator:
+    """Allocates owned shared buffers whose segment names share a prefix."""
+
     def __init__(self, name_prefix: str = "pcie_pool") -> None:
         self.name_prefix = str(name_prefix)
 
@@ -229,31 +284,34 @@ class SharedPinnedCpuBufferAllocator:
         return SharedPinnedCpuBuffer.allocate(buffer_id, job_id, size_bytes, name_prefix=self.name_prefix)
 
 
+# ---- CUDA IPC device buffer -------------------------------------------------------------------
+
 @dataclass(frozen=True)
 class CudaIpcDeviceBuffer:
+    """A device buffer another process opens through its allocation's IPC
+    handle; ``ipc_offset`` is the buffer's distance from the allocation base
+    (the handle always maps the base)."""
+
     buffer_id: str
     job_id: str
     device_index: int
     size_bytes: int
     cuda_ipc_handle: bytes
     device_ptr: int | None = None
-    ipc_offset: int = 0  # device_ptr - base of its allocation (the handle maps the base)
+    ipc_offset: int = 0
 
     @classmethod
     def from_device_pointer(cls, buffer_id: str, job_id: str, device_index: int, size_bytes: int,
                             device_ptr: int, *, backend=None) -> "CudaIpcDeviceBuffer":
-        if int(size_bytes) <= 0:
-            raise ValueError("size_bytes must be positive")
-        if int(device_ptr) <= 0:
-            raise ValueError("device_ptr must be positive")
-        backend = backend or default_backend()
-        setter = getattr(backend, "set_device", None)
-        if callable(setter):
-            setter(int(device_index))
-        off = getattr(backend, "device_allocation_offset", None)
-        return cls(buffer_id=str(buffer_id), job_id=str(job_id), device_index=int(device_index),
-                   size_bytes=int(size_bytes), cuda_ipc_handle=backend.export_device_ipc_handle(int(device_ptr)),
-                   device_ptr=int(device_ptr), ipc_offset=int(off(int(device_ptr))) if callable(off) else 0)
+        if int(size_bytes) <= 0 or int(device_ptr) <= 0:
+            raise ValueError("an IPC buffer needs a positive size and a device pointer")
+        b = backend or default_backend()
+        if callable(getattr(b, "set_device", None)):
+            b.set_device(int(device_index))
+        base_offset = getattr(b, "device_allocation_offset", None)
+        return cls(str(buffer_id), str(job_id), int(device_index), int(size_bytes),
+                   b.export_device_ipc_handle(int(device_ptr)), int(device_ptr),
+                   int(base_offset(int(device_ptr))) if callable(base_offset) else 0)
 
     @classmethod
     def from_tensor(cls, buffer_id: str, job_id: str, tensor, *, backend=None) -> "CudaIpcDeviceBuffer":
@@ -270,23 +328,13 @@ class CudaIpcDeviceBuffer:
     def buffer_registration(self) -> BufferRegistration:
         return BufferRegistration(buffer_id=self.buffer_id, job_id=self.job_id, kind="gpu",
                                   size_bytes=self.size_bytes, device_index=self.device_index,
-                                  address=self.device_ptr, handle_type="cuda_ipc_device", metadata=self.metadata)
+                                  address=self.device_ptr, handle_type=IPC_HANDLE, metadata=self.metadata)
 
     def register_with_daemon(self, daemon_client) -> DaemonResponse:
-        return daemon_client.register_buffer(buffer_id=self.buffer_id, job_id=self.job_id, kind="gpu",
-                                             size_bytes=self.size_bytes, device_index=self.device_index,
-                                             address=self.device_ptr, handle_type="cuda_ipc_device",
-                                             metadata=self.metadata)
+        r = self.buffer_registration()
+        return daemon_client.register_buffer(buffer_id=r.buffer_id, job_id=r.job_id, kind=r.kind,
+                                             size_bytes=r.size_bytes, device_index=r.device_index, address=r.address,
+                                             handle_type=r.handle_type, metadata=dict(r.metadata))
 
 
-def check_backing(offset: int, size: int, declared: int, actual: int) -> None:
-    span = int(offset) + int(size)
-    if span > int(declared):
-        raise ValueError("shared_pinned_cpu shared_memory_size_bytes is smaller than buffer span")
-    if span > int(actual):
-        raise ValueError("shared_pinned_cpu backing is smaller than authorized buffer span")
-    if int(declared) > int(actual):
-        raise ValueError("shared_pinned_cpu backing is smaller than declared shared memory size")
-
-
-__all__ = ["CudaIpcDeviceBuffer", "SharedPinnedCpuBuffer", "SharedPinnedCpuBufferAllocator"]
+__all__ = ["CudaIpcDeviceBuffer", "SharedPinnedCpuBuffer", "SharedPinnedCpuBufferAllocator", "validate_backing"]

@@ -35,9 +35,32 @@ OPERATIONS = {"prefetch": ("h2d", BlockState.PREFETCHING, BlockState.GPU),
 
 @dataclass(frozen=True)
 class TransferStats:
+    """Bytes and chunk counts of one or more transfers, split by path kind.
+    Stats add, so a batch's figure is the sum of its transfers'."""
+
     bytes: int = 0
     direct_chunks: int = 0
     relay_chunks: int = 0
+
+    def __add__(self, other: "TransferStats") -> "TransferStats":
+        return TransferStats(self.bytes + other.bytes, self.direct_chunks + other.direct_chunks,
+                             self.relay_chunks + other.relay_chunks)
+
+    @classmethod
+    def of_path(cls, path: Mapping[str, object]) -> "TransferStats":
+        """One receipt path record (``kind``, ``bytes``, ``chunk_count``)."""
+        nbytes = int(path.get("bytes", 0) or 0)
+        chunks = int(path.get("chunk_count", path.get("chunks", 0)) or 0)
+        relay = str(path.get("kind", "")).lower() == "relay"
+        return cls(nbytes, 0 if relay else chunks, chunks if relay else 0)
+
+    @classmethod
+    def coerce(cls, value) -> "TransferStats":
+        """A stats object, mapping or anything with the three attributes."""
+        if isinstance(value, TransferStats):
+            return value
+        get = value.get if isinstance(value, Mapping) else (lambda k, d=0: getattr(value, k, d))
+        return cls(*(int(get(k, 0) or 0) for k in ("bytes", "direct_chunks", "relay_chunks")))
 
     def as_dict(self) -> dict[str, int]:
         return {"bytes": self.bytes, "direct_chunks": self.direct_chunks, "relay_chunks": self.relay_chunks}
@@ -51,23 +74,39 @@ class TransferIntentClient(Protocol):
         ...
 
 
-def _nonempty(v, name: str) -> str:
-    s = str(v)
-    if not s.strip():
-        raise ValueError(f"{name} must be non-empty")
-    return s
-
-
 def check_policy_hints(hints: Mapping[str, object]) -> dict[str, object]:
+    """Adapters state intent, not routing: hints naming relays, lanes or
+    paths are refused (the daemon alone chooses physical paths)."""
     h = dict(hints)
-    bad = sorted(str(k) for k in h if str(k).lower() in FORBIDDEN_POLICY_KEYS)
-    if bad:
-        raise ValueError("policy_hints must not choose physical paths: " + ", ".join(bad))
+    routing = sorted(k for k in map(str, h) if k.lower() in FORBIDDEN_POLICY_KEYS)
+    if routing:
+        raise ValueError(f"policy_hints may not pick physical paths ({', '.join(routing)}); the daemon does")
     return h
+
+
+def _text(name: str):
+    def norm(v) -> str:
+        if not str(v).strip():
+            raise ValueError(f"AdapterTransferContext.{name} must be non-empty")
+        return str(v)
+    return norm
+
+
+def _timeout(v):
+    if v is None:
+        return None
+    t = float(v)
+    if t < 0:
+        raise ValueError(f"wait_timeout_seconds must be non-negative, got {t}")
+    return t
 
 
 @dataclass(frozen=True)
 class AdapterTransferContext:
+    """What every intent of one adapter shares: job, session, the CPU and GPU
+    backing buffers, workload class, priority, hints, metadata, the intent-id
+    prefix and the wait timeout."""
+
     job_id: str
     session_id: str
     cpu_buffer_id: str
@@ -79,82 +118,72 @@ class AdapterTransferContext:
     intent_prefix: str | None = None
     wait_timeout_seconds: float | None = None
 
+    _NORMALIZE = {
+        "job_id": _text("job_id"), "session_id": _text("session_id"),
+        "cpu_buffer_id": _text("cpu_buffer_id"), "gpu_buffer_id": _text("gpu_buffer_id"),
+        "workload_kind": WorkloadKind, "priority": int, "policy_hints": check_policy_hints,
+        "metadata": dict, "wait_timeout_seconds": _timeout,
+        "intent_prefix": lambda v: _text("intent_prefix")(v or f"adapter-{uuid.uuid4()}"),
+    }
+
     def __post_init__(self) -> None:
-        for name in ("job_id", "session_id", "cpu_buffer_id", "gpu_buffer_id"):
-            object.__setattr__(self, name, _nonempty(getattr(self, name), name))
-        object.__setattr__(self, "workload_kind", WorkloadKind(self.workload_kind))
-        object.__setattr__(self, "priority", int(self.priority))
-        object.__setattr__(self, "policy_hints", check_policy_hints(self.policy_hints))
-        object.__setattr__(self, "metadata", dict(self.metadata))
-        object.__setattr__(self, "intent_prefix",
-                           _nonempty(self.intent_prefix or f"adapter-{uuid.uuid4()}", "intent_prefix"))
-        if self.wait_timeout_seconds is not None:
-            t = float(self.wait_timeout_seconds)
-            if t < 0:
-                raise ValueError("wait_timeout_seconds must be non-negative")
-            object.__setattr__(self, "wait_timeout_seconds", t)
+        for name, norm in self._NORMALIZE.items():
+            object.__setattr__(self, name, norm(getattr(self, name)))
 
 
 def transfer_stats_from_receipt(receipt: TransferReceipt) -> TransferStats:
-    d_b = r_b = d_c = r_c = 0
-    for p in receipt.path_stats:
-        n = int(p.get("bytes", 0) or 0)
-        c = int(p.get("chunk_count", p.get("chunks", 0)) or 0)
-        if str(p.get("kind", "")).lower() == "relay":
-            r_b, r_c = r_b + n, r_c + c
-        else:
-            d_b, d_c = d_b + n, d_c + c
-    return TransferStats(bytes=d_b + r_b, direct_chunks=d_c, relay_chunks=r_c)
-
-
-def _stat(stats, name: str) -> int:
-    return int((stats.get(name, 0) if isinstance(stats, dict) else getattr(stats, name, 0)) or 0)
+    return sum((TransferStats.of_path(p) for p in receipt.path_stats), TransferStats())
 
 
 def summarize_transfer_handles(handles: Iterable) -> TransferStats:
-    seen, uniq = set(), []
-    for h in handles:
-        if id(h) in seen:
-            continue
-        st = getattr(h, "stats", None)
-        if st is None:
-            continue
-        seen.add(id(h))
-        uniq.append(st)
-    return TransferStats(bytes=sum(_stat(s, "bytes") for s in uniq),
-                         direct_chunks=sum(_stat(s, "direct_chunks") for s in uniq),
-                         relay_chunks=sum(_stat(s, "relay_chunks") for s in uniq))
+    """Stats of distinct handles (a handle shared by several blocks counts once)."""
+    distinct = {id(h): h for h in handles if getattr(h, "stats", None) is not None}
+    return sum((TransferStats.coerce(h.stats) for h in distinct.values()), TransferStats())
+
+
+_FAILED = (TransferStatusState.FAILED, TransferStatusState.CANCELED)
 
 
 @dataclass
 class ReceiptTransferHandle:
+    """The receipt of one submitted intent.  ``wait`` asks the daemon until it
+    sees a terminal receipt, then answers from it; a failed or canceled
+    transfer raises."""
+
     client: TransferIntentClient
     intent: TransferIntent
     receipt: TransferReceipt
     wait_timeout_seconds: float | None = None
     wait_calls: int = 0
-    _waited: bool = field(default=False, init=False, repr=False)
+    _final: TransferReceipt | None = field(default=None, init=False, repr=False)
 
     @property
     def stats(self) -> TransferStats:
         return transfer_stats_from_receipt(self.receipt)
 
-    def wait(self) -> TransferReceipt:
-        if self._waited:
-            return self.receipt
-        r = self.client.wait_transfer_receipt(self.intent.intent_id, timeout_seconds=self.wait_timeout_seconds)
+    @property
+    def done(self) -> bool:
+        return self._final is not None
+
+    def _accept(self, r) -> TransferReceipt:
         if not isinstance(r, TransferReceipt):
-            raise TypeError("wait_transfer_receipt must return a TransferReceipt")
+            raise TypeError(f"the daemon client returned {type(r).__name__}, not a TransferReceipt")
         if r.intent_id != self.intent.intent_id:
-            raise ValueError("receipt intent_id does not match transfer intent")
+            raise ValueError(f"receipt for {r.intent_id!r} does not match intent {self.intent.intent_id!r}")
+        return r
+
+    def wait(self) -> TransferReceipt:
+        if self._final is not None:
+            return self._final
+        r = self._accept(self.client.wait_transfer_receipt(self.intent.intent_id,
+                                                           timeout_seconds=self.wait_timeout_seconds))
         self.receipt = r
         self.wait_calls += 1
-        st = TransferStatusState(r.state)
-        # a timed-out (or timeout=None poll) wait can return a live receipt: only a
-        # terminal one ends the handle
-        self._waited = st in TERMINAL_STATES
-        if st in (TransferStatusState.FAILED, TransferStatusState.CANCELED):
-            raise RuntimeError(r.error or f"transfer {st.value}")
+        state = TransferStatusState(r.state)
+        if state in TERMINAL_STATES:  # a timed-out wait may still return a live receipt
+            self._final = r
+        if state in _FAILED:
+            raise RuntimeError(r.error or f"transfer {self.intent.intent_id} {state.value}")
         return r
 
 

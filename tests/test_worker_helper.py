@@ -561,7 +561,7 @@ def test_endpoint_matches_the_message_handler(rig):
     req, _ = rig.authorization(token="forged")
     a = decode_worker_response_envelope(ep.handle_message(_line(req)))
     assert a.ok and a.final_state == "authorization_failed" and "token" in a.error
-    with pytest.raises(ValueError, match="daemon_client"):
+    with pytest.raises(ValueError, match="daemon client"):
         WorkerServiceEndpoint()
     with pytest.raises(TypeError):
         WorkerServiceEndpoint(service=object())
