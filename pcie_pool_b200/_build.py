@@ -26,7 +26,7 @@ CSRC = PKG_DIR / "csrc"
 BUILD_DIR = PKG_DIR / "_build"
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 
-CU_SOURCES = ["ppb_common.cu", "pool_kernels.cu", "engine.cu", "native_ops.cu", "noalloc.cu"]
+CU_SOURCES = ["ppb_common.cu", "pool_kernels.cu", "engine.cu", "native_ops.cu", "noalloc.cu", "vmm.cu"]
 CC_SOURCES = ["planner.cc", "host_ops.cc", "bindings.cc", "bind_ops.cc"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

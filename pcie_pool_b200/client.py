@@ -29,6 +29,7 @@ from .schema import BufferRegistration, DaemonResponse
 
 SHARED_HANDLE = "shared_pinned_cpu"
 IPC_HANDLE = "cuda_ipc_device"
+VMM_HANDLE = "cuda_vmm_fd"
 
 
 def default_backend():
@@ -337,4 +338,71 @@ class CudaIpcDeviceBuffer:
                                              handle_type=r.handle_type, metadata=dict(r.metadata))
 
 
-__all__ = ["CudaIpcDeviceBuffer", "SharedPinnedCpuBuffer", "SharedPinnedCpuBufferAllocator", "validate_backing"]
+# ---- CUDA VMM device buffer (POSIX file descriptor) ----------------------------------------------
+
+class CudaVmmDeviceBuffer:
+    """A device buffer made with CUDA virtual memory management and exported
+    as a POSIX file descriptor.  The descriptor is passed to the daemon with
+    the registration (``SCM_RIGHTS`` on its socket; the number itself for an
+    in-process daemon), which imports and maps the allocation.  Unlike a
+    legacy IPC handle the export is an ordinary descriptor: it can be
+    duplicated, passed on and closed, and the memory lives until every
+    mapping and descriptor is gone.  Legacy IPC (``CudaIpcDeviceBuffer``)
+    stays available as the other import path."""
+
+    def __init__(self, buffer_id: str, job_id: str, device_index: int, size_bytes: int, device_ptr: int,
+                 mapped_bytes: int, fd: int, owner: bool) -> None:
+        self.buffer_id, self.job_id = str(buffer_id), str(job_id)
+        self.device_index, self.size_bytes = int(device_index), int(size_bytes)
+        self.device_ptr, self.mapped_bytes, self.fd, self.owner = int(device_ptr), int(mapped_bytes), int(fd), owner
+
+    @classmethod
+    def allocate(cls, buffer_id: str, job_id: str, device_index: int, size_bytes: int) -> "CudaVmmDeviceBuffer":
+        from ._native import native
+
+        if int(size_bytes) <= 0:
+            raise ValueError("a VMM buffer needs a positive size")
+        ptr, mapped, fd = native().vmm_alloc(int(device_index), int(size_bytes))
+        return cls(buffer_id, job_id, device_index, size_bytes, ptr, mapped, fd, True)
+
+    @classmethod
+    def import_fd(cls, buffer_id: str, job_id: str, device_index: int, size_bytes: int, fd: int,
+                  mapped_bytes: int) -> "CudaVmmDeviceBuffer":
+        """Map a descriptor received from the exporting process."""
+        from ._native import native
+
+        ptr = native().vmm_import(int(fd), int(device_index), int(mapped_bytes))
+        return cls(buffer_id, job_id, device_index, size_bytes, ptr, mapped_bytes, fd, False)
+
+    @property
+    def metadata(self) -> dict[str, object]:
+        return {"vmm_mapped_bytes": self.mapped_bytes}
+
+    def buffer_registration(self, *, with_fd: bool = False) -> BufferRegistration:
+        md = dict(self.metadata)
+        if with_fd:
+            md["vmm_fd"] = self.fd
+        return BufferRegistration(buffer_id=self.buffer_id, job_id=self.job_id, kind="gpu",
+                                  size_bytes=self.size_bytes, device_index=self.device_index,
+                                  address=self.device_ptr, handle_type=VMM_HANDLE, metadata=md)
+
+    def register_with_daemon(self, daemon_client) -> DaemonResponse:
+        r = self.buffer_registration()
+        return daemon_client.register_buffer(buffer_id=r.buffer_id, job_id=r.job_id, kind=r.kind,
+                                             size_bytes=r.size_bytes, device_index=r.device_index,
+                                             address=r.address, handle_type=r.handle_type,
+                                             metadata=dict(r.metadata), fds=[self.fd])
+
+    def release(self) -> None:
+        from ._native import native
+
+        if self.device_ptr:
+            native().vmm_release(self.device_ptr)
+            self.device_ptr = 0
+        if self.owner and self.fd >= 0:
+            os.close(self.fd)
+            self.fd = -1
+
+
+__all__ = ["CudaIpcDeviceBuffer", "CudaVmmDeviceBuffer", "SharedPinnedCpuBuffer", "SharedPinnedCpuBufferAllocator",
+           "validate_backing"]

@@ -12,6 +12,7 @@
 #include <cstring>
 
 #include "engine.h"
+#include "vmm.h"
 #include "native_ops.h"
 #include "planner.h"
 #include "ppb_common.h"
@@ -100,6 +101,19 @@ PYBIND11_MODULE(_C, m) {
     if (rc != 0) throw std::runtime_error("cuMemGetAddressRange failed with CUresult " + std::to_string(rc));
     return static_cast<uint64_t>(base);
   });
+  // VMM shareable device buffers (POSIX file descriptors)
+  m.def("vmm_alloc", [](int device, uint64_t bytes) {
+    const VmmBuffer b = vmm_alloc(device, bytes);
+    return py::make_tuple(b.ptr, b.size, b.fd);
+  }, py::arg("device"), py::arg("bytes"));
+  m.def("vmm_import", [](int fd, int device, uint64_t size) { return vmm_import(fd, device, size).ptr; },
+        py::arg("fd"), py::arg("device"), py::arg("size"));
+  m.def("vmm_release", &vmm_release, py::arg("ptr"));
+  m.def("vmm_granularity", &vmm_granularity, py::arg("device"));
+  // plain cudaMemcpy (either direction, inferred from the pointers)
+  m.def("memcpy", [](uint64_t dst, uint64_t src, uint64_t n) {
+    PPB_CUDA(cudaMemcpy(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), n, cudaMemcpyDefault));
+  }, py::arg("dst"), py::arg("src"), py::arg("bytes"), py::call_guard<py::gil_scoped_release>());
   m.def("open_ipc_handle", [](py::bytes raw, int device) {
     std::string s = raw;
     if (s.size() != sizeof(cudaIpcMemHandle_t)) throw std::invalid_argument("IPC handle must be 64 bytes");

@@ -6,6 +6,8 @@
 #include <stdexcept>
 #include <thread>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "ppb_common.h"
 
 namespace ppb {
@@ -70,6 +72,41 @@ bool can_flush_remote_writes(int device) {
 
 }  // namespace
 
+// NVTX annotations (header-only NVTX3: free when no tool is attached).  One
+// range per transfer from submit to the end of wait() (started and ended on
+// possibly different host threads), a nested push/pop range around each
+// lane's copy-engine enqueue and around each lane-kernel launch, all in the
+// "pcie_pool_b200" domain.
+nvtxDomainHandle_t nvtx_domain() {
+  static nvtxDomainHandle_t d = nvtxDomainCreateA("pcie_pool_b200");
+  return d;
+}
+
+nvtxRangeId_t nvtx_start(const std::string& msg, uint32_t color) {
+  nvtxEventAttributes_t a{};
+  a.version = NVTX_VERSION;
+  a.size = NVTX_EVENT_ATTRIB_STRUCT_SIZE;
+  a.colorType = NVTX_COLOR_ARGB;
+  a.color = color;
+  a.messageType = NVTX_MESSAGE_TYPE_ASCII;
+  a.message.ascii = msg.c_str();
+  return nvtxDomainRangeStartEx(nvtx_domain(), &a);
+}
+
+struct NvtxScope {
+  explicit NvtxScope(const std::string& msg, uint32_t color) {
+    nvtxEventAttributes_t a{};
+    a.version = NVTX_VERSION;
+    a.size = NVTX_EVENT_ATTRIB_STRUCT_SIZE;
+    a.colorType = NVTX_COLOR_ARGB;
+    a.color = color;
+    a.messageType = NVTX_MESSAGE_TYPE_ASCII;
+    a.message.ascii = msg.c_str();
+    nvtxDomainRangePushEx(nvtx_domain(), &a);
+  }
+  ~NvtxScope() { nvtxDomainRangePop(nvtx_domain()); }
+};
+
 struct PoolEngine::Pending {
   struct LaneRec {
     int device = -1;
@@ -93,6 +130,7 @@ struct PoolEngine::Pending {
   uint64_t id = 0;
   int target = 0;
   int direction = 0;
+  nvtxRangeId_t nvtx = 0;   // transfer range (submit -> wait)
   size_t total_chunks = 0;  // chunks in spec order (for the checksum vector)
   std::vector<int> spec_chunk_to_kernel;  // spec-order chunk -> kernel chunk (-1: none)
   std::vector<int> kernel_lane_to_spec;   // kernel lane index -> spec lane index
@@ -470,6 +508,10 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
   P.direction = s.direction;
   P.timeout_s = s.timeout_s > 0 ? s.timeout_s : options_.timeout_s;
   P.t_submit = std::chrono::steady_clock::now();
+  P.nvtx = nvtx_start("transfer " + std::to_string(P.id) + (s.direction == 0 ? " h2d" : " d2h") + " target " +
+                          std::to_string(s.target) + " lanes " + std::to_string(s.lanes.size()) + " op " +
+                          std::to_string(s.op),
+                      0xFF2E86C1u);
 
   // ---- classify lanes --------------------------------------------------------
   for (const auto& L : s.lanes) {
@@ -708,8 +750,13 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     }
     // Launch before any copy-engine work is queued: if the launch fails no
     // relay stream is left waiting for a kernel that never runs.
-    const cudaError_t lrc = h2d ? launch_land(kp, static_cast<int>(cta), tkern)
-                                : launch_push(kp, static_cast<int>(cta), tkern);
+    cudaError_t lrc;
+    {
+      NvtxScope k(std::string(h2d ? "land_kernel" : "push_kernel") + " launch: " + std::to_string(cta) + " CTAs, " +
+                      std::to_string(chunks_d.size()) + " chunks",
+                  0xFF28B463u);
+      lrc = h2d ? launch_land(kp, static_cast<int>(cta), tkern) : launch_push(kp, static_cast<int>(cta), tkern);
+    }
     if (lrc != cudaSuccess) {
       cudaStreamSynchronize(tkern);  // the scratch upload is done before reuse
       give_scratch(T, P.scratch);
@@ -737,6 +784,7 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
   }
 
   // ---- copy-engine side, chunks interleaved round-robin across lanes ------------
+  NvtxScope enqueue("copy-engine enqueue: " + std::to_string(s.lanes.size()) + " lanes", 0xFFF39C12u);
   const uint8_t* host = reinterpret_cast<const uint8_t*>(s.host_ptr);
   uint8_t* devp = reinterpret_cast<uint8_t*>(s.dev_ptr);
   std::vector<size_t> next(s.lanes.size(), 0);
@@ -878,6 +926,7 @@ TransferResult PoolEngine::wait(uint64_t id, double host_timeout_s) {
   Pp = std::move(it->second);
   pending_.erase(it);
   Pending& P = *Pp;
+  if (P.nvtx) nvtxDomainRangeEnd(nvtx_domain(), P.nvtx);
   if (!done) {
     // Watchdog: something never advanced (kernel not scheduled, peer stuck).
     // Push every counter of this transfer far ahead from the host so no copy

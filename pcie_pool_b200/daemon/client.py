@@ -27,18 +27,19 @@ class TurboBusDaemonClient:
             self._conn.close()
             self._conn = None
 
-    def send(self, request: DaemonRequest) -> DaemonResponse:
+    def send(self, request: DaemonRequest, fds=None) -> DaemonResponse:
         msg = asdict(request)
         msg["request_type"] = RequestType(request.request_type).value
         msg.pop("peer_identity", None)
-        data = self._conn.request(msg) if self._conn is not None else send_request(
-            self.socket_path, msg, self._timeout)
+        data = self._conn.request(msg, fds=fds) if self._conn is not None else send_request(
+            self.socket_path, msg, self._timeout, fds=fds)
         return DaemonResponse(ok=bool(data["ok"]), payload=data.get("payload", {}) or {},
                               error=data.get("error"))
 
     def _call(self, rtype: RequestType, payload: dict | None = None,
-              session_id: str | None = None) -> DaemonResponse:
-        return self.send(DaemonRequest(request_type=rtype, session_id=session_id, payload=payload or {}))
+              session_id: str | None = None, fds=None) -> DaemonResponse:
+        req = DaemonRequest(request_type=rtype, session_id=session_id, payload=payload or {})
+        return self.send(req, fds=fds) if fds else self.send(req)
 
     def register_session(self, target_gpu: int, relay_gpus: list[int], max_inflight_chunks: int = 8,
                          connection_scoped: bool = False) -> DaemonResponse:
@@ -64,7 +65,10 @@ class TurboBusDaemonClient:
 
     def register_buffer(self, buffer_id: str, job_id: str, kind: str, size_bytes: int,
                         device_index: int | None = None, address: int | None = None, pinned: bool = False,
-                        handle_type: str = "registered_buffer", metadata: dict | None = None) -> DaemonResponse:
+                        handle_type: str = "registered_buffer", metadata: dict | None = None,
+                        fds: list[int] | None = None) -> DaemonResponse:
+        """``fds``: descriptors the buffer needs in the daemon (a CUDA VMM
+        export), passed beside the request."""
         p: dict[str, object] = {"buffer_id": str(buffer_id), "job_id": str(job_id), "kind": str(kind),
                                 "size_bytes": int(size_bytes), "pinned": bool(pinned),
                                 "handle_type": str(handle_type)}
@@ -74,7 +78,7 @@ class TurboBusDaemonClient:
             p["address"] = int(address)
         if metadata is not None:
             p["metadata"] = dict(metadata)
-        return self._call(RequestType.REGISTER_BUFFER, p)
+        return self._call(RequestType.REGISTER_BUFFER, p, fds=fds)
 
     def reserve_transfer(self, session_id: str, relay_gpu: int, chunks: int, bytes_: int = 0,
                          direction: str = "unknown") -> DaemonResponse:
@@ -194,8 +198,9 @@ class InProcessDaemonClient(TurboBusDaemonClient):
         self._conn = None
         self._timeout = None
 
-    def send(self, request: DaemonRequest) -> DaemonResponse:
-        return self._daemon.handle_request(request)
+    def send(self, request: DaemonRequest, fds=None) -> DaemonResponse:
+        # same process: the descriptors are valid here as they are
+        return self._daemon.handle_request(request, fds=list(fds) if fds else None)
 
 
 __all__ = ["InProcessDaemonClient", "TurboBusDaemonClient"]

@@ -144,6 +144,16 @@ class EngineDataPlane:
         return int(buf.address)
 
     def device_pointer(self, buf: BufferRegistration) -> int:
+        if buf.handle_type == "cuda_vmm_fd":
+            # import the exporter's VMM allocation once per registration
+            key = f"vmm:{buf.buffer_id}:{buf.metadata['vmm_fd']}"
+            with self._lock:
+                if key not in self._ipc:
+                    from .._native import native
+
+                    self._ipc[key] = native().vmm_import(int(buf.metadata["vmm_fd"]), int(buf.device_index or 0),
+                                                         int(buf.metadata["vmm_mapped_bytes"]))
+                return self._ipc[key]
         if buf.handle_type == "cuda_ipc_device":
             h = str(buf.metadata["cuda_ipc_handle"])
             with self._lock:

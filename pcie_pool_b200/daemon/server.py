@@ -82,6 +82,7 @@ class DaemonState:
     job_peers: dict[str, PeerIdentity] = field(default_factory=dict)
     session_peers: dict[str, PeerIdentity] = field(default_factory=dict)
     buffers: dict[str, BufferRegistration] = field(default_factory=dict)
+    buffer_fds: dict[str, int] = field(default_factory=dict)  # daemon-owned VMM descriptors
     sessions: dict[str, Session] = field(default_factory=dict)
     reservations: dict[str, TransferReservation] = field(default_factory=dict)
     reservation_transfer: dict[str, str] = field(default_factory=dict)
@@ -289,10 +290,29 @@ class TurboBusDaemon:
                         device_index: int | None = None, address: int | None = None,
                         pinned: bool = False, handle_type: str = "registered_buffer",
                         metadata: dict | None = None,
-                        peer_identity: PeerIdentity | None = None) -> DaemonResponse:
-        buf = BufferRegistration(buffer_id=buffer_id, job_id=job_id, kind=kind, size_bytes=size_bytes,
-                                 device_index=device_index, address=address, pinned=pinned,
-                                 handle_type=handle_type, metadata=metadata or {})
+                        peer_identity: PeerIdentity | None = None, fds: list[int] | None = None) -> DaemonResponse:
+        md = dict(metadata or {})
+        owned_fd = None
+        if str(handle_type).lower() == "cuda_vmm_fd":
+            # keep a duplicate of the exporter's descriptor for as long as the
+            # buffer stays registered (the executor imports and maps it)
+            if fds:
+                if len(fds) != 1:
+                    return fail("a cuda_vmm_fd buffer takes exactly one descriptor")
+                owned_fd = os.dup(int(fds[0]))
+            elif "vmm_fd" in md:  # in-process caller: its own descriptor number
+                owned_fd = os.dup(int(md["vmm_fd"]))
+            else:
+                return fail("a cuda_vmm_fd buffer needs its descriptor attached")
+            md["vmm_fd"] = owned_fd
+        try:
+            buf = BufferRegistration(buffer_id=buffer_id, job_id=job_id, kind=kind, size_bytes=size_bytes,
+                                     device_index=device_index, address=address, pinned=pinned,
+                                     handle_type=handle_type, metadata=md)
+        except (TypeError, ValueError):
+            if owned_fd is not None:
+                os.close(owned_fd)
+            raise
         with self._lock:
             self._reap(self._now())
             if buf.job_id not in self._st.jobs:
@@ -302,9 +322,24 @@ class TurboBusDaemon:
             except ValueError as exc:
                 return fail(str(exc))
             if self._buffer_leases(buf.buffer_id):
+                if owned_fd is not None:
+                    os.close(owned_fd)
                 return fail("buffer has active lease")
+            self._drop_buffer(buf.buffer_id)
             self._st.buffers[buf.buffer_id] = buf
+            if owned_fd is not None:
+                self._st.buffer_fds[buf.buffer_id] = owned_fd
             return ok(buffer=asdict(buf))
+
+    def _drop_buffer(self, buffer_id: str):
+        """Forget a registration and close the descriptor the daemon kept for it."""
+        fd = self._st.buffer_fds.pop(str(buffer_id), None)
+        if fd is not None:
+            try:
+                os.close(fd)
+            except OSError:
+                pass
+        return self._st.buffers.pop(str(buffer_id), None)
 
     # ---- cleanup -----------------------------------------------------------------------
     def cleanup(self, target_kind: str, target_id: str, reason: str, force: bool = False) -> DaemonResponse:
@@ -322,7 +357,7 @@ class TurboBusDaemon:
                 transfers = self._transfers_for_buffer(tid)
                 for lid in self._buffer_leases(tid):
                     merge_removed(removed, self._release_counted(lid, TransferStatusState.CANCELED, req.reason))
-                if self._st.buffers.pop(tid, None) is not None:
+                if self._drop_buffer(tid) is not None:
                     removed["buffers"] += 1
                 for t in transfers:
                     if self._cancel_if_active(t, req.reason):
@@ -1024,14 +1059,17 @@ class TurboBusDaemon:
             self._reschedule(tid, self._now())
 
     # ---- wire -------------------------------------------------------------------------------------
-    def handle_request(self, request: DaemonRequest, connection_id: str | None = None) -> DaemonResponse:
+    def handle_request(self, request: DaemonRequest, connection_id: str | None = None,
+                       fds: list[int] | None = None) -> DaemonResponse:
+        """``fds``: descriptors that arrived with the request (valid in this
+        process until the call returns; the daemon keeps duplicates)."""
         try:
-            return self._dispatch_request(request, connection_id)
-        except (KeyError, TypeError, ValueError) as exc:
+            return self._dispatch_request(request, connection_id, fds or [])
+        except (KeyError, TypeError, ValueError, OSError) as exc:
             return fail(f"invalid request: {exc}")
 
     def handle_wire_message(self, data: bytes | str, peer_identity: PeerIdentity | None = None,
-                            connection_id: str | None = None) -> DaemonResponse:
+                            connection_id: str | None = None, fds: list[int] | None = None) -> DaemonResponse:
         try:
             text = data.decode("utf-8") if isinstance(data, bytes) else str(data)
             obj = json.loads(text)
@@ -1045,7 +1083,12 @@ class TurboBusDaemon:
                                 peer_identity=peer_identity)
         except Exception as exc:  # noqa: BLE001 - every malformed message gets an error reply
             return fail(f"invalid request: {exc}")
-        return self.handle_request(req, connection_id=connection_id)
+        # a descriptor number in the JSON would name one of the daemon's own
+        # files: over the socket only attached descriptors count
+        md = payload.get("metadata") if isinstance(payload.get("metadata"), dict) else None
+        if md is not None and "vmm_fd" in md:
+            return fail("vmm_fd cannot be given in the request; attach the descriptor instead")
+        return self.handle_request(req, connection_id=connection_id, fds=fds)
 
     def close_connection(self, peer_identity: PeerIdentity | None, connection_id: str | None,
                          reason: str = "socket_disconnect") -> dict[str, int]:
@@ -1068,7 +1111,7 @@ class TurboBusDaemon:
 
         serve_unix(self, socket_path, stop_event=stop_event, ready_event=ready_event)
 
-    def _dispatch_request(self, r: DaemonRequest, conn_id: str | None) -> DaemonResponse:
+    def _dispatch_request(self, r: DaemonRequest, conn_id: str | None, fds: list[int] | None = None) -> DaemonResponse:
         p = r.payload
         T = RequestType
         t = r.request_type
@@ -1083,7 +1126,7 @@ class TurboBusDaemon:
                 size_bytes=int(p.get("size_bytes", 0)), device_index=p.get("device_index"),
                 address=p.get("address"), pinned=bool(p.get("pinned", False)),
                 handle_type=str(p.get("handle_type", "registered_buffer")), metadata=p.get("metadata") or {},
-                peer_identity=r.peer_identity)
+                peer_identity=r.peer_identity, fds=fds)
         if t == T.GET_INVENTORY:
             return self.get_inventory()
         if t == T.DISCOVER_RELAYS:
@@ -1516,7 +1559,7 @@ class TurboBusDaemon:
             S.job_peers.pop(j, None)
         for b, buf in list(S.buffers.items()):
             if buf.job_id in jobs:
-                S.buffers.pop(b, None)
+                self._drop_buffer(b)
                 nb += 1
         S.session_peers.pop(sid, None)
         if removed is not None:
@@ -1540,7 +1583,7 @@ class TurboBusDaemon:
                 out["transfers"] += 1
         for b, buf in list(S.buffers.items()):
             if buf.job_id == str(job_id):
-                S.buffers.pop(b, None)
+                self._drop_buffer(b)
                 out["buffers"] += 1
         return out
 

@@ -6,6 +6,11 @@ The server runs one thread per connection so a slow client (or a long
 WAIT_TRANSFER_RECEIPT) never blocks the others; peer identity comes from
 SO_PEERCRED; sessions registered as connection-scoped are closed when their
 connection ends.
+
+File descriptors (CUDA VMM buffer exports) travel beside a request as
+``SCM_RIGHTS`` ancillary data; the request says how many with a top-level
+``"attached_fds"`` count, and only the server -- never the JSON -- hands
+descriptors to the daemon.
 """
 
 from __future__ import annotations
@@ -35,17 +40,32 @@ def peer_identity_from_socket(conn: socket.socket) -> PeerIdentity:
                         unsupported_reason="SO_PEERCRED is unavailable on this platform")
 
 
+MAX_FDS_PER_MESSAGE = 8
+
+
+def _attached_fd_count(line: bytes) -> int:
+    if b'"attached_fds"' not in line:
+        return 0
+    try:
+        n = json.loads(line).get("attached_fds", 0)
+    except (ValueError, AttributeError):
+        return 0
+    return max(0, min(int(n), MAX_FDS_PER_MESSAGE)) if isinstance(n, int) else 0
+
+
 def _serve_connection(daemon, conn: socket.socket) -> None:
     peer = peer_identity_from_socket(conn)
     conn_id = str(uuid.uuid4())
     buf = b""
+    fds: list[int] = []  # received descriptors not yet claimed by a request
     try:
         with conn:
             while True:
                 try:
-                    data = conn.recv(1 << 16)
+                    data, got, _flags, _addr = socket.recv_fds(conn, 1 << 16, MAX_FDS_PER_MESSAGE)
                 except OSError:
                     break
+                fds.extend(got)
                 if not data:
                     break
                 buf += data
@@ -53,12 +73,21 @@ def _serve_connection(daemon, conn: socket.socket) -> None:
                     line, _, buf = buf.partition(b"\n")
                     if not line.strip():
                         continue
-                    resp = daemon.handle_wire_message(line, peer_identity=peer, connection_id=conn_id)
+                    n = _attached_fd_count(line)
+                    mine, fds = fds[:n], fds[n:]
+                    try:
+                        resp = daemon.handle_wire_message(line, peer_identity=peer, connection_id=conn_id,
+                                                          fds=mine)
+                    finally:
+                        for fd in mine:  # the daemon keeps its own duplicates
+                            os.close(fd)
                     try:
                         conn.sendall((json.dumps(asdict(resp), default=_json_default) + "\n").encode())
                     except OSError:
                         return
     finally:
+        for fd in fds:
+            os.close(fd)
         daemon.close_connection(peer, conn_id, reason="socket_disconnect")
 
 
@@ -127,14 +156,27 @@ def serve_unix(daemon, socket_path: str, *, stop_event: threading.Event | None =
             os.unlink(socket_path)
 
 
-def send_request(socket_path: str, message: dict, timeout: float | None = None) -> dict:
-    """One request over a fresh connection; returns the decoded response."""
+def _send(sock: socket.socket, message: dict, fds=None) -> None:
+    if fds:
+        message = {**message, "attached_fds": len(fds)}
+    data = (json.dumps(message, default=_json_default) + "\n").encode()
+    if fds:
+        sent = socket.send_fds(sock, [data], list(fds))
+        if sent < len(data):
+            sock.sendall(data[sent:])
+    else:
+        sock.sendall(data)
+
+
+def send_request(socket_path: str, message: dict, timeout: float | None = None, fds=None) -> dict:
+    """One request over a fresh connection; returns the decoded response.
+    ``fds`` ride along as SCM_RIGHTS ancillary data."""
     c = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
     if timeout is not None:
         c.settimeout(timeout)
     try:
         c.connect(socket_path)
-        c.sendall((json.dumps(message, default=_json_default) + "\n").encode())
+        _send(c, message, fds)
         data = b""
         while b"\n" not in data:
             chunk = c.recv(1 << 16)
@@ -160,9 +202,9 @@ class PersistentConnection:
         self._buf = b""
         self._lock = threading.Lock()
 
-    def request(self, message: dict) -> dict:
+    def request(self, message: dict, fds=None) -> dict:
         with self._lock:
-            self._sock.sendall((json.dumps(message, default=_json_default) + "\n").encode())
+            _send(self._sock, message, fds)
             while b"\n" not in self._buf:
                 chunk = self._sock.recv(1 << 16)
                 if not chunk:

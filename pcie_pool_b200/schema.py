@@ -275,6 +275,18 @@ def buffer_handle_metadata(*, kind: str, pinned: bool, device_index: int | None,
             off = md["cuda_ipc_offset"]
             if isinstance(off, bool) or not isinstance(off, int) or off < 0:
                 raise ValueError("cuda_ipc_offset must be a non-negative integer")
+    elif handle_type == "cuda_vmm_fd":
+        # a CUDA VMM allocation exported as a POSIX file descriptor; the
+        # descriptor itself travels beside the request (SCM_RIGHTS on the
+        # daemon socket) and the daemon records its own copy as ``vmm_fd``
+        if kind != "gpu" or device_index is None:
+            raise ValueError("cuda_vmm_fd handles require gpu buffers with a device_index")
+        mapped = md.get("vmm_mapped_bytes")
+        if isinstance(mapped, bool) or not isinstance(mapped, int) or mapped < int(size_bytes):
+            raise ValueError("cuda_vmm_fd metadata requires vmm_mapped_bytes covering the buffer")
+        if "vmm_fd" in md and (isinstance(md["vmm_fd"], bool) or not isinstance(md["vmm_fd"], int)
+                               or md["vmm_fd"] < 0):
+            raise ValueError("vmm_fd must be a descriptor number")
     return md
 
 
