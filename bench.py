@@ -49,6 +49,8 @@ def parse_args(argv=None):
                         "among the visible GPUs, or simply GPUs 0..N-1")
     p.add_argument("--no-checksum", action="store_true", help="skip the fused per-chunk checksum")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-extra", action="store_true",
+                   help="skip the other two BASELINE metrics (8B-shape load s, KV reload p50)")
     p.add_argument("--json-out", default="")
     p.add_argument("--reference-e2e-child", action="store_true", help=argparse.SUPPRESS)
     return p.parse_args(argv)
@@ -102,7 +104,47 @@ class Dist:
 
 # ---- clocks and host data ---------------------------------------------------------------
 
-from pcie_pool_b200.benchmarks.common import ClockSampler, fill_random  # noqa: E402
+from pcie_pool_b200.benchmarks.common import ClockSampler, fill_random, fill_random_torch  # noqa: E402
+
+
+# ---- the other two BASELINE metrics ---------------------------------------------------------
+
+def extra_metrics(args, impl: str, devices) -> dict:
+    """Llama-3-8B-shape bf16 load time (BASELINE config 3a, 16.06 GB into
+    GPU0 over the lane set) and the vLLM KV reload p50 (config 4: 32k-token
+    requests of a Llama-3-8B KV cache restored into permuted block tables),
+    on the same GPUs as the headline.  Ours goes through the daemon (intents
+    under relay leases); the reference through its own runtime.  Measured
+    after the headline's timed region; each failure is reported in place of
+    its figure."""
+    from types import SimpleNamespace
+
+    from pcie_pool_b200.benchmarks import kv_offload, llama_load
+
+    out: dict = {}
+    common = dict(gpus=len(devices), devices=list(devices), impl=impl, via="daemon", json_out="")
+    try:
+        a = SimpleNamespace(**common, steps=3, warmup=1, variant="bf16", chunk=16 << 20, api=False, layers=0)
+        r = llama_load.run_reference(a) if impl == "reference" else llama_load.run_ours(a)
+        out["load_s"] = (r["unavailable"] if "unavailable" in r else round(r["ms"] / 1e3, 4))
+        out["load_verified"] = r.get("verified")
+    except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+        out["load_s"] = f"error: {type(exc).__name__}: {exc}"
+    try:
+        import statistics
+
+        a = SimpleNamespace(**common, requests=4, tokens=32768, layers=32, steps=2, warmup=1, chunk=4 << 20, seed=0)
+        r = kv_offload.run_reference(a) if impl == "reference" else kv_offload.run_ours(a)
+        if "unavailable" in r:
+            out["kv_reload_p50_ms"] = r["unavailable"]
+        else:
+            out["kv_reload_p50_ms"] = round(statistics.median(r["reload_ms"]), 3)
+            out["kv_offload_p50_ms"] = round(statistics.median(r["offload_ms"]), 3)
+            out["kv_verified"] = r.get("verified")
+            out["kv_config"] = "Llama-3-8B KV, 4 requests x 32k tokens (4 GiB each), permuted block tables"
+    except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+        out["kv_reload_p50_ms"] = f"error: {type(exc).__name__}: {exc}"
+    return out
 
 
 # ---- our implementation ---------------------------------------------------------------
@@ -213,8 +255,11 @@ def run_ours(args, dist: Dist) -> dict:
                 out["e2e_inprocess"] = public_api_pooled_load(args, eng, host, dev, profile)
             except Exception as exc:  # pragma: no cover - reported in the JSON line
                 out["e2e_inprocess"] = {"error": f"{type(exc).__name__}: {exc}"}
-        del eng
+        del eng, dev
         host.release()
+        torch.cuda.empty_cache()
+        if not args.no_extra and direction == H2D:
+            out["extra"] = extra_metrics(args, "ours", devices)
     return out
 
 
@@ -361,7 +406,7 @@ def run_reference(args, dist: Dist) -> dict:
             return {"unavailable": "reference native extension failed to import"}
         torch.cuda.set_device(0)
         host_t = torch.empty(n, dtype=torch.uint8, pin_memory=True)
-        fill_random(host_t.numpy(), seed=1234)
+        fill_random_torch(host_t, seed=1234)
         dev = torch.empty(n, dtype=torch.uint8, device="cuda:0")
         opts = RuntimeOptions(chunk_bytes=args.chunk)
         rt = native.Runtime(opts.to_native())
@@ -417,6 +462,8 @@ def run_reference(args, dist: Dist) -> dict:
         torch.cuda.empty_cache()
         if not args.no_e2e and args.direction == "h2d":
             out["e2e"] = reference_e2e_isolated(args, ref_root)
+        if not args.no_extra and args.direction == "h2d":
+            out["extra"] = extra_metrics(args, "reference", list(range(N)))
     return out
 
 
@@ -462,7 +509,7 @@ def reference_e2e_child(args) -> int:
     torch.cuda.set_device(0)
     n = args.bytes
     host_t = torch.empty(n, dtype=torch.uint8, pin_memory=True)
-    fill_random(host_t.numpy(), seed=1234)
+    fill_random_torch(host_t, seed=1234)
     dev = torch.empty(n, dtype=torch.uint8, device="cuda:0")
     relays = list(range(1, args.gpus))
     rt = native.Runtime(RuntimeOptions(chunk_bytes=args.chunk).to_native())
@@ -525,6 +572,7 @@ def main(argv=None) -> int:
                 },
                 "clocks": res.get("clocks"),
                 "gpu_launches": res.get("gpu_launches"),
+                **{k: v for k, v in (res.get("extra") or {}).items()},
                 "verified": res.get("verified"),
                 "lane_ms": res.get("lane_ms"),
             }

@@ -80,6 +80,21 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
+def fill_random_torch(host_t, seed: int = 0, device: int = 0) -> None:
+    """Uniform-random bytes into a host uint8 tensor, generated on the GPU
+    with torch and copied back.  The reference arms use this one: nothing of
+    this project's native code may run on their path."""
+    import torch
+
+    g = torch.Generator(device=f"cuda:{device}").manual_seed(int(seed))
+    step = 1 << 30
+    n = host_t.numel()
+    for o in range(0, n, step):
+        k = min(step, n - o)
+        host_t[o:o + k].copy_(torch.randint(0, 256, (k,), dtype=torch.uint8, device=f"cuda:{device}", generator=g))
+    torch.cuda.synchronize(device)
+
+
 def fill_random(arr, seed: int = 0, threads: int = 0) -> None:
     """Uniform-random bytes into a numpy uint8 array (native, multithreaded)."""
     from .._native import native

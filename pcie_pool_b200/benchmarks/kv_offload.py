@@ -105,7 +105,7 @@ def run_ours(a) -> dict:
 
     torch.cuda.set_device(0)
     w = KVWorld(a)
-    devices = list(range(a.gpus))
+    devices = list(getattr(a, "devices", None) or range(a.gpus))
     eng = PoolEngine(devices, slot_bytes=a.chunk, slots=3, ctas_per_lane=4, timeout_s=30.0)
     lane_set, _weights, balancer, profile = calibrate(eng, 0, devices, w.req_bytes, a.chunk)
     relays = [d for d in lane_set if d != 0]

@@ -104,7 +104,7 @@ def run_ours(a) -> dict:
 
     manifest = _manifest(a.layers)
     total = manifest.total_bytes
-    devices = list(range(a.gpus))
+    devices = list(getattr(a, "devices", None) or range(a.gpus))
     torch.cuda.set_device(0)
     host = _host_image(manifest)
     eng = PoolEngine(devices, slot_bytes=a.chunk, slots=3, ctas_per_lane=4, timeout_s=30.0)
@@ -178,7 +178,7 @@ def _api_load(a, eng, host, dst, manifest, profile) -> dict:
     from ..schema import WorkloadKind
 
     total = manifest.total_bytes
-    devices = list(range(a.gpus))
+    devices = list(getattr(a, "devices", None) or range(a.gpus))
     _daemon, dc = build_inprocess_node(eng, devices, 0, profile)
     sid = dc.register_session(0, devices[1:], max_inflight_chunks=1 << 16).payload["session"]["session_id"]
     dc.register_job("llama-load", session_id=sid)
@@ -239,9 +239,15 @@ def run_reference(a) -> dict:
     if rt is None:
         return {"unavailable": why}
     host_t = torch.empty(total, dtype=torch.uint8, pin_memory=True)
-    from .._native import native
-
-    native().fill_normal_bf16(host_t.data_ptr(), total // 2, 0.0, 0.02, 20240601, 0)
+    # random-init image made with torch only: nothing of this project's
+    # native code runs on the reference's path
+    g = torch.Generator(device="cuda:0").manual_seed(20240601)
+    step = 1 << 30
+    for o in range(0, total, step):
+        n = min(step, total - o)
+        w = torch.randn(n // 2, device="cuda:0", generator=g, dtype=torch.float32).mul_(0.02).to(torch.bfloat16)
+        host_t[o:o + n].copy_(w.view(torch.uint8))
+    del w
     dst = torch.empty(total, dtype=torch.uint8, device="cuda:0")
     nplan, _profile = reference_plan(rt, total, a.chunk)
 

@@ -73,25 +73,45 @@ def jain(xs) -> float:
     return (sum(xs) ** 2) / (len(xs) * sum(x * x for x in xs)) if xs else 0.0
 
 
+class _Host:
+    """A page-locked host buffer (torch)."""
+
+    def __init__(self, n: int) -> None:
+        import torch
+
+        self.t = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+        self.ptr = int(self.t.data_ptr())
+
+    def numpy(self):
+        return self.t.numpy()
+
+    def release(self) -> None:
+        self.t = None
+
+
 class Tenants:
     """Host and device buffers of every GPU shard."""
 
     def __init__(self, a):
         import torch
 
-        from .._native import native
-        from ..utils.host_memory import PinnedHostBuffer
-
+        # torch only (page-locked tensors, device RNG): both arms use these
+        # buffers and nothing of this project's native code may run on the
+        # reference's path
         self.n = shard_bytes(a)
         self.gpus = list(range(a.jobs * a.gpus_per_job))
         self.job_of = {g: g // a.gpus_per_job for g in self.gpus}
-        C = native()
         self.host_params, self.host_grads, self.dev_params, self.dev_grads = {}, {}, {}, {}
         for g in self.gpus:
-            hp = PinnedHostBuffer(self.n, fill=None)
-            C.fill_normal_bf16(hp.ptr, self.n // 2, 0.0, 0.02, 1000 + g, 0)
+            hp = _Host(self.n)
+            gen = torch.Generator(device=f"cuda:{g}").manual_seed(1000 + g)
+            step = 1 << 30
+            for o in range(0, self.n, step):
+                k = min(step, self.n - o)
+                w = (torch.randn(k // 2, device=f"cuda:{g}", generator=gen) * 0.02).to(torch.bfloat16)
+                hp.t[o:o + k].copy_(w.view(torch.uint8))
             self.host_params[g] = hp
-            self.host_grads[g] = PinnedHostBuffer(self.n, fill=None)
+            self.host_grads[g] = _Host(self.n)
             self.dev_params[g] = torch.empty(self.n, dtype=torch.uint8, device=f"cuda:{g}")
             dg = torch.empty(self.n // 2, dtype=torch.bfloat16, device=f"cuda:{g}")
             dg.normal_(0.0, 1e-3)
