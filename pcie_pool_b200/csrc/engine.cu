@@ -910,15 +910,23 @@ TransferResult PoolEngine::wait(uint64_t id, double host_timeout_s) {
     tmo = host_timeout_s > 0 ? host_timeout_s : it->second->timeout_s * 2 + 10.0;
   }
   // Poll without holding the lock so other threads can keep submitting.
-  const auto deadline = std::chrono::steady_clock::now() + std::chrono::duration<double>(tmo);
+  const auto t_wait = std::chrono::steady_clock::now();
+  const auto deadline = t_wait + std::chrono::duration<double>(tmo);
   bool done = false;
   bool rescued = false;
   while (true) {
     const cudaError_t rc = cudaEventQuery(stop);
     if (rc == cudaSuccess) { done = true; break; }
     if (rc != cudaErrorNotReady) { check_cuda(rc, "cudaEventQuery(transfer stop)"); }
-    if (std::chrono::steady_clock::now() > deadline) break;
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    const auto now = std::chrono::steady_clock::now();
+    if (now > deadline) break;
+    // Small transfers finish within tens of microseconds: poll without
+    // sleeping for the first 200 us, then back off to 20 us sleeps.
+    if (now - t_wait < std::chrono::microseconds(200)) {
+      std::this_thread::yield();
+    } else {
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
   }
   const auto t_done = std::chrono::steady_clock::now();
   std::lock_guard<std::mutex> g(mu_);
