@@ -187,6 +187,7 @@ class DaemonKVOffloader:
         self.sync_stream = sync_stream
         self.in_process = isinstance(daemon_client, InProcessDaemonClient)
         self._seq = 0
+        self._spec = None
         self._host_ids: dict[int, str] = {}
         self._keep: list = []
         self.kv_buffer_ids = [f"{self.prefix}-layer{i}" for i in range(len(self.kv_caches))]
@@ -255,8 +256,13 @@ class DaemonKVOffloader:
         else:
             ranges = tuple({"src_offset": u0 * u, "dst_offset": h, "bytes": n * u} for h, u0, n in segs)
             src, dst = self.kv_buffer_ids[0], hid
-        spec = kv_spec(self.kv_caches, ids, self.kv_buffer_ids, op="scatter_units" if h2d else "gather_units",
-                       ctas_per_lane=self.ctas_per_lane)
+        if self._spec is None:  # the layer layout is fixed: check it once
+            self._spec = kv_spec(self.kv_caches, ids[:1], self.kv_buffer_ids, op="scatter_units",
+                                 ctas_per_lane=self.ctas_per_lane)
+        from dataclasses import replace
+
+        spec = replace(self._spec, op="scatter_units" if h2d else "gather_units",
+                       kv=replace(self._spec.kv, block_ids=tuple(ids)))
         self._seq += 1
         iid = f"{self.prefix}-{'restore' if h2d else 'save'}-{self._seq}"
         intent = TransferIntent(iid, self.job_id, self.session_id, src, dst, "h2d" if h2d else "d2h",

@@ -10,6 +10,8 @@ from __future__ import annotations
 
 from dataclasses import asdict
 
+from ..schema import contract_asdict
+
 from ..schema import (DaemonRequest, DaemonResponse, RequestType, TransferIntent,
                       WorkerTransferAuthorizationRequest)
 from ..transfer import TransferRequest
@@ -99,7 +101,9 @@ class TurboBusDaemonClient:
     def submit_transfer_intent(self, intent: TransferIntent) -> DaemonResponse:
         if not isinstance(intent, TransferIntent):
             raise TypeError("intent must be a TransferIntent")
-        return self._call(RequestType.SUBMIT_TRANSFER_INTENT, {"intent": asdict(intent)},
+        # shallow: an intent is immutable once built and may carry a large
+        # landing spec (block ids), which a deep copy would walk element by element
+        return self._call(RequestType.SUBMIT_TRANSFER_INTENT, {"intent": contract_asdict(intent)},
                           session_id=intent.session_id)
 
     def wait_transfer_receipt(self, intent_id: str, timeout_seconds: float | None = None) -> DaemonResponse:

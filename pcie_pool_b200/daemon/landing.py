@@ -52,6 +52,7 @@ from dataclasses import dataclass, field
 from typing import Any, Sequence
 
 OPS = ("copy", "scatter_units", "gather_units", "fp8_quant", "adamw")
+_PARSED: dict[int, tuple] = {}  # id(landing object) -> (object, parsed spec)
 TILE_ROWS = 128
 ADAM_TILE_PARAMS = 2048
 ADAM_TILE_BYTES = 3 * 4 * ADAM_TILE_PARAMS
@@ -107,10 +108,24 @@ class LandingSpec:
     # ---- wire form ------------------------------------------------------------------
     @classmethod
     def from_metadata(cls, meta: Any) -> "LandingSpec | None":
-        """The spec in ``intent.metadata["landing"]`` (None when absent)."""
+        """The spec in ``intent.metadata["landing"]`` (None when absent).
+        An intent is parsed at submit, by the buffer lookup and by the
+        executor: the parse of one landing object is remembered (by identity,
+        the object kept alive with it) so its block table is read once."""
         if not isinstance(meta, Mapping) or meta.get("landing") is None:
             return None
         d = meta["landing"]
+        hit = _PARSED.get(id(d))
+        if hit is not None and hit[0] is d:
+            return hit[1]
+        spec = cls._parse(d)
+        if len(_PARSED) >= 64:
+            _PARSED.pop(next(iter(_PARSED)))
+        _PARSED[id(d)] = (d, spec)
+        return spec
+
+    @classmethod
+    def _parse(cls, d: Any) -> "LandingSpec":
         if not isinstance(d, Mapping):
             raise ValueError("landing spec must be an object")
         op = str(d.get("op", "copy")).lower()
@@ -122,10 +137,14 @@ class LandingSpec:
             if not isinstance(k, Mapping):
                 raise ValueError("landing kv layout must be an object")
             try:
+                import numpy as np
+
+                ids = np.asarray(k["block_ids"], dtype=np.int64)
+                if ids.ndim != 1:
+                    raise ValueError("block_ids must be a flat list")
                 kv = KVUnits(buffers=tuple(str(b) for b in k["buffers"]), lanes=int(k.get("lanes", 1)),
                              lane_stride=int(k.get("lane_stride", 0)), block_stride=int(k["block_stride"]),
-                             num_blocks=int(k["num_blocks"]),
-                             block_ids=tuple(int(b) for b in k["block_ids"]))
+                             num_blocks=int(k["num_blocks"]), block_ids=tuple(ids.tolist()))
             except (KeyError, TypeError, ValueError) as exc:
                 raise ValueError(f"landing kv layout is incomplete: {exc}") from None
         tensors = []
@@ -316,12 +335,10 @@ def unit_addresses(spec: LandingSpec, base_of) -> "Any":
 
     k = spec.kv
     ids = np.asarray(k.block_ids, dtype=np.uint64)
-    parts = []
-    for bid in k.buffers:
-        base = np.uint64(int(base_of(bid)))
-        for lane in range(k.lanes):
-            parts.append(base + np.uint64(lane * k.lane_stride) + ids * np.uint64(k.block_stride))
-    return np.concatenate(parts).astype(np.uint64)
+    # one row per (layer, lane) base address, one column per block: stream order
+    bases = np.array([int(base_of(bid)) + lane * k.lane_stride for bid in k.buffers for lane in range(k.lanes)],
+                     dtype=np.uint64)
+    return (bases[:, None] + ids[None, :] * np.uint64(k.block_stride)).ravel()
 
 
 def annotate_lanes(spec: LandingSpec, lanes, h2d: bool) -> None:
@@ -367,9 +384,11 @@ def kv_spec(kv_caches, block_ids: Sequence[int], buffer_ids: Sequence[str], *, o
         if (x.lanes, x.lane_stride, x.block_stride, x.unit_bytes, x.num_blocks) != \
                 (l0.lanes, l0.lane_stride, l0.block_stride, l0.unit_bytes, l0.num_blocks):
             raise ValueError("all kv layers must share one layout")
+    import numpy as np
+
     return LandingSpec(op=op, unit_bytes=l0.unit_bytes,
                        kv=KVUnits(tuple(str(b) for b in buffer_ids), l0.lanes, l0.lane_stride, l0.block_stride,
-                                  l0.num_blocks, tuple(int(b) for b in block_ids)),
+                                  l0.num_blocks, tuple(np.asarray(block_ids, dtype=np.int64).tolist())),
                        ctas_per_lane=int(ctas_per_lane))
 
 
