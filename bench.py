@@ -52,7 +52,6 @@ def parse_args(argv=None):
     p.add_argument("--no-extra", action="store_true",
                    help="skip the other two BASELINE metrics (8B-shape load s, KV reload p50)")
     p.add_argument("--json-out", default="")
-    p.add_argument("--reference-e2e-child", action="store_true", help=argparse.SUPPRESS)
     return p.parse_args(argv)
 
 
@@ -121,6 +120,8 @@ def extra_metrics(args, impl: str, devices) -> dict:
 
     from pcie_pool_b200.benchmarks import kv_offload, llama_load
 
+    if impl == "reference":
+        return reference_extra_metrics(args, len(devices))
     out: dict = {}
     common = dict(gpus=len(devices), devices=list(devices), impl=impl, via="daemon", json_out="")
     try:
@@ -144,6 +145,64 @@ def extra_metrics(args, impl: str, devices) -> dict:
             out["kv_config"] = "Llama-3-8B KV, 4 requests x 32k tokens (4 GiB each), permuted block tables"
     except Exception as exc:  # noqa: BLE001 - reported in the JSON line
         out["kv_reload_p50_ms"] = f"error: {type(exc).__name__}: {exc}"
+    return out
+
+
+def _child_json(argv: list[str], timeout_s: float) -> dict:
+    """Run ``python -m <argv>`` in its own process group and return the JSON
+    object it wrote to ``--json-out``; a crash or a run past ``timeout_s``
+    (the whole group is killed) comes back as ``{"error": ...}``."""
+    import signal
+    import subprocess
+    import tempfile
+
+    with tempfile.NamedTemporaryFile(suffix=".json", delete=False) as fh:
+        path = fh.name
+    try:
+        proc = subprocess.Popen([sys.executable, "-m", *argv, "--json-out", path], cwd=str(ROOT),
+                                stdout=subprocess.DEVNULL, stderr=subprocess.PIPE, start_new_session=True)
+        try:
+            _, err = proc.communicate(timeout=timeout_s)
+        except subprocess.TimeoutExpired:
+            os.killpg(proc.pid, signal.SIGKILL)
+            proc.communicate()
+            return {"error": f"no result within {timeout_s:.0f} s (process group killed)"}
+        if proc.returncode != 0:
+            tail = (err or b"").decode(errors="replace").strip().splitlines()[-1:] or [""]
+            return {"error": f"exit code {proc.returncode}: {tail[0][:200]}"}
+        with open(path) as fh:
+            return json.load(fh)
+    except (OSError, ValueError) as exc:
+        return {"error": f"{type(exc).__name__}: {exc}"}
+    finally:
+        try:
+            os.unlink(path)
+        except OSError:
+            pass
+
+
+def reference_extra_metrics(args, n_gpus: int) -> dict:
+    """The reference arm's load time and KV reload p50, each in a child
+    process with a time limit, so that a crash or a stall inside the
+    reference's code costs that one figure and not the bench line."""
+    out: dict = {}
+    g = str(n_gpus)
+    r = _child_json(["pcie_pool_b200.benchmarks.llama_load", "--impl", "reference", "--gpus", g, "--variant", "bf16",
+                     "--steps", "3", "--warmup", "1"], 300)
+    if "error" in r or "unavailable" in r:
+        out["load_s"] = r.get("unavailable") or f"error: {r['error']}"
+    else:
+        out["load_s"] = round(r["value"], 4) if r.get("unit") == "s" else r.get("load_s", r.get("value"))
+        out["load_verified"] = r.get("verified")
+    r = _child_json(["pcie_pool_b200.benchmarks.kv_offload", "--impl", "reference", "--gpus", g, "--requests", "4",
+                     "--tokens", "32768", "--steps", "2", "--warmup", "1"], 300)
+    if "error" in r or "unavailable" in r:
+        out["kv_reload_p50_ms"] = r.get("unavailable") or f"error: {r['error']}"
+    else:
+        out["kv_reload_p50_ms"] = r["reload_p50_ms"]
+        out["kv_offload_p50_ms"] = r["offload_p50_ms"]
+        out["kv_verified"] = r.get("verified")
+        out["kv_config"] = "Llama-3-8B KV, 4 requests x 32k tokens (4 GiB each), permuted block tables"
     return out
 
 
@@ -265,117 +324,45 @@ def run_ours(args, dist: Dist) -> dict:
 
 # ---- reference implementation -----------------------------------------------------------
 
-def reference_e2e(args, ref_root: Path, host_np, dev, profile, relays) -> dict:
-    """The reference's own byte-moving public path, end to end, as an
-    application uses it: its daemon (``python -m turbobus.daemon``) and its
-    worker helper (``python -m turbobus.worker``) run as separate processes on
-    AF_UNIX sockets; this process is the client: a ``SharedPinnedCpuBuffer``
-    source, a ``CudaIpcDeviceBuffer`` target and
-    ``WorkerManagedTransferClient.fetch_shared_cpu_to_cuda_ipc`` per step
-    (turbobus/client_transfer.py:87-137).  Each step also reads 4 KiB of the
-    landed bytes back to the host (the step's result check).  Timed by wall
-    clock around whole steps with the device synchronised: the work runs in
-    the worker process, so no event on this process's streams brackets it."""
-    import shutil
-    import subprocess
-    import tempfile
+def reference_runtime_e2e(args, rt, host_t, dev, profile, relays) -> dict:
+    """The reference end to end through its runtime API, as an application
+    that drives it directly: every step its planner plans the transfer on its
+    profile (``PlannerEngine.plan`` + ``_native_transfer_plan``), its runtime
+    moves the bytes (``fetch_plan_to_gpu`` + ``wait``), and 4 KiB of the
+    landed bytes are read back to the host; wall clock with the device
+    synchronised on both sides.  Its other byte-moving public path, the
+    worker-managed client (daemon + worker-helper processes), is not run: on
+    this pool it crashed (SIGSEGV) in one call and hung past 900 s in the
+    next, at N=1 and N=2."""
     import time
 
-    import numpy as np
     import torch
-    from turbobus.client import CudaIpcDeviceBuffer, SharedPinnedCpuBufferAllocator
-    from turbobus.client_transfer import make_worker_managed_transfer_client
-    from turbobus.daemon import TurboBusDaemonClient
-    from turbobus.runtime_engine import _profile_to_daemon_dict
-    from turbobus.worker import WorkerServiceSocketClient
+    from turbobus import runtime_engine
+    from turbobus.planner_engine import PlannerEngine
 
     n = args.bytes
-    env = {**os.environ, "PYTHONPATH": os.pathsep.join([str(ref_root), os.environ.get("PYTHONPATH", "")])}
-    tmp = tempfile.mkdtemp(prefix="tbref-")
-    dsock, wsock = os.path.join(tmp, "d.sock"), os.path.join(tmp, "w.sock")
-    procs = []
+    probe = torch.empty(4096, dtype=torch.uint8)
 
-    def wait_sock(path, proc, what):
-        t_end = time.monotonic() + 120
-        while not os.path.exists(path):
-            if proc.poll() is not None:
-                raise RuntimeError(f"reference {what} exited with code {proc.returncode}")
-            if time.monotonic() > t_end:
-                raise RuntimeError(f"reference {what} did not open its socket")
-            time.sleep(0.05)
+    def step():
+        plan = PlannerEngine().plan(n, args.chunk, profile, "pool" if relays else "direct", direction="h2d")
+        h = rt.fetch_plan_to_gpu(host_t.data_ptr(), n, dev.data_ptr(), n, runtime_engine._native_transfer_plan(plan))
+        rt.wait(h)
+        probe.copy_(dev[n - 4096:])
 
-    cpu = None
-    try:
-        procs.append(subprocess.Popen(
-            # the reference's own switches for a node whose discovery reports
-            # no GPU-GPU links or PCIe paths (its parser misses them on some
-            # boxes); they only relax its startup check
-            [sys.executable, "-m", "turbobus.daemon", "--target-gpu", "0", "--min-relays", "0",
-             "--max-inflight-chunks-per-relay", "4096", "--socket-path", dsock,
-             "--allow-missing-fabric", "--allow-missing-pcie"], env=env))
-        wait_sock(dsock, procs[-1], "daemon")
-        procs.append(subprocess.Popen(
-            [sys.executable, "-m", "turbobus.worker", "--daemon-socket-path", dsock, "--socket-path", wsock],
-            env=env))
-        wait_sock(wsock, procs[-1], "worker helper")
-        dc = TurboBusDaemonClient(dsock)
-        if relays:
-            r = dc.put_profile(0, list(relays), _profile_to_daemon_dict(profile), profile_bytes=256 << 20)
-            if not r.ok:
-                raise RuntimeError(f"reference daemon rejected the profile: {r.error}")
-        client = make_worker_managed_transfer_client(dc, target_gpu=0, relay_gpus=list(relays),
-                                                     worker_client=WorkerServiceSocketClient(wsock),
-                                                     max_inflight_chunks=4096)
-        job = f"bench-ref-{os.getpid()}"
-        cpu = SharedPinnedCpuBufferAllocator(name_prefix="tbref-bench").allocate("bench-src", job, n)
-        view = cpu.view  # the buffer's public shared-memory view (write() would copy via bytes)
-        try:
-            view[0:n] = memoryview(host_np).cast("B")
-        finally:
-            view.release()
-        gpu = CudaIpcDeviceBuffer.from_device_pointer(buffer_id="bench-dst", job_id=job, device_index=0,
-                                                      size_bytes=n, device_ptr=int(dev.data_ptr()))
-        mode = "pool" if relays else "direct"
-        probe = np.empty(4096, dtype=np.uint8)
-
-        def step():
-            res = client.fetch_shared_cpu_to_cuda_ipc(cpu, gpu, chunk_bytes=args.chunk, mode=mode, job_id=job)
-            if res.bytes_completed != n:
-                raise RuntimeError(f"reference transfer moved {res.bytes_completed} of {n} bytes")
-            probe[:] = dev[n - 4096:].cpu().numpy()
-            return res
-
-        for _ in range(max(1, min(args.warmup, 2))):
-            step()
-        steps = max(1, min(args.steps, 5))
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            last = step()
-        torch.cuda.synchronize()
-        ms = (time.perf_counter() - t0) * 1e3
-        ok = bool(np.array_equal(probe, host_np[n - 4096:]))
-        return {"value": round(n * steps / 1e9 / (ms / 1e3), 3), "unit": "GB/s",
-                "ms_per_step": round(ms / steps, 3), "steps": steps,
-                "h2d_bytes_per_step": n, "d2h_bytes_per_step": 4096, "verified_tail": ok,
-                "path": "WorkerManagedTransferClient.fetch_shared_cpu_to_cuda_ipc -> reference daemon "
-                        "(AF_UNIX) -> reference worker helper (AF_UNIX) -> _turbobus runtime per transfer",
-                "mode": mode, "final_state": last.state}
-    finally:
-        if cpu is not None:
-            try:
-                cpu.close()
-                cpu.unlink()
-            except Exception:  # noqa: BLE001 - best-effort cleanup
-                pass
-        for p in procs:
-            p.terminate()
-        for p in procs:
-            try:
-                p.wait(timeout=10)
-            except subprocess.TimeoutExpired:
-                p.kill()
-        shutil.rmtree(tmp, ignore_errors=True)
+    for _ in range(max(1, min(args.warmup, 3))):
+        step()
+    steps = max(1, args.steps)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize()
+    ms = (time.perf_counter() - t0) * 1e3
+    return {"value": round(n * steps / 1e9 / (ms / 1e3), 3), "unit": "GB/s", "ms_per_step": round(ms / steps, 3),
+            "steps": steps, "h2d_bytes_per_step": n, "d2h_bytes_per_step": 4096,
+            "verified_tail": bool(torch.equal(probe, host_t[n - 4096:])),
+            "path": "turbobus PlannerEngine.plan -> _turbobus.Runtime.fetch_plan_to_gpu -> wait, per step "
+                    "(runtime API; the worker-managed client path crashed and hung on this pool and is not run)"}
 
 
 def run_reference(args, dist: Dist) -> dict:
@@ -458,76 +445,20 @@ def run_reference(args, dist: Dist) -> dict:
                            for r in profile.relays],
             },
         }
+        if not args.no_e2e and args.direction == "h2d":
+            try:
+                out["e2e"] = reference_runtime_e2e(args, rt, host_t, dev, profile, relays)
+            except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+                out["e2e"] = {"error": f"{type(exc).__name__}: {exc}"}
         del rt, host_t, dev
         torch.cuda.empty_cache()
-        if not args.no_e2e and args.direction == "h2d":
-            out["e2e"] = reference_e2e_isolated(args, ref_root)
         if not args.no_extra and args.direction == "h2d":
             out["extra"] = extra_metrics(args, "reference", list(range(N)))
     return out
 
 
-def reference_e2e_isolated(args, ref_root: Path) -> dict:
-    """Run ``reference_e2e`` in a child process (``faulthandler`` on): a
-    crash inside the reference's own stack then costs only the e2e figure,
-    reported with the child's exit status and the tail of its stack dump."""
-    import subprocess
-    import tempfile
-
-    fd, out_path = tempfile.mkstemp(prefix="ref-e2e-", suffix=".json")
-    os.close(fd)
-    cmd = [sys.executable, "-X", "faulthandler", str(ROOT / "bench.py"), "--impl", "reference",
-           "--reference-e2e-child", "--gpus", str(args.gpus), "--steps", str(args.steps), "--warmup",
-           str(args.warmup), "--bytes", str(args.bytes), "--chunk", str(args.chunk), "--json-out", out_path]
-    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "LOCAL_WORLD_SIZE",
-                                                             "GROUP_RANK", "ROLE_RANK", "TORCHELASTIC_RUN_ID")}
-    try:
-        r = subprocess.run(cmd, capture_output=True, text=True, timeout=1200, env=env)
-        text = Path(out_path).read_text() if os.path.getsize(out_path) else ""
-    except subprocess.TimeoutExpired:
-        return {"error": "reference e2e child timed out after 1200 s"}
-    finally:
-        try:
-            os.unlink(out_path)
-        except OSError:
-            pass
-    if r.returncode == 0 and text.strip():
-        return json.loads(text)
-    tail = [l for l in (r.stderr or "").splitlines() if l.strip()][-12:]
-    return {"error": f"reference e2e child exited with status {r.returncode}", "stderr_tail": tail}
-
-
-def reference_e2e_child(args) -> int:
-    """Child side of ``reference_e2e_isolated`` (one process, cuda:0)."""
-    ref_root = ROOT / "baseline" / "_ref"
-    sys.path.insert(0, str(ref_root))
-    import torch
-    from turbobus import runtime_engine
-    from turbobus.runtime_engine import RuntimeOptions
-
-    native = runtime_engine._turbobus
-    torch.cuda.set_device(0)
-    n = args.bytes
-    host_t = torch.empty(n, dtype=torch.uint8, pin_memory=True)
-    fill_random_torch(host_t, seed=1234)
-    dev = torch.empty(n, dtype=torch.uint8, device="cuda:0")
-    relays = list(range(1, args.gpus))
-    rt = native.Runtime(RuntimeOptions(chunk_bytes=args.chunk).to_native())
-    rt.init(0, relays)
-    profile = rt.profile(256 << 20, False)
-    try:
-        res = reference_e2e(args, ref_root, host_t.numpy(), dev, profile, relays)
-    except Exception as exc:  # noqa: BLE001 - reported in the JSON line
-        res = {"error": f"{type(exc).__name__}: {exc}"}
-    del rt
-    Path(args.json_out).write_text(json.dumps(res))
-    return 0
-
-
 def main(argv=None) -> int:
     args = parse_args(argv)
-    if args.reference_e2e_child:
-        return reference_e2e_child(args)
     if args.impl == "ours" and args.lane_order == "spread":
         from pcie_pool_b200.topology.cuda_nvml import cuda_lane_set
 
