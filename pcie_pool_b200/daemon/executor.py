@@ -256,6 +256,7 @@ class EngineDataPlane:
                             "gib_per_second": (l.bytes / (1 << 30)) / (l.cuda_ms / 1e3) if l.cuda_ms > 0 else 0.0}
                            for l in lane_stats],
         }
+        measured["landing_op"] = spec.op if spec is not None else "copy"
         if failover is not None:
             measured["failover"] = failover
             measured["fallback_reason"] = (f"lane failover: relay {failover['failed_lane_device']} failed, "

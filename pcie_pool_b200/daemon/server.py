@@ -127,7 +127,7 @@ class TurboBusDaemon:
                  scheduler: DaemonScheduler | None = None, executor=None,
                  profile_store_path: str | None = None,
                  clock: Callable[[], float] = time.time, link_hold_seconds: float = 1.0,
-                 history_limit: int = 10000, audit_limit: int = 100000) -> None:
+                 history_limit: int = 10000, audit_limit: int = 100000, lane_feedback: bool = True) -> None:
         self._lock = threading.RLock()
         self._changed = threading.Condition(self._lock)
         self._st = DaemonState()
@@ -150,6 +150,15 @@ class TurboBusDaemon:
         self._quotas = {g: RelayQuota(relay_gpu=g, max_sessions=int(max_sessions_per_relay),
                                       max_inflight_chunks=int(max_inflight_chunks_per_relay))
                         for g in norm_relays(relay_gpus)}
+        # Per-lane rates measured by the data plane, per (target, direction,
+        # landing op): a fused op loads the lanes differently from the plain
+        # copies a profile probes (the target's own landing kernel shares its
+        # SMs and HBM with every relay's), so each op's split converges to all
+        # lanes finishing together.  They refine the profile's concurrent
+        # lane rates once every lane of the profile has been measured.
+        from ..parallel.balance import LaneBalancer
+
+        self._feedback = LaneBalancer(alpha=0.5) if lane_feedback else None
         self._executor = None
         self._profile_store = profile_store_path
         if profile_store_path:
@@ -1015,6 +1024,8 @@ class TurboBusDaemon:
                           error: str | None = None, measured: dict | None = None) -> None:
         """Record the data plane's outcome: status, measured stats, leases."""
         m = measured or {}
+        if ok_ and self._feedback is not None:
+            self._observe_lanes(m)
         if ok_:
             _LOG.info("transfer_complete", transfer_id=transfer_id, bytes=int(bytes_completed),
                       cuda_ms=float(m.get("cuda_ms", 0.0) or 0.0), gb_per_s=float(m.get("gb_per_s", 0.0) or 0.0),
@@ -1036,6 +1047,44 @@ class TurboBusDaemon:
                                       min(int(bytes_completed), st.bytes_total), error or "data plane failed")
             self._changed.notify_all()
             self._readmit_delayed()
+
+    def _observe_lanes(self, m: Mapping) -> None:
+        stats = m.get("path_stats") or ()
+        if not stats or m.get("failover"):
+            return
+        rates: dict[int, float] = {}
+        for p in stats:
+            if not isinstance(p, Mapping) or float(p.get("cuda_ms", 0.0) or 0.0) <= 0.0:
+                return
+            dev = int(p["target_device"]) if int(p.get("relay_device", -1)) < 0 else int(p["relay_device"])
+            rates[dev] = float(p.get("gib_per_second", 0.0) or 0.0)
+        first = stats[0]
+        key = f"{first.get('direction', 'h2d')}:{m.get('landing_op', 'copy')}"
+        self._feedback.observe_rates(int(first.get("target_device", 0)), key, rates)
+
+    def _refined_profile(self, entry, target: int, direction: str, intent) -> Mapping | None:
+        """``entry`` with its concurrent ``direction`` lane rates replaced by
+        the rates measured for this intent's landing op, when every lane of
+        the profile has one; otherwise ``entry`` itself."""
+        from ..scheduler.daemon import profile_payload
+
+        payload = profile_payload(entry)
+        if payload is None or self._feedback is None:
+            return entry
+        spec = LandingSpec.from_metadata(intent.metadata) if intent is not None else None
+        rates = self._feedback.rates(target, f"{direction}:{spec.op if spec is not None else 'copy'}")
+        if not rates:
+            return entry
+        conc = dict(payload.get("concurrent") or {})
+        block = conc.get(direction)
+        lanes = ([int(x) for x in block["lanes"]] if isinstance(block, Mapping) and block.get("lanes") else
+                 [int(payload.get("target_device", target))] +
+                 [int(r["relay_device"]) for r in payload.get("relays", ()) or () if isinstance(r, Mapping)])
+        if not all(d in rates for d in lanes):
+            return entry
+        conc[direction] = {**(dict(block) if isinstance(block, Mapping) else {}), "lanes": lanes,
+                           "lane_gibps": {str(d): rates[d] for d in lanes}, "source": "measured lane feedback"}
+        return {**payload, "concurrent": conc}
 
     def _dispatch(self, tid: str, ticket: ExecutionTicket) -> None:
         if self._executor is None:
@@ -1326,6 +1375,7 @@ class TurboBusDaemon:
             max_inflight_chunks=session.max_inflight_chunks, active_chunks=session.active_chunks,
             active=session.active, created_at=session.created_at, last_seen=session.last_seen,
             closed_at=session.closed_at)
+        entry = self._refined_profile(entry, session.target_gpu, str(direction).lower(), intent)
         state = self._runtime_state(now, active_only=True)
         if exclude is not None:
             state = state_without_transfer(state, str(exclude))

@@ -39,6 +39,16 @@ class LaneBalancer:
                 prev = est.get(lane.device)
                 est[lane.device] = rate if prev is None else (1 - self.alpha) * prev + self.alpha * rate
 
+    def observe_rates(self, target: int, direction: str, rates: dict[int, float]) -> None:
+        """Fold measured per-lane rates (GiB/s by device) into the estimates."""
+        key = (int(target), str(direction))
+        with self._lock:
+            est = self._rates.setdefault(key, {})
+            for dev, rate in rates.items():
+                if rate > 0.0:
+                    prev = est.get(int(dev))
+                    est[int(dev)] = rate if prev is None else (1 - self.alpha) * prev + self.alpha * rate
+
     def seed(self, target: int, direction: str, rates: dict[int, float]) -> None:
         with self._lock:
             self._rates[(int(target), str(direction))] = {int(k): float(v) for k, v in rates.items()}
