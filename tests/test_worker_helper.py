@@ -166,18 +166,18 @@ def test_one_relay_of_the_ticket_narrows_the_ranges(rig):
 
 
 @pytest.mark.parametrize("mutate,msg", [
-    (lambda p: p["decision"].update(intent_id="someone-else"), "intent_id does not match scheduling decision"),
-    (lambda p: p["decision"].update(session_id="other-session"), "session_id does not match"),
-    (lambda p: p["decision"]["plan"].update(total_bytes=1), "plan does not match scheduling decision"),
-    (lambda p: p["src_buffer"].update(buffer_id="other"), "source buffer does not match"),
-    (lambda p: p["dst_buffer"].update(buffer_id="other"), "destination buffer does not match"),
+    (lambda p: p["decision"].update(intent_id="someone-else"), "intent_id differs from the scheduling decision"),
+    (lambda p: p["decision"].update(session_id="other-session"), "session_id differs"),
+    (lambda p: p["decision"]["plan"].update(total_bytes=1), "plan differs from the scheduling decision"),
+    (lambda p: p["src_buffer"].update(buffer_id="other"), "source buffer differs"),
+    (lambda p: p["dst_buffer"].update(buffer_id="other"), "destination buffer differs"),
     (lambda p: p["ticket"]["metadata"].update(issuer="not-the-daemon"), "issued by"),
     (lambda p: p.update(plan_generation=p["plan_generation"] + 1), "stale"),
-    (lambda p: p["ticket"]["metadata"].pop("plan_generation"), "missing plan_generation"),
+    (lambda p: p["ticket"]["metadata"].pop("plan_generation"), "no plan_generation"),
     (lambda p: p["ticket"]["metadata"].update(plan_generation=0), "positive"),
     (lambda p: p["ticket"]["metadata"].update(transfer_id=" "), "transfer_id"),
-    (lambda p: p.update(lease_id="not-a-lease"), "lease_id does not match"),
-    (lambda p: p.update(lease_ids=()), "lease_ids must be non-empty"),
+    (lambda p: p.update(lease_id="not-a-lease"), "not one of the requested lease_ids"),
+    (lambda p: p.update(lease_ids=()), "lease_ids is empty"),
 ], ids=["decision-intent", "decision-session", "decision-plan", "src-buffer", "dst-buffer", "issuer",
         "stale-generation", "no-generation", "zero-generation", "no-transfer-id", "foreign-lease", "no-leases"])
 def test_ticket_payload_rejections(rig, mutate, msg):
@@ -191,17 +191,17 @@ def test_data_plane_must_match_the_authority_and_handles(rig):
     _, _, payload = authorized(rig)
     wr = WorkerTransferRequest.from_authorization_payload(payload)
     a = wr.authorization
-    with pytest.raises(ValueError, match="data-plane lease_id does not match"):
+    with pytest.raises(ValueError, match="data-plane request's lease_id disagrees"):
         WorkerTransferRequest(authorization=replace(a, lease_id=wr.lease_ids[1]), ticket=wr.ticket,
                               data_plane=wr.data_plane)
     other = BufferRegistration(**{**asdict(a.src_buffer), "buffer_id": "elsewhere"})
-    with pytest.raises(ValueError, match="data-plane src handle does not match"):
+    with pytest.raises(ValueError, match="data-plane request's src handle disagrees"):
         WorkerTransferRequest(authorization=replace(a, src_buffer=other), ticket=wr.ticket, data_plane=wr.data_plane)
-    with pytest.raises(ValueError, match="data-plane ranges"):
+    with pytest.raises(ValueError, match="data-plane request's ranges"):
         WorkerTransferRequest(authorization=replace(a, ranges=a.ranges[:1]), ticket=wr.ticket,
                               data_plane=wr.data_plane)
     # without an explicit data plane the authorization's own is built, and the ticket must still agree
-    with pytest.raises(ValueError, match="ticket ranges do not match"):
+    with pytest.raises(ValueError, match="ticket's relay ranges disagree"):
         WorkerTransferRequest(authorization=replace(a, ranges=a.ranges[:1]), ticket=wr.ticket)
 
 
@@ -222,7 +222,7 @@ def _move_first_chunk(plan, key, value):
 
 
 @pytest.mark.parametrize("edit,msg", [
-    (lambda pl: pl.update(assignments=[]), "relay path"),
+    (lambda pl: pl.update(assignments=[]), "no relay lane"),
     (lambda pl: _move_first_chunk(pl, "dst_offset", N), "exceeds dst buffer size"),
     (lambda pl: _move_first_chunk(pl, "src_offset", N), "exceeds src buffer size"),
     (lambda pl: pl.update(total_bytes=pl["total_bytes"] + MiB), "total"),
