@@ -179,23 +179,28 @@ def main(argv=None) -> int:
         if r.state.value != "complete":
             raise RuntimeError(r.error)
 
+    cpu = []
+
     def timed(k):
         out = []
         for _ in range(5):
-            t0 = time.perf_counter()
+            t0, c0 = time.perf_counter(), time.process_time()
             for _ in range(max(1, k // 5)):
                 step()
             out.append((time.perf_counter() - t0) * 1e3 / max(1, k // 5))
+            cpu.append((time.process_time() - c0) * 1e3 / max(1, k // 5))
         return statistics.median(out)
 
     for _ in range(10):
         step()
     first = timed(a.intents)
+    cpu_first = statistics.median(cpu)
     for _ in range(a.history):
         step()
     later = timed(a.intents)
     print(json.dumps({"metric": "control-plane ms per intent (instant data plane)", "lanes": a.lanes, "bytes": n,
                       "chunk_bytes": chunk, "chunks": -(-n // chunk), "ms_per_intent": round(first, 3),
+                      "cpu_ms_per_intent": round(cpu_first, 3),
                       "ms_per_intent_after_history": round(later, 3), "history": a.history,
                       "retained_transfers": len(daemon.describe().payload["transfer_queue"])}), flush=True)
     return 0

@@ -95,17 +95,29 @@ def contract_asdict(obj: Any) -> dict[str, Any]:
     ranges) are shared rather than deep-copied.  Contracts are immutable once
     issued, and a plan of N chunks would otherwise be copied N-deep on every
     response (``dataclasses.asdict`` dominated the per-intent control cost)."""
+    cls = type(obj)
+    names = _FIELD_NAMES.get(cls)
+    if names is None:
+        names = _FIELD_NAMES[cls] = tuple(f.name for f in fields(obj))
     out: dict[str, Any] = {}
-    for f in fields(obj):
-        v = getattr(obj, f.name)
-        if is_dataclass(v) and not isinstance(v, type):
+    for name in names:
+        v = getattr(obj, name)
+        t = type(v)
+        if t is dict:
+            v = dict(v)
+        elif t is list:
+            v = list(v)
+        elif hasattr(t, "__dataclass_fields__"):
             v = contract_asdict(v)
         elif isinstance(v, dict):
             v = dict(v)
         elif isinstance(v, list):
             v = list(v)
-        out[f.name] = v
+        out[name] = v
     return out
+
+
+_FIELD_NAMES: dict[type, tuple[str, ...]] = {}
 
 
 # ---- field coercers ------------------------------------------------------------------
