@@ -16,6 +16,7 @@ measured per-lane statistics back to the daemon.  Data planes:
 from __future__ import annotations
 
 import threading
+from collections import OrderedDict
 import time
 import traceback
 from concurrent.futures import ThreadPoolExecutor
@@ -107,6 +108,7 @@ class EngineDataPlane:
         self._host_maps: dict[str, tuple[Any, int]] = {}
         self._ipc: dict[str, int] = {}
         self._lock = threading.Lock()
+        self._lane_cache: OrderedDict = OrderedDict()
 
     @property
     def engine(self):
@@ -119,6 +121,29 @@ class EngineDataPlane:
                 self._devices = list(range(torch.cuda.device_count()))
             self._engine = PoolEngine(self._devices, **self._engine_kw)
         return self._engine
+
+    def _lanes(self, plan, target: int, cache: bool):
+        """Engine lanes of a plan.  The scheduler reuses plan objects for a
+        repeated intent shape, so plain-copy lanes (which nothing annotates)
+        are kept per plan; the cache holds the plan's assignments so their
+        identity stays unique."""
+        from ..parallel.engine import lanes_from_plan
+
+        asg = plan.get("assignments")
+        if not cache or asg is None:
+            return lanes_from_plan(plan, target)
+        key = (id(asg), int(target))
+        with self._lock:
+            hit = self._lane_cache.get(key)
+            if hit is not None and hit[0] is asg:
+                self._lane_cache.move_to_end(key)
+                return list(hit[1])
+        lanes = lanes_from_plan(plan, target)
+        with self._lock:
+            self._lane_cache[key] = (asg, tuple(lanes))
+            while len(self._lane_cache) > 64:
+                self._lane_cache.popitem(last=False)
+        return lanes
 
     # -- buffer resolution ------------------------------------------------------------------
     def host_pointer(self, buf: BufferRegistration) -> int:
@@ -178,11 +203,11 @@ class EngineDataPlane:
         target = int(dev_buf.device_index or 0)
         host_ptr = self.host_pointer(host_buf)
         dev_ptr = self.device_pointer(dev_buf)
-        lanes = lanes_from_plan(ticket.plan, target)
-        eng = self.engine
-        direction = H2D if h2d else D2H
         # fused landing op named by the intent (validated by the daemon)
         spec = LandingSpec.from_metadata(intent.metadata) if intent is not None else None
+        lanes = self._lanes(ticket.plan, target, cache=spec is None or spec.op == "copy")
+        eng = self.engine
+        direction = H2D if h2d else D2H
         op_kw: dict = {}
         if spec is not None and spec.op != "copy":
             from .._native import native

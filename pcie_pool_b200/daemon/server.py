@@ -159,6 +159,7 @@ class TurboBusDaemon:
         from ..parallel.balance import LaneBalancer
 
         self._feedback = LaneBalancer(alpha=0.5) if lane_feedback else None
+        self._published: dict[tuple[int, str], tuple[object, dict, dict]] = {}
         self._executor = None
         self._profile_store = profile_store_path
         if profile_store_path:
@@ -541,7 +542,8 @@ class TurboBusDaemon:
             mode="auto", direction=intent.direction, job_id=intent.job_id,
             buffer_ids=[intent.source_buffer_id, intent.destination_buffer_id], ranges=intent.ranges,
             intent_id=intent.intent_id, workload_kind=intent.workload_kind.value,
-            priority=intent.priority, peer_identity=peer_identity, allow_delayed_admission=True)
+            priority=intent.priority, peer_identity=peer_identity, allow_delayed_admission=True,
+            _for_intent=True)
         if not planned.ok:
             return planned
         tid = str(planned.payload["transfer_id"])
@@ -800,7 +802,7 @@ class TurboBusDaemon:
                       intent_id: str | None = None, topology_snapshot_id: str | None = None,
                       workload_kind: str = "generic", priority: int = 0,
                       peer_identity: PeerIdentity | None = None,
-                      allow_delayed_admission: bool = False) -> DaemonResponse:
+                      allow_delayed_admission: bool = False, _for_intent: bool = False) -> DaemonResponse:
         now = self._now()
         try:
             rs = norm_ranges(ranges)
@@ -848,6 +850,9 @@ class TurboBusDaemon:
             if not reservations and len(bids) >= 2 and direct_only(decision):
                 tk = self._plan_ticket(tid, decision, bids[0], bids[1], now, None, ())
                 self._store_ticket(tid, tk)
+            if _for_intent:  # submit_transfer_intent answers with its own record of the decision
+                return DaemonResponse(ok=True, payload=self._intent_planned_payload(tid, session, relays, elig,
+                                                                                  reservations))
             return DaemonResponse(ok=True, payload=self._planned_payload(tid, decision, status, session,
                                                                          relays, elig, reservations))
 
@@ -1072,9 +1077,17 @@ class TurboBusDaemon:
         if payload is None or self._feedback is None:
             return entry
         spec = LandingSpec.from_metadata(intent.metadata) if intent is not None else None
-        rates = self._feedback.rates(target, f"{direction}:{spec.op if spec is not None else 'copy'}")
+        key = (int(target), f"{direction}:{spec.op if spec is not None else 'copy'}")
+        rates = self._feedback.rates(*key)
         if not rates:
             return entry
+        # Publish new rates only when a lane moved by more than 4 %: the
+        # split does not jitter with every measurement, and a repeated intent
+        # shape keeps hitting the scheduler's plan cache.
+        pub = self._published.get(key)
+        if pub is not None and pub[0] is payload and set(pub[1]) == set(rates) and all(
+                abs(rates[d] - pub[1][d]) <= 0.04 * pub[1][d] for d in rates):
+            return pub[2]
         conc = dict(payload.get("concurrent") or {})
         block = conc.get(direction)
         lanes = ([int(x) for x in block["lanes"]] if isinstance(block, Mapping) and block.get("lanes") else
@@ -1084,7 +1097,9 @@ class TurboBusDaemon:
             return entry
         conc[direction] = {**(dict(block) if isinstance(block, Mapping) else {}), "lanes": lanes,
                            "lane_gibps": {str(d): rates[d] for d in lanes}, "source": "measured lane feedback"}
-        return {**payload, "concurrent": conc}
+        refined = {**payload, "concurrent": conc}
+        self._published[key] = (payload, dict(rates), refined)
+        return refined
 
     def _dispatch(self, tid: str, ticket: ExecutionTicket) -> None:
         if self._executor is None:
@@ -1747,6 +1762,18 @@ class TurboBusDaemon:
             bytes_completed=st.bytes_completed, started_at=started, completed_at=done_at,
             path_stats=tuple(measured["path_stats"]) if measured and measured.get("path_stats") else decision.path_summary,
             error=err, metadata=md)
+
+    def _intent_planned_payload(self, tid, session, relays, elig, reservations) -> dict:
+        """The parts of a plan answer that an intent submission passes on."""
+        S = self._st
+        return {"admission": dict(S.admissions.get(str(tid), {})),
+                "plan_generation": S.generations.get(str(tid), 0), "plan_expires_at": S.plan_expiry.get(str(tid)),
+                "transfer_id": str(tid),
+                "planning": {"target_gpu": session.target_gpu, "profile_key": profile_key(session.target_gpu, relays),
+                             "relay_eligibility": elig},
+                "reservations": [asdict(r) for r in reservations],
+                "lease_tokens": [asdict(S.leases[r.reservation_id]) for r in reservations
+                                 if r.reservation_id in S.leases]}
 
     def _planned_payload(self, tid, decision, status, session, relays, elig, reservations) -> dict:
         S = self._st

@@ -14,7 +14,9 @@ any failure in 3-4 degrades to a direct plan with a ``fallback_reason``
 
 from __future__ import annotations
 
+import threading
 import uuid
+from collections import OrderedDict
 from dataclasses import dataclass
 from collections.abc import Mapping
 from typing import Callable
@@ -71,6 +73,14 @@ class DaemonScheduler:
         self._lease_id = lease_id_factory or (lambda: str(uuid.uuid4()))
         self._decision_id = decision_id_factory or (lambda: str(uuid.uuid4()))
         self._lease_seconds = max(0.0, float(lease_seconds))
+        # Plans are pure functions of (bytes, ranges, chunk, profile view,
+        # mode, direction) and immutable once issued, so a repeated intent
+        # shape (a training step, a KV layer group, a benchmark loop) reuses
+        # its plan, the plan's dict form and its path summary.
+        self._plans: OrderedDict = OrderedDict()
+        self._plans_lock = threading.Lock()
+        self.plan_cache_size = 256
+        self.plan_cache_hits = 0
 
     @property
     def planner(self) -> PlannerEngine:
@@ -118,6 +128,7 @@ class DaemonScheduler:
             plan = self._direct_plan(total, chunk, rs, profile, direction)
             leases = ()
         stats = plan_stats(plan, requested_mode=requested, fallback_reason=reason)
+        plan_dict, summary = self._plan_forms(plan)
         return SchedulingDecision(
             decision_id=self._decision_id(),
             intent_id=_cid(intent_id, "intent", session.session_id),
@@ -125,8 +136,8 @@ class DaemonScheduler:
             job_id=str(job_id or session.session_id),
             session_id=session.session_id,
             state=SchedulingDecisionState.FALLBACK if reason else SchedulingDecisionState.PLANNED,
-            plan=plan.as_dict(),
-            path_summary=path_summary(plan),
+            plan=plan_dict,
+            path_summary=summary,
             fallback_reason=reason,
             issued_at=float(now),
             metadata={"leases": [l.as_dict() for l in leases], "stats": stats.as_dict(),
@@ -168,20 +179,54 @@ class DaemonScheduler:
         return ProfileView(int(payload.get("target_device", session.target_gpu)), h2d, d2h,
                            tuple(relays), dict(payload.get("concurrent", {}) or {})), None
 
+    def _cached(self, key, make) -> PlannerTransferPlan:
+        with self._plans_lock:
+            hit = self._plans.get(key)
+            if hit is not None:
+                self._plans.move_to_end(key)
+                self.plan_cache_hits += 1
+                return hit[0]
+        plan = make()
+        with self._plans_lock:
+            self._plans[key] = (plan, None)
+            while len(self._plans) > self.plan_cache_size:
+                self._plans.popitem(last=False)
+        return plan
+
+    def _plan_forms(self, plan: PlannerTransferPlan) -> tuple[dict, tuple]:
+        """(dict form, path summary) of a plan, kept with the cached plan."""
+        with self._plans_lock:
+            for key in reversed(self._plans):
+                p, forms = self._plans[key]
+                if p is plan:
+                    if forms is None:
+                        forms = (plan.as_dict(), path_summary(plan))
+                        self._plans[key] = (p, forms)
+                    return forms
+                break  # only the entry just used is looked at
+        return plan.as_dict(), path_summary(plan)
+
     def _plan_or_direct(self, total, chunk, rs, profile, mode, direction) -> PlannerTransferPlan:
-        try:
-            if rs is not None:
-                return self._planner.plan_ranges(rs, chunk, profile, mode, direction=direction)
-            return self._planner.plan(total, chunk, profile, mode, direction=direction)
-        except RuntimeError:
-            return self._direct_plan(total, chunk, rs, profile, direction)
+        def make():
+            try:
+                if rs is not None:
+                    return self._planner.plan_ranges(rs, chunk, profile, mode, direction=direction)
+                return self._planner.plan(total, chunk, profile, mode, direction=direction)
+            except RuntimeError:
+                return self._direct_plan(total, chunk, rs, profile, direction)
+
+        return self._cached(_plan_key("plan", total, chunk, rs, profile, mode, direction), make)
 
     def _direct_plan(self, total, chunk, rs, profile: ProfileView, direction) -> PlannerTransferPlan:
         prof = ProfileView(profile.target_device, profile.direct_h2d_bw_gbps or 1.0,
                            profile.direct_d2h_bw_gbps or profile.direct_h2d_bw_gbps or 1.0, ())
-        if rs is not None:
-            return self._planner.plan_ranges(rs, chunk, prof, TransferMode.DIRECT, direction=direction)
-        return self._planner.plan(total, chunk, prof, TransferMode.DIRECT, direction=direction)
+
+        def make():
+            if rs is not None:
+                return self._planner.plan_ranges(rs, chunk, prof, TransferMode.DIRECT, direction=direction)
+            return self._planner.plan(total, chunk, prof, TransferMode.DIRECT, direction=direction)
+
+        return self._cached(_plan_key("direct", total, chunk, rs, prof, TransferMode.DIRECT, direction), make)
 
     def _leases(self, plan: PlannerTransferPlan, session: Session, quotas, direction, now, job_id,
                 defer) -> tuple[tuple[PlannerLease, ...], str | None]:
@@ -225,6 +270,17 @@ def resolved_mode(plan: PlannerTransferPlan) -> TransferMode:
     if {"direct", "relay"} <= kinds:
         return TransferMode.POOL
     return TransferMode.RELAY if "relay" in kinds else TransferMode.DIRECT
+
+
+def _plan_key(tag: str, total, chunk, rs, profile: ProfileView, mode, direction) -> tuple:
+    conc = (profile.concurrent or {}).get(direction) if profile.concurrent else None
+    ck = None
+    if isinstance(conc, Mapping):
+        ck = (tuple(int(x) for x in conc.get("lanes") or ()),
+              tuple(sorted((str(k), float(v)) for k, v in (conc.get("lane_gibps") or {}).items())))
+    ranges = None if rs is None else tuple((r["src_offset"], r["dst_offset"], r["bytes"]) for r in rs)
+    return (tag, int(total), int(chunk), ranges, profile.target_device, profile.direct_h2d_bw_gbps,
+            profile.direct_d2h_bw_gbps, profile.relays, ck, str(getattr(mode, "value", mode)), direction)
 
 
 def plan_stats(plan: PlannerTransferPlan, *, requested_mode: TransferMode,
@@ -274,8 +330,19 @@ def profile_payload(entry: Mapping[str, object] | None) -> Mapping[str, object] 
 
 
 def scheduling_decision_leases(decision: SchedulingDecision) -> tuple[PlannerLease, ...]:
+    """The decision's leases as records; parsed once per decision (a
+    decision is immutable) and kept on it."""
     if not isinstance(decision, SchedulingDecision):
         raise TypeError("decision must be a SchedulingDecision")
+    cached = decision.__dict__.get("_parsed_leases")
+    if cached is not None:
+        return cached
+    out = _parse_leases(decision)
+    object.__setattr__(decision, "_parsed_leases", out)
+    return out
+
+
+def _parse_leases(decision: SchedulingDecision) -> tuple[PlannerLease, ...]:
     leases = decision.metadata.get("leases", ())
     if not isinstance(leases, (tuple, list)):
         raise ValueError("scheduling decision metadata leases must be a sequence")
