@@ -24,16 +24,42 @@ for files and tools that expect it.
 from __future__ import annotations
 
 from collections.abc import Mapping
-from dataclasses import asdict, dataclass, field
+from dataclasses import asdict, dataclass, field, fields
 
 from .schema import TransferMode
 
 DEFAULT_CHUNK_BYTES = 16 * 1024 * 1024
 
 
+_NAMES: dict[type, tuple[str, ...]] = {}
+
+
+def _plain(v):
+    """``dataclasses.asdict`` semantics for these records (nested records to
+    dicts, containers rebuilt), without its per-value generic dispatch."""
+    t = type(v)
+    if t in (int, float, str, bool) or v is None:
+        return v
+    if hasattr(t, "__dataclass_fields__"):
+        return _record_dict(v)
+    if t is tuple or t is list:
+        return t(_plain(x) for x in v)
+    if t is dict:
+        return {k: _plain(x) for k, x in v.items()}
+    return v
+
+
+def _record_dict(obj) -> dict[str, object]:
+    t = type(obj)
+    names = _NAMES.get(t)
+    if names is None:
+        names = _NAMES[t] = tuple(f.name for f in fields(t))
+    return {n: _plain(getattr(obj, n)) for n in names}
+
+
 class _AsDict:
     def as_dict(self) -> dict[str, object]:
-        return asdict(self)
+        return _record_dict(self)
 
 
 @dataclass(frozen=True)
