@@ -740,13 +740,10 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     kp.trace = s.trace ? reinterpret_cast<unsigned long long*>(dsc + o_trace) : nullptr;
     if (s.op == kOpAdamW) {
       const auto& a = s.adam;
-      const double bc1 = 1.0 - std::pow(static_cast<double>(a.beta1), a.step);
-      const double bc2 = 1.0 - std::pow(static_cast<double>(a.beta2), a.step);
       kp.grads = reinterpret_cast<const uint16_t*>(a.grads);
       kp.params_out = reinterpret_cast<uint16_t*>(a.params);
       kp.nparams = a.nparams;
-      kp.adam = AdamCoeffs{a.lr, a.beta1, a.beta2, a.eps, a.weight_decay, a.grad_scale,
-                           static_cast<float>(a.lr / bc1), static_cast<float>(1.0 / std::sqrt(bc2))};
+      kp.adam = AdamCoeffs::make(a.lr, a.beta1, a.beta2, a.eps, a.weight_decay, a.grad_scale, a.step);
     }
     // Launch before any copy-engine work is queued: if the launch fails no
     // relay stream is left waiting for a kernel that never runs.

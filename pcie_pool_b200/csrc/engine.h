@@ -73,12 +73,12 @@ struct AdamStepSpec {
   uint64_t grads = 0;    // bf16 gradients on the target, nparams elements
   uint64_t params = 0;   // bf16 parameters written on the target, nparams elements
   uint64_t nparams = 0;
-  float lr = 1e-3f;
-  float beta1 = 0.9f;
-  float beta2 = 0.999f;
-  float eps = 1e-8f;
-  float weight_decay = 0.0f;
-  float grad_scale = 1.0f;
+  double lr = 1e-3;      // scalars in double: the kernel's factors are formed from them
+  double beta1 = 0.9;
+  double beta2 = 0.999;
+  double eps = 1e-8;
+  double weight_decay = 0.0;
+  double grad_scale = 1.0;
   int step = 1;          // 1-based step count (bias correction)
 };
 

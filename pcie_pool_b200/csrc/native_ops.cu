@@ -9,6 +9,7 @@
 #include "device_utils.cuh"
 #include "native_ops.h"
 #include "adamw.cuh"
+#include "fp8_e4m3.cuh"
 
 namespace ppb {
 namespace {
@@ -30,22 +31,42 @@ int sm_count() {
 __global__ void __launch_bounds__(kThreads) fp8_quant_kernel(const __nv_bfloat16* __restrict__ src,
                                                              uint64_t rows, uint64_t cols,
                                                              uint8_t* __restrict__ q,
-                                                             float* __restrict__ scales) {
+                                                             float* __restrict__ scales, bool vec) {
+  // one CTA per 128x128 block; thread t holds 64 elements of row t/2 (the
+  // block's left or right half).  ``vec``: cols % 16 == 0 and both tensors
+  // 16-byte aligned, so a half row is eight 16-byte loads and four 16-byte
+  // stores.
   __shared__ float red[kThreads / 32];
   const uint64_t ncb = (cols + 127) / 128;
   const uint64_t rb = blockIdx.x / ncb;
   const uint64_t cb = blockIdx.x - rb * ncb;
   const uint64_t r = rb * 128 + (threadIdx.x >> 1);
   const uint64_t c0 = cb * 128 + (threadIdx.x & 1) * 64;
+  const bool full = vec && r < rows && c0 + 64 <= cols;
   float vals[64];
   float amax = 0.f;
+  if (full) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src + r * cols + c0);
 #pragma unroll
-  for (int i = 0; i < 64; ++i) {
-    const uint64_t c = c0 + i;
-    const float x = (r < rows && c < cols) ? __bfloat162float(src[r * cols + c]) : 0.f;
-    vals[i] = x;
-    amax = fmaxf(amax, fabsf(x));
+    for (int i = 0; i < 8; ++i) {
+      const uint4 w = __ldcs(s4 + i);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        vals[8 * i + 2 * e] = f.x;
+        vals[8 * i + 2 * e + 1] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const uint64_t c = c0 + i;
+      vals[i] = (r < rows && c < cols) ? __bfloat162float(src[r * cols + c]) : 0.f;
+    }
   }
+#pragma unroll
+  for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(vals[i]));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
@@ -53,12 +74,25 @@ __global__ void __launch_bounds__(kThreads) fp8_quant_kernel(const __nv_bfloat16
   float bmax = 0.f;
   for (int w = 0; w < kThreads / 32; ++w) bmax = fmaxf(bmax, red[w]);
   const float scale = bmax > 0.f ? __fdiv_rn(bmax, 448.0f) : 1.0f;
-  if (r < rows) {
+  const float rcp = __frcp_rn(scale);
+  const bool exact_only = isinf(rcp);
+  if (full) {
+    uint4* q4 = reinterpret_cast<uint4*>(q + r * cols + c0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int e = 16 * i + 4 * k;
+        w[k] = e4m3x2_quotient(vals[e], vals[e + 1], scale, rcp, exact_only) |
+               (e4m3x2_quotient(vals[e + 2], vals[e + 3], scale, rcp, exact_only) << 16);
+      }
+      q4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else if (r < rows) {
 #pragma unroll
     for (int i = 0; i < 64; i += 2) {
-      const __nv_fp8x2_storage_t pair = __nv_cvt_float2_to_fp8x2(
-          make_float2(__fdiv_rn(vals[i], scale), __fdiv_rn(vals[i + 1], scale)), __NV_SATFINITE,
-          __NV_E4M3);
+      const uint32_t pair = e4m3x2_quotient(vals[i], vals[i + 1], scale, rcp, exact_only);
       const uint64_t c = c0 + i;
       if (c < cols) q[r * cols + c] = static_cast<uint8_t>(pair & 0xff);
       if (c + 1 < cols) q[r * cols + c + 1] = static_cast<uint8_t>(pair >> 8);
@@ -133,10 +167,7 @@ __global__ void __launch_bounds__(kThreads) adamw_kernel(float* __restrict__ mas
                                                          float* __restrict__ v,
                                                          const __nv_bfloat16* __restrict__ g,
                                                          __nv_bfloat16* __restrict__ out, uint64_t n,
-                                                         float lr, float b1, float b2, float eps,
-                                                         float wd, float gscale, float step_size,
-                                                         float inv_sqrt_bc2) {
-  const AdamCoeffs c{lr, b1, b2, eps, wd, gscale, step_size, inv_sqrt_bc2};
+                                                         const AdamCoeffs c) {
   const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
   for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n; i += stride) {
     float mi = m[i], vi = v[i];
@@ -194,8 +225,10 @@ cudaError_t fp8_block_quant(const void* src, uint64_t rows, uint64_t cols, void*
   if (rows == 0 || cols == 0) return cudaSuccess;
   const uint64_t blocks = ((rows + 127) / 128) * ((cols + 127) / 128);
   if (blocks > 0x7fffffffull) return cudaErrorInvalidValue;
+  const bool vec = cols % 16 == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(q) & 15u) == 0;
   fp8_quant_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(src), rows, cols, static_cast<uint8_t*>(q), scales);
+      static_cast<const __nv_bfloat16*>(src), rows, cols, static_cast<uint8_t*>(q), scales, vec);
   return cudaGetLastError();
 }
 
@@ -243,13 +276,9 @@ cudaError_t fused_adamw(float* master, float* m, float* v, const void* grad, voi
                         uint64_t n, const AdamParams& a, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   if (a.step < 1) return cudaErrorInvalidValue;
-  const double bc1 = 1.0 - std::pow(static_cast<double>(a.beta1), a.step);
-  const double bc2 = 1.0 - std::pow(static_cast<double>(a.beta2), a.step);
-  const float step_size = static_cast<float>(a.lr / bc1);
-  const float inv_sqrt_bc2 = static_cast<float>(1.0 / std::sqrt(bc2));
   adamw_kernel<<<grid_for(n, kThreads * 4), kThreads, 0, stream>>>(
       master, m, v, static_cast<const __nv_bfloat16*>(grad), static_cast<__nv_bfloat16*>(param_out),
-      n, a.lr, a.beta1, a.beta2, a.eps, a.weight_decay, a.grad_scale, step_size, inv_sqrt_bc2);
+      n, AdamCoeffs::make(a.lr, a.beta1, a.beta2, a.eps, a.weight_decay, a.grad_scale, a.step));
   return cudaGetLastError();
 }
 

@@ -18,12 +18,12 @@
 namespace ppb {
 
 struct AdamParams {
-  float lr = 1e-3f;
-  float beta1 = 0.9f;
-  float beta2 = 0.999f;
-  float eps = 1e-8f;
-  float weight_decay = 0.0f;
-  float grad_scale = 1.0f;  // multiplies the incoming gradient
+  double lr = 1e-3;
+  double beta1 = 0.9;
+  double beta2 = 0.999;
+  double eps = 1e-8;
+  double weight_decay = 0.0;
+  double grad_scale = 1.0;  // multiplies the incoming gradient
   int step = 1;
 };
 

@@ -17,6 +17,7 @@
 #include <cuda_fp8.h>
 
 #include "device_utils.cuh"
+#include "fp8_e4m3.cuh"
 #include "pool_kernels.h"
 
 namespace ppb {
@@ -293,7 +294,9 @@ __device__ bool move_contiguous(const uint8_t* src, uint8_t* dst, uint32_t bytes
 // ---- bf16 -> fp8 e4m3 with one fp32 scale per 128x128 block ------------------
 // scale = amax / 448 (IEEE division, 1.0 for an all-zero block); q = e4m3(x /
 // scale) with round-to-nearest-even and saturation to +-448 (the hardware
-// cvt.rn.satfinite.e4m3x2.f32 conversion).  256 threads cover one block: two
+// cvt.rn.satfinite.e4m3x2.f32 conversion), the quotient taken as if rounded
+// to fp32 (fp8_e4m3.cuh: estimate by the reciprocal, divide only near a
+// rounding boundary).  256 threads cover one block: two
 // threads per row, 64 columns (128 bytes) each.
 __device__ bool land_fp8_chunk(const LaneKernelParams& p, const ChunkDesc& c,
                                const uint8_t* src, uint32_t j, uint32_t G, bool do_csum,
@@ -338,6 +341,8 @@ __device__ bool land_fp8_chunk(const LaneKernelParams& p, const ChunkDesc& c,
     for (int w = 0; w < kLaneThreads / 32; ++w) bmax = fmaxf(bmax, red[w]);
     __syncthreads();
     const float scale = bmax > 0.f ? __fdiv_rn(bmax, 448.0f) : 1.0f;
+    const float rcp = __frcp_rn(scale);
+    const bool exact_only = isinf(rcp);
     if (valid) {
       uint32_t packed[16];
 #pragma unroll
@@ -347,13 +352,9 @@ __device__ bool land_fp8_chunk(const LaneKernelParams& p, const ChunkDesc& c,
         for (int e = 0; e < 4; e += 2) {
           const float2 f0 = __bfloat1622float2(h[e]);
           const float2 f1 = __bfloat1622float2(h[e + 1]);
-          const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
-              make_float2(__fdiv_rn(f0.x, scale), __fdiv_rn(f0.y, scale)), __NV_SATFINITE,
-              __NV_E4M3);
-          const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
-              make_float2(__fdiv_rn(f1.x, scale), __fdiv_rn(f1.y, scale)), __NV_SATFINITE,
-              __NV_E4M3);
-          packed[i * 2 + e / 2] = uint32_t(lo) | (uint32_t(hi) << 16);
+          const uint32_t lo = e4m3x2_quotient(f0.x, f0.y, scale, rcp, exact_only);
+          const uint32_t hi = e4m3x2_quotient(f1.x, f1.y, scale, rcp, exact_only);
+          packed[i * 2 + e / 2] = lo | (hi << 16);
         }
       }
       uint8_t* qrow = T.q + uint64_t(row0 + row_local) * C + uint64_t(cb) * 128u + half * 64u;

@@ -229,10 +229,14 @@ class _MockLanding:
 
         a = self.spec.adam_params
         f32 = np.float32
-        lr, b1, b2, eps, wd, gs = (f32(a[k]) for k in ("lr", "beta1", "beta2", "eps", "weight_decay", "grad_scale"))
+        lr, b1, b2, eps, wd, gs = (float(a[k]) for k in ("lr", "beta1", "beta2", "eps", "weight_decay",
+                                                          "grad_scale"))
         t = int(a["step"])
-        step_size = f32(float(a["lr"]) / (1.0 - float(a["beta1"]) ** t))
-        inv_sqrt_bc2 = f32(1.0 / np.sqrt(1.0 - float(a["beta2"]) ** t))
+        # factors formed in double and rounded once, as the kernel's host side does
+        decay, fb2, omb1, omb2 = f32(1.0 - lr * wd), f32(b2), f32(1.0 - b1), f32(1.0 - b2)
+        step_size = f32(lr / (1.0 - b1 ** t))
+        sqrt_bc2 = f32(np.sqrt(1.0 - b2 ** t))
+        eps, gs = f32(eps), f32(gs)
         nparams = int(a["nparams"])
         tiles = n // ADAM_TILE_BYTES
         st = np.ctypeslib.as_array((ctypes.c_float * (n // 4)).from_address(hbase + so)).reshape(tiles, 3,
@@ -243,10 +247,10 @@ class _MockLanding:
         g = (graw.astype(np.uint32) << 16).view(np.float32) * gs
         flat = st.transpose(1, 0, 2).reshape(3, -1)[:, :cnt].copy()
         mast, m, v = flat
-        p = mast * (f32(1.0) - lr * wd)
-        m = b1 * m + (f32(1.0) - b1) * g
-        v = b2 * v + (f32(1.0) - b2) * g * g
-        p = p - step_size * (m / (np.sqrt(v) * inv_sqrt_bc2 + eps))
+        p = mast * decay
+        m = m + omb1 * (g - m)
+        v = v * fb2 + (g * g) * omb2
+        p = p - step_size * (m / (np.sqrt(v) / sqrt_bc2 + eps))
         full = st.transpose(1, 0, 2).reshape(3, -1).copy()
         full[0, :cnt], full[1, :cnt], full[2, :cnt] = p, m, v
         st[:] = full.reshape(3, tiles, ADAM_TILE_PARAMS).transpose(1, 0, 2)

@@ -82,3 +82,25 @@ def block_dequant(q: np.ndarray, scales: np.ndarray, block: int = 128) -> np.nda
     R, C = q.shape
     s = np.repeat(np.repeat(scales, block, axis=0), block, axis=1)[:R, :C]
     return (e4m3_decode(q) * s).astype(np.float32)
+
+
+def e4m3_quotient_estimated(x, scale) -> tuple[np.ndarray, np.ndarray]:
+    """The device quantizer's method for ``e4m3(x / scale)``, restated on the
+    host (csrc/fp8_e4m3.cuh): estimate q = x * fp32(1/scale), bracket |q| by
+    the floats 8 steps below and above it, and divide exactly only where the
+    bracket's ends convert to different codes.  Returns (codes, mask of the
+    elements that took the exact division)."""
+    x = np.asarray(x, dtype=np.float32)
+    s = np.float32(scale)
+    r = np.float32(1.0) / s
+    with np.errstate(over="ignore", invalid="ignore"):
+        q = (x * r).astype(np.float32)
+    bits = q.view(np.uint32)
+    a = bits & np.uint32(0x7FFFFFFF)
+    lo = np.where(a > 8, a - np.uint32(8), np.uint32(0)).astype(np.uint32).view(np.float32)
+    hi = (a + np.uint32(8)).astype(np.uint32).view(np.float32)
+    clo, chi = e4m3_encode(lo), e4m3_encode(hi)
+    exact = (clo != chi) | (not np.isfinite(r))
+    mag = np.where(exact, e4m3_encode(np.abs(x) / s) & 0x7F, clo & 0x7F).astype(np.uint8)
+    sign = ((bits >> 24) & 0x80).astype(np.uint8)
+    return mag | sign, exact
