@@ -298,6 +298,17 @@ __device__ bool move_contiguous(const uint8_t* src, uint8_t* dst, uint32_t bytes
 // to fp32 (fp8_e4m3.cuh: estimate by the reciprocal, divide only near a
 // rounding boundary).  256 threads cover one block: two
 // threads per row, 64 columns (128 bytes) each.
+__device__ __forceinline__ void fp8_load_half_row(uint4 (&v)[8], const uint8_t* p) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = ld_cg_v4(p + 16u * i);
+}
+
+// red: 2 x (kLaneThreads / 32) floats.  The block maximum goes through one of
+// two halves by block parity, so one barrier per block suffices: a half is
+// rewritten two blocks later, after a barrier that every reader has passed.
+// The next block's loads are issued before that barrier, so their latency
+// (HBM, or NVLink for a relay's ring) overlaps the reduction and the
+// quantization of the current block.
 __device__ bool land_fp8_chunk(const LaneKernelParams& p, const ChunkDesc& c,
                                const uint8_t* src, uint32_t j, uint32_t G, bool do_csum,
                                Csum& cs, float* red) {
@@ -311,17 +322,22 @@ __device__ bool land_fp8_chunk(const LaneKernelParams& p, const ChunkDesc& c,
   const uint32_t nblocks = nrb * ncb;
   const uint32_t r = threadIdx.x >> 1;
   const uint32_t half = threadIdx.x & 1u;
-  for (uint32_t b = j; b < nblocks; b += G) {
+  auto row_of = [&](uint32_t b) { return (b / ncb) * 128u + r; };
+  auto offset_of = [&](uint32_t b) {
+    const uint32_t rb = b / ncb;
+    return uint64_t(rb * 128u + r) * row_bytes + (uint64_t(b - rb * ncb) * 128u + half * 64u) * 2u;
+  };
+  uint4 v[8];
+  if (j < nblocks && row_of(j) < nrows) fp8_load_half_row(v, src + offset_of(j));
+  uint32_t parity = 0;
+  for (uint32_t b = j; b < nblocks; b += G, parity ^= 1u) {
     const uint32_t rb = b / ncb;
     const uint32_t cb = b - rb * ncb;
     const uint32_t row_local = rb * 128u + r;
     const bool valid = row_local < nrows;
-    const uint64_t byte_off = uint64_t(row_local) * row_bytes + (uint64_t(cb) * 128u + half * 64u) * 2u;
-    uint4 v[8];
+    const uint64_t byte_off = offset_of(b);
     float amax = 0.f;
     if (valid) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = ld_cg_v4(src + byte_off + 16u * i);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         if (do_csum) csum_vec(cs, v[i], (byte_off >> 2) + 4u * i);
@@ -335,11 +351,16 @@ __device__ bool land_fp8_chunk(const LaneKernelParams& p, const ChunkDesc& c,
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    float* rd = red + parity * (kLaneThreads / 32);
+    if ((threadIdx.x & 31) == 0) rd[threadIdx.x >> 5] = amax;
+    uint4 nv[8];
+    const uint32_t nb = b + G;
+    const bool nvalid = nb < nblocks && row_of(nb) < nrows;
+    if (nvalid) fp8_load_half_row(nv, src + offset_of(nb));
     __syncthreads();
     float bmax = 0.f;
-    for (int w = 0; w < kLaneThreads / 32; ++w) bmax = fmaxf(bmax, red[w]);
-    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < kLaneThreads / 32; ++w) bmax = fmaxf(bmax, rd[w]);
     const float scale = bmax > 0.f ? __fdiv_rn(bmax, 448.0f) : 1.0f;
     const float rcp = __frcp_rn(scale);
     const bool exact_only = isinf(rcp);
@@ -364,7 +385,14 @@ __device__ bool land_fp8_chunk(const LaneKernelParams& p, const ChunkDesc& c,
         qo[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
     }
     if (threadIdx.x == 0) T.scales[uint64_t(row0 / 128u + rb) * ncb + cb] = scale;
+    if (nvalid) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = nv[i];
+    }
   }
+  // the next chunk's first block reuses the halves from parity 0: wait until
+  // every thread has read this chunk's last maximum
+  __syncthreads();
   return true;
 }
 
@@ -374,7 +402,7 @@ __global__ void __launch_bounds__(kLaneThreads, 1) land_kernel(const LaneKernelP
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(kStages) * kTileBytes);
   __shared__ unsigned long long red[2 * (kLaneThreads / 32)];
-  __shared__ float fred[kLaneThreads / 32];
+  __shared__ float fred[2 * (kLaneThreads / 32)];
   __shared__ int s_ok;
 
   LaneDesc L;
