@@ -89,3 +89,33 @@ def test_feedback_is_kept_per_landing_op():
     d._observe_lanes({"landing_op": "copy", "failover": {"failed_lane_device": 1}, "path_stats": [
         {"direction": "h2d", "target_device": 0, "relay_device": -1, "cuda_ms": 10.0, "gib_per_second": 10.0}]})
     assert d._feedback.rates(0, "h2d:copy") == {}
+
+
+def test_plan_cache_reuses_plans_only_for_the_same_shape_and_profile():
+    from pcie_pool_b200.e2e import nominal_profile
+    from pcie_pool_b200.schema import RelayQuota, Session
+    from pcie_pool_b200.scheduler import DaemonScheduler
+
+    sch = DaemonScheduler()
+    sess = Session(session_id="s", target_gpu=0, relay_gpus=[1, 2, 3], max_inflight_chunks=1 << 16)
+    quotas = {g: RelayQuota(relay_gpu=g, max_sessions=4, max_inflight_chunks=1 << 16) for g in (1, 2, 3)}
+
+    def plan(total=N, profile=None, ranges=None, direction="h2d"):
+        prof = profile or {"profile": nominal_profile(0, [1, 2, 3])}
+        before = sch.plan_cache_hits
+        d = sch.plan_transfer(session=sess, profile_entry=prof, relay_quotas=quotas, total_bytes=total,
+                              chunk_bytes=4 * MiB, ranges=ranges, direction=direction)
+        return d.plan, sch.plan_cache_hits - before
+
+    a, miss = plan()
+    b, hit = plan()
+    assert (miss, hit) == (0, 1) and a == b  # same shape, same profile: the issued plan is reused
+    assert len({x["path"]["relay_device"] for x in a["assignments"]}) == 4  # direct + 3 relays
+    assert plan(total=N // 2)[1] == 0
+    assert plan(direction="d2h")[1] == 0
+    assert plan(ranges=({"src_offset": 4096, "dst_offset": 0, "bytes": N},))[1] == 0
+    assert plan(profile={"profile": nominal_profile(0, [1, 2, 3], lane_gibps=20.0)})[1] == 0
+    # the reused plan is what a fresh planner gives
+    fresh = DaemonScheduler().plan_transfer(session=sess, profile_entry={"profile": nominal_profile(0, [1, 2, 3])},
+                                            relay_quotas=quotas, total_bytes=N, chunk_bytes=4 * MiB)
+    assert fresh.plan == a
