@@ -772,25 +772,26 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
     PPB_CUDA(cudaEventRecord(P.kern_done, tkern));
   };
 
-  if (!kernel_after_copies) launch_kernel();
-  if (s.serialize && !h2d && P.has_kernel) {
-    for (auto& R : P.lanes) {
-      DeviceGuard lg(R.device);
-      PPB_CUDA(cudaStreamWaitEvent(R.stream, P.kern_done, 0));
-    }
-  }
-
   // ---- copy-engine side, chunks interleaved round-robin across lanes ------------
-  NvtxScope enqueue("copy-engine enqueue: " + std::to_string(s.lanes.size()) + " lanes", 0xFFF39C12u);
   const uint8_t* host = reinterpret_cast<const uint8_t*>(s.host_ptr);
   uint8_t* devp = reinterpret_cast<uint8_t*>(s.dev_ptr);
   std::vector<size_t> next(s.lanes.size(), 0);
+  std::vector<uint64_t> left(s.lanes.size(), 0);
+  for (size_t li = 0; li < s.lanes.size(); ++li)
+    for (const auto& c : s.lanes[li].chunks) left[li] += c.bytes;
+  // Lanes whose copies depend on nothing (a direct lane copying straight to
+  // or from its final place) are queued first, so their copy engine starts
+  // while the kernel's descriptors are still being prepared; a failed kernel
+  // launch leaves them nothing to wait for.
+  const bool direct_first = !s.serialize;
+  auto enqueue = [&](bool unstaged_only) {
   bool any = true;
   while (any) {
     any = false;
     for (size_t li = 0; li < s.lanes.size(); ++li) {
       const auto& L = s.lanes[li];
       auto& R = P.lanes[li];
+      if (unstaged_only && R.staged) continue;
       const size_t k = next[li];
       if (k >= L.chunks.size()) continue;
       any = true;
@@ -799,20 +800,26 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
       DeviceGuard lg(R.device);
       if (!R.staged) {
         // Plain direct lane: merge chunks that are contiguous on both sides
-        // into one copy-engine transfer (up to coalesce_bytes) and publish
-        // the last chunk's sequence number once for the whole group.
+        // into one copy-engine transfer and publish the last chunk's
+        // sequence number once for the group.  A group takes at most half of
+        // the lane's remaining bytes (and at most coalesce_bytes), so the
+        // groups shrink towards the end: the kernel's in-place checksum of a
+        // group overlaps the copy of the next, and what is left after the
+        // last copy is one chunk's checksum.
+        const uint64_t cap = std::min<uint64_t>(options_.coalesce_bytes, std::max<uint64_t>(c.bytes, left[li] / 2));
         size_t end = k + 1;
         uint64_t run = c.bytes;
         while (end < L.chunks.size()) {
           const auto& nx = L.chunks[end];
           const auto& pv = L.chunks[end - 1];
           if (nx.src_off != pv.src_off + pv.bytes || nx.dst_off != pv.dst_off + pv.bytes ||
-              run + nx.bytes > options_.coalesce_bytes)
+              run + nx.bytes > cap)
             break;
           run += nx.bytes;
           ++end;
         }
         next[li] = end;
+        left[li] -= run;
         const uint32_t last_seq = R.ring ? static_cast<uint32_t>(R.seq0 + end) : 0u;
         const bool pub = static_cast<int>(li) != s.debug_drop_publish;
         if (h2d) {
@@ -854,6 +861,23 @@ uint64_t PoolEngine::submit(const TransferSpec& s) {
         }
       }
     }
+  }
+
+  };
+  {
+    NvtxScope enqueue_scope("copy-engine enqueue: " + std::to_string(s.lanes.size()) + " lanes", 0xFFF39C12u);
+    if (direct_first) enqueue(true);
+  }
+  if (!kernel_after_copies) launch_kernel();
+  if (s.serialize && !h2d && P.has_kernel) {
+    for (auto& R : P.lanes) {
+      DeviceGuard lg(R.device);
+      PPB_CUDA(cudaStreamWaitEvent(R.stream, P.kern_done, 0));
+    }
+  }
+  {
+    NvtxScope enqueue_scope("copy-engine enqueue: " + std::to_string(s.lanes.size()) + " lanes", 0xFFF39C12u);
+    enqueue(false);
   }
 
   for (auto& R : P.lanes) {

@@ -36,21 +36,30 @@ __device__ __forceinline__ uint32_t e4m3x2_code(float a, float b) {
   return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
 }
 
+// The rare exact path, kept out of line so the unrolled hot loops that call
+// e4m3x2_quotient stay small (inlined divisions filled the instruction cache).
+static __device__ __noinline__ uint32_t e4m3x2_settle(uint32_t mag, uint32_t diff, float x0, float x1, float s) {
+  if (diff & 0x00ffu) mag = (mag & 0xff00u) | (e4m3x2_code(__fdiv_rn(fabsf(x0), s), 0.f) & 0x00ffu);
+  if (diff & 0xff00u) mag = (mag & 0x00ffu) | (e4m3x2_code(0.f, __fdiv_rn(fabsf(x1), s)) & 0xff00u);
+  return mag;
+}
+
+static __device__ __noinline__ uint32_t e4m3x2_divide(float x0, float x1, float s) {
+  return e4m3x2_code(__fdiv_rn(x0, s), __fdiv_rn(x1, s));
+}
+
 // Two e4m3 codes (x0 in the low byte) of x0 / s and x1 / s; r = __frcp_rn(s).
 __device__ __forceinline__ uint32_t e4m3x2_quotient(float x0, float x1, float s, float r, bool exact_only) {
-  if (exact_only) return e4m3x2_code(__fdiv_rn(x0, s), __fdiv_rn(x1, s));
+  if (exact_only) return e4m3x2_divide(x0, x1, s);
   const float q0 = __fmul_rn(x0, r);
   const float q1 = __fmul_rn(x1, r);
   const uint32_t b0 = __float_as_uint(q0), b1 = __float_as_uint(q1);
   const uint32_t a0 = b0 & 0x7fffffffu, a1 = b1 & 0x7fffffffu;
   const uint32_t lo = e4m3x2_code(__uint_as_float(a0 > 8u ? a0 - 8u : 0u), __uint_as_float(a1 > 8u ? a1 - 8u : 0u));
   const uint32_t hi = e4m3x2_code(__uint_as_float(a0 + 8u), __uint_as_float(a1 + 8u));
-  uint32_t mag = lo;
   const uint32_t diff = lo ^ hi;
-  if (diff) {  // rare: an estimate within 8 ulps of a rounding boundary
-    if (diff & 0x00ffu) mag = (mag & 0xff00u) | (e4m3x2_code(__fdiv_rn(fabsf(x0), s), 0.f) & 0x00ffu);
-    if (diff & 0xff00u) mag = (mag & 0x00ffu) | (e4m3x2_code(0.f, __fdiv_rn(fabsf(x1), s)) & 0xff00u);
-  }
+  // rare: an estimate within 8 ulps of a rounding boundary
+  const uint32_t mag = diff ? e4m3x2_settle(lo, diff, x0, x1, s) : lo;
   return mag | ((b0 >> 24) & 0x80u) | ((b1 >> 16) & 0x8000u);
 }
 

@@ -33,9 +33,9 @@ __global__ void __launch_bounds__(kThreads) fp8_quant_kernel(const __nv_bfloat16
                                                              uint8_t* __restrict__ q,
                                                              float* __restrict__ scales, bool vec) {
   // one CTA per 128x128 block; thread t holds 64 elements of row t/2 (the
-  // block's left or right half).  ``vec``: cols % 16 == 0 and both tensors
-  // 16-byte aligned, so a half row is eight 16-byte loads and four 16-byte
-  // stores.
+  // block's left or right half) as raw bf16 pairs.  ``vec``: cols % 16 == 0
+  // and both tensors 16-byte aligned, so a half row is eight 16-byte loads
+  // and four 16-byte stores.
   __shared__ float red[kThreads / 32];
   const uint64_t ncb = (cols + 127) / 128;
   const uint64_t rb = blockIdx.x / ncb;
@@ -43,59 +43,59 @@ __global__ void __launch_bounds__(kThreads) fp8_quant_kernel(const __nv_bfloat16
   const uint64_t r = rb * 128 + (threadIdx.x >> 1);
   const uint64_t c0 = cb * 128 + (threadIdx.x & 1) * 64;
   const bool full = vec && r < rows && c0 + 64 <= cols;
-  float vals[64];
-  float amax = 0.f;
+  uint32_t w[32];  // bf16 pairs
   if (full) {
     const uint4* s4 = reinterpret_cast<const uint4*>(src + r * cols + c0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint4 w = __ldcs(s4 + i);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(h[e]);
-        vals[8 * i + 2 * e] = f.x;
-        vals[8 * i + 2 * e + 1] = f.y;
-      }
+      const uint4 t = __ldcs(s4 + i);
+      w[4 * i] = t.x;
+      w[4 * i + 1] = t.y;
+      w[4 * i + 2] = t.z;
+      w[4 * i + 3] = t.w;
     }
   } else {
+    const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const uint64_t c = c0 + i;
-      vals[i] = (r < rows && c < cols) ? __bfloat162float(src[r * cols + c]) : 0.f;
+    for (int i = 0; i < 32; ++i) {
+      const uint64_t c = c0 + 2 * i;
+      const uint32_t lo = (r < rows && c < cols) ? s16[r * cols + c] : 0u;
+      const uint32_t hi = (r < rows && c + 1 < cols) ? s16[r * cols + c + 1] : 0u;
+      w[i] = lo | (hi << 16);
     }
   }
+  float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(vals[i]));
+  for (int i = 0; i < 32; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   float bmax = 0.f;
-  for (int w = 0; w < kThreads / 32; ++w) bmax = fmaxf(bmax, red[w]);
+  for (int k = 0; k < kThreads / 32; ++k) bmax = fmaxf(bmax, red[k]);
   const float scale = bmax > 0.f ? __fdiv_rn(bmax, 448.0f) : 1.0f;
   const float rcp = __frcp_rn(scale);
   const bool exact_only = isinf(rcp);
+  uint32_t codes[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[2 * i]));
+    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[2 * i + 1]));
+    codes[i] = e4m3x2_quotient(f0.x, f0.y, scale, rcp, exact_only) |
+               (e4m3x2_quotient(f1.x, f1.y, scale, rcp, exact_only) << 16);
+  }
   if (full) {
     uint4* q4 = reinterpret_cast<uint4*>(q + r * cols + c0);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint32_t w[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int e = 16 * i + 4 * k;
-        w[k] = e4m3x2_quotient(vals[e], vals[e + 1], scale, rcp, exact_only) |
-               (e4m3x2_quotient(vals[e + 2], vals[e + 3], scale, rcp, exact_only) << 16);
-      }
-      q4[i] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
+    for (int i = 0; i < 4; ++i) q4[i] = make_uint4(codes[4 * i], codes[4 * i + 1], codes[4 * i + 2], codes[4 * i + 3]);
   } else if (r < rows) {
 #pragma unroll
-    for (int i = 0; i < 64; i += 2) {
-      const uint32_t pair = e4m3x2_quotient(vals[i], vals[i + 1], scale, rcp, exact_only);
+    for (int i = 0; i < 64; ++i) {
       const uint64_t c = c0 + i;
-      if (c < cols) q[r * cols + c] = static_cast<uint8_t>(pair & 0xff);
-      if (c + 1 < cols) q[r * cols + c + 1] = static_cast<uint8_t>(pair >> 8);
+      if (c < cols) q[r * cols + c] = static_cast<uint8_t>(codes[i / 4] >> (8 * (i % 4)));
     }
   }
   if (threadIdx.x == 0) scales[rb * ncb + cb] = scale;
