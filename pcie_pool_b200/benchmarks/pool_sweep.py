@@ -6,10 +6,13 @@
 Moves uniform-random bytes between a page-locked host buffer and GPU0 over
 the direct lane plus the first R relay GPUs (equal split, then the
 balancer's weights after two calibration transfers), for every size, chunk
-size and direction; each point is the median of ``--repeats`` CUDA-event
-timings and is verified byte-exactly (H2D: the per-chunk checksums of the
-landing kernels against the host checksum; D2H: the host buffer against the
-device buffer).  ``--solo`` adds one line per GPU with its own link alone
+size and direction; each point is the median of ``--repeats`` timings and is
+verified byte-exactly.  ``ms`` brackets the whole ``PoolEngine.run`` call with
+CUDA events on the caller's stream (the Python submit, the engine's work and
+the host noticing completion); ``engine_ms`` is the engine's own event pair
+around the transfer's device work.  Verification: H2D compares the per-chunk
+checksums of the landing kernels with the host checksum, D2H the host buffer
+with the device buffer.  ``--solo`` adds one line per GPU with its own link alone
 (the isolated-link roofline); the largest size with all lanes gives the
 concurrent aggregate.  One JSON line per point.
 """
@@ -81,7 +84,7 @@ def main(argv=None) -> int:
                         if r:
                             bal.observe(0, dname, res)
                             lanes = plan_lanes(n, chunk, devices, target=0, bw_gibps=bal.weights(0, dname, devices))
-                    ms = []
+                    ms, dev_ms = [], []
                     for _ in range(a.repeats):
                         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                         e0.record()
@@ -90,6 +93,7 @@ def main(argv=None) -> int:
                         e1.synchronize()
                         res.raise_for_status()
                         ms.append(e0.elapsed_time(e1))
+                        dev_ms.append(res.cuda_ms)
                     ok = None
                     if not a.no_verify:
                         if direction == H2D:
@@ -98,9 +102,13 @@ def main(argv=None) -> int:
                         else:
                             ok = bool(torch.equal(dev[:n].cpu(), torch.from_numpy(host.numpy()[:n])))
                     med = statistics.median(ms)
+                    dmed = statistics.median(dev_ms)
                     print(json.dumps({"direction": dname, "relays": r, "lanes": len(devices), "bytes": n,
                                       "chunk_bytes": chunk, "ms": round(med, 3),
-                                      "gb_per_s": round(n / 1e9 / (med / 1e3), 2), "verified": ok,
+                                      "gb_per_s": round(n / 1e9 / (med / 1e3), 2),
+                                      "engine_ms": round(dmed, 3),
+                                      "engine_gb_per_s": round(n / 1e9 / (dmed / 1e3), 2) if dmed > 0 else None,
+                                      "verified": ok,
                                       "lane_ms": [(l.device, round(l.cuda_ms, 2), l.bytes) for l in res.lanes]}),
                           flush=True)
         del eng
