@@ -1,8 +1,8 @@
 // Fused lane kernels for sm_100a (see pool_kernels.h for the protocol).
 //
 // Data path per CTA: a kStages-deep ring of kTileBytes shared-memory stages.
-// One elected thread issues 1-D TMA bulk copies (cp.async.bulk, never with
-// .multicast::cluster) from the source -- for landing that is the relay GPU's
+// One elected thread issues 1-D TMA bulk copies (cp.async.bulk, never the
+// cluster-multicast form) from the source -- for landing that is the relay GPU's
 // staging slot reached through the peer mapping over NVLink -- into shared
 // memory, tracked by per-stage mbarriers with complete_tx.  All threads fold
 // the tile into the chunk checksum straight from shared memory, then the
