@@ -609,15 +609,16 @@ class TurboBusDaemon:
         deadline = time.monotonic() + timeout
         with self._lock:
             while True:
-                try:
-                    receipt = self._receipt(iid)
-                except ValueError as exc:
-                    return fail(str(exc))
-                if receipt.state in TERMINAL_STATES or timeout_seconds is None:
-                    return ok(receipt=asdict(receipt))
+                # the receipt is built once, when it is answered; a wake-up
+                # before the transfer ends only looks at its state
+                tid = self._st.intent_transfer.get(iid)
+                st = self._st.statuses.get(tid) if tid is not None else None
                 left = deadline - time.monotonic()
-                if left <= 0:
-                    return ok(receipt=asdict(receipt))
+                if st is None or st.state in TERMINAL_STATES or timeout_seconds is None or left <= 0:
+                    try:
+                        return ok(receipt=asdict(self._receipt(iid)))
+                    except ValueError as exc:
+                        return fail(str(exc))
                 self._changed.wait(timeout=min(left, 0.5))
 
     # ---- leases -----------------------------------------------------------------------------
