@@ -45,8 +45,8 @@ def parse_args(argv=None):
                    help="largest merged copy-engine transfer on the direct lane (bytes)")
     p.add_argument("--direction", choices=["h2d", "d2h"], default="h2d")
     p.add_argument("--lane-order", choices=["spread", "index"], default="spread",
-                   help="ours: GPU0 plus N-1 relays spread over PCIe uplinks (socket, root complex, switch) "
-                        "among the visible GPUs, or simply GPUs 0..N-1")
+                   help="ours: GPU0 plus N-1 relays spread over measured contention groups and PCIe uplinks "
+                        "(socket, root complex, switch) among the visible GPUs, or simply GPUs 0..N-1")
     p.add_argument("--no-checksum", action="store_true", help="skip the fused per-chunk checksum")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-extra", action="store_true",
@@ -461,12 +461,66 @@ def run_reference(args, dist: Dist) -> dict:
     return out
 
 
+def _measured_lane_set(n: int) -> tuple[list[int], dict]:
+    """GPU0 plus n-1 relays among the visible GPUs: spread over contention
+    groups measured by a short engine-free copy probe
+    (``topology.uplink_probe``), then over the PCIe topology.  With every
+    visible GPU in the set the order is the topology's."""
+    import torch
+
+    from pcie_pool_b200.topology.cuda_nvml import cuda_lane_set
+    from pcie_pool_b200.topology.uplink_probe import contention_groups, probe_rates
+
+    visible = torch.cuda.device_count()
+    if n <= 1 or n >= visible:
+        return cuda_lane_set(n)
+    try:
+        rates = probe_rates(list(range(visible)))
+        groups = contention_groups(rates["solo"], rates["concurrent"])
+    except Exception as exc:  # noqa: BLE001 - a failed probe keeps the topology rule
+        lane_set, info = cuda_lane_set(n)
+        return lane_set, {**info, "probe": f"failed: {type(exc).__name__}: {exc}"}
+    lane_set, info = cuda_lane_set(n, groups=groups)
+    info["probe_gb_per_s"] = {k: {str(d): round(v, 2) for d, v in sorted(r.items())} for k, r in rates.items()}
+    return lane_set, info
+
+
+def choose_lane_set(n: int) -> tuple[list[int], dict]:
+    """The lane set, identical on every rank: the local rank 0 measures and
+    chooses before any process group exists and hands the choice to the other
+    ranks of this launch through a file named for the launcher's process and
+    port (every rank of one torchrun launch shares both); they wait for it
+    with a time limit."""
+    import tempfile
+    import time
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world <= 1:
+        return _measured_lane_set(n)
+    path = Path(tempfile.gettempdir()) / (f"ppb_lane_set_{os.getppid()}_"
+                                          f"{os.environ.get('MASTER_PORT', '0')}.json")
+    if int(os.environ.get("LOCAL_RANK", "0")) == 0:
+        try:
+            lane_set, info = _measured_lane_set(n)
+        except Exception as exc:  # noqa: BLE001 - every rank must still get a lane set
+            lane_set, info = list(range(n)), {"rule": "GPUs 0..N-1", "fallback": f"{type(exc).__name__}: {exc}"}
+        tmp = path.with_suffix(".tmp")
+        tmp.write_text(json.dumps({"lane_set": lane_set, "info": info}))
+        os.replace(tmp, path)
+        return lane_set, info
+    deadline = time.monotonic() + 300.0
+    while not path.exists():
+        if time.monotonic() > deadline:
+            raise RuntimeError(f"local rank 0 did not publish the lane set ({path}) within 300 s")
+        time.sleep(0.05)
+    d = json.loads(path.read_text())
+    return [int(x) for x in d["lane_set"]], d["info"]
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.impl == "ours" and args.lane_order == "spread":
-        from pcie_pool_b200.topology.cuda_nvml import cuda_lane_set
-
-        args.lane_set, args.lane_info = cuda_lane_set(args.gpus)
+        args.lane_set, args.lane_info = choose_lane_set(args.gpus)
     else:
         args.lane_set, args.lane_info = list(range(args.gpus)), {"rule": "GPUs 0..N-1"}
     dist = Dist(args.lane_set)
@@ -530,6 +584,12 @@ def main(argv=None) -> int:
         print(s, flush=True)
         if args.json_out:
             Path(args.json_out).write_text(s + "\n")
+    if dist.world > 1 and dist.local_rank == 0:
+        import tempfile
+
+        # every rank read the lane set before the process group formed
+        (Path(tempfile.gettempdir()) / (f"ppb_lane_set_{os.getppid()}_"
+                                        f"{os.environ.get('MASTER_PORT', '0')}.json")).unlink(missing_ok=True)
     dist.close()
     return 0
 

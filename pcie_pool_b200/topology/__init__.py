@@ -246,10 +246,12 @@ class StaticTopologyProvider(TopologyProvider):
 
 def spread_by_keys(target: int, pool: Iterable[int], count: int, keys_of) -> list[int]:
     """Greedy uplink spreading (see ``DaemonResourceInventory.spread_relays``)
-    over any device numbering: ``keys_of(dev)`` gives its (socket, root
-    complex, top switch) keys."""
+    over any device numbering: ``keys_of(dev)`` gives its sharing keys, most
+    significant first -- (socket, root complex, top switch), optionally led by
+    a measured contention group."""
     pool = list(pool)
-    load: list[dict[str, int]] = [{}, {}, {}]
+    levels = max([len(tuple(keys_of(int(target))))] + [len(tuple(keys_of(d))) for d in pool])
+    load: list[dict[str, int]] = [{} for _ in range(levels)]
 
     def add(dev: int) -> None:
         for lvl, key in enumerate(keys_of(dev)):

@@ -476,15 +476,20 @@ def _bdf(s: str | None) -> tuple[int, int, int] | None:
 
 
 def cuda_lane_set(n: int, target: int = 0, provider: "CudaNvmlTopologyProvider | None" = None,
-                  bus_ids: dict[int, tuple[int, int, int]] | None = None) -> tuple[list[int], dict]:
+                  bus_ids: dict[int, tuple[int, int, int]] | None = None,
+                  groups: dict[int, str] | None = None) -> tuple[list[int], dict]:
     """CUDA device indices of ``target`` plus ``n - 1`` relays among the
     visible GPUs, spread over PCIe uplinks (socket, root complex, switch)
     with the daemon's rule.  Topology comes from NVML and sysfs and CUDA
     indices are matched to it by PCI address, so no CUDA context is created
-    on any GPU.  Falls back to ``target, 0, 1, ...`` when discovery fails."""
+    on any GPU.  ``groups`` (CUDA index -> measured contention group,
+    ``uplink_probe.contention_groups``) leads the keys when given.  Falls
+    back to ``target, 0, 1, ...`` when discovery fails."""
     from . import spread_by_keys
 
-    info: dict = {"rule": "spread over socket, root complex, switch"}
+    groups = {int(k): v for k, v in (groups or {}).items()}
+    info: dict = {"rule": "spread over measured contention group, socket, root complex, switch" if groups
+                  else "spread over socket, root complex, switch"}
     if bus_ids is None:
         import torch
 
@@ -499,6 +504,9 @@ def cuda_lane_set(n: int, target: int = 0, provider: "CudaNvmlTopologyProvider |
     try:
         inv = (provider or CudaNvmlTopologyProvider()).snapshot()
     except Exception as exc:  # noqa: BLE001 - any discovery failure keeps the index order
+        if groups:  # the measurement alone still spreads the lanes
+            relays = spread_by_keys(int(target), cands, n - 1, lambda i: (groups.get(i),))
+            return [int(target), *relays], {**info, "groups": groups, "topology": f"unavailable: {exc}"}
         return fallback, {**info, "fallback": f"topology unavailable: {exc}"}
     nvml_of = {}
     by_bdf = {_bdf(g.pci_bus_id): g.device_id for g in inv.gpus}
@@ -509,10 +517,13 @@ def cuda_lane_set(n: int, target: int = 0, provider: "CudaNvmlTopologyProvider |
         return fallback, {**info, "fallback": "target GPU not found in the topology"}
 
     def keys(i: int):
-        return inv.uplink_keys(nvml_of[i]) if i in nvml_of else (None, None, None)
+        topo = inv.uplink_keys(nvml_of[i]) if i in nvml_of else (None, None, None)
+        return (groups.get(i), *topo) if groups else topo
 
     relays = spread_by_keys(int(target), [c for c in cands if c in nvml_of], n - 1, keys)
     if len(relays) < n - 1:
         relays += [c for c in cands if c not in relays][:n - 1 - len(relays)]
     info["uplinks"] = {str(i): list(keys(i)) for i in [int(target), *relays]}
+    if groups:
+        info["groups"] = {str(k): v for k, v in sorted(groups.items())}
     return [int(target), *relays], info

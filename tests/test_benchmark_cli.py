@@ -185,3 +185,33 @@ def test_multi_tenant_slow_transfers_never_wait_on_the_link_hold():
     for g in gpus:
         hp, hg, dp, dg = bufs[g]
         assert np.array_equal(dp, hp) and np.array_equal(hg, dg)
+
+
+def test_bench_lane_set_is_chosen_once_and_shared_by_every_rank(tmp_path):
+    """bench.py: local rank 0 measures and chooses the lane set before any
+    process group exists; the other ranks of the launch (same launcher
+    process, same port) read its choice.  Two ranks as child processes of
+    this test, the non-zero rank started first."""
+    import os
+    import subprocess
+    import sys
+    import time
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    code = ("import json, bench\n"
+            "bench._measured_lane_set = lambda n: ([0, 4, 1, 5][:n], {'rule': 'test'})\n"
+            "print(json.dumps(bench.choose_lane_set(4)))\n")
+    port = str(20000 + os.getpid() % 20000)
+    env = {**os.environ, "WORLD_SIZE": "2", "MASTER_PORT": port, "PYTHONPATH": str(root)}
+    r1 = subprocess.Popen([sys.executable, "-c", code], cwd=root, env={**env, "LOCAL_RANK": "1", "RANK": "1"},
+                          stdout=subprocess.PIPE, text=True)
+    time.sleep(1.0)
+    r0 = subprocess.run([sys.executable, "-c", code], cwd=root, env={**env, "LOCAL_RANK": "0", "RANK": "0"},
+                        stdout=subprocess.PIPE, text=True, timeout=120)
+    out1, _ = r1.communicate(timeout=120)
+    a, b = json.loads(r0.stdout.strip().splitlines()[-1]), json.loads(out1.strip().splitlines()[-1])
+    assert a == b == [[0, 4, 1, 5], {"rule": "test"}]
+    import tempfile
+
+    (Path(tempfile.gettempdir()) / f"ppb_lane_set_{os.getpid()}_{port}.json").unlink(missing_ok=True)

@@ -258,3 +258,55 @@ def test_daemon_recommends_relays_spread_over_uplinks():
     assert r.ok and r.payload["relay_discovery"]["recommended_relays"][:3] == [4, 1, 5]
     assert d.choose_relays(0, 3) == [4, 1, 5]
     assert d.choose_relays(0, 2, candidates=[1, 2, 3]) == [1, 2]
+
+
+def test_contention_groups_from_measured_rates():
+    """The rates of this pool's 8-GPU nodes: every link 55 GB/s alone, with
+    all eight busy GPUs 0-3 get ~19 GB/s and GPUs 4-7 ~32 GB/s."""
+    from pcie_pool_b200.topology.uplink_probe import contention_groups
+
+    solo = {d: 55.0 + 0.3 * d for d in range(8)}
+    conc = {d: (19.3 if d < 4 else 32.5) + 0.1 * d for d in range(8)}
+    g = contention_groups(solo, conc)
+    assert g[0] == g[1] == g[2] == g[3] != g[4] == g[5] == g[6] == g[7]
+    # one level of concurrent rates: no structure to spread over
+    assert contention_groups(solo, {d: 26.0 + 0.2 * d for d in range(8)}) == {}
+    # a GPU that is slow on its own has a slow link, not a shared one
+    assert contention_groups({**solo, 3: 30.0}, conc) == {}
+    assert contention_groups({0: 55.0}, {0: 20.0}) == {}
+
+
+def test_lane_set_spreads_over_measured_groups_before_topology():
+    """Each GPU has its own root port in the topology (as NVML reports on
+    these nodes); the measured groups still put the relays on the other
+    group first: 4 lanes into GPU0 are 0, 4, 1, 5 rather than 0..3."""
+    from pcie_pool_b200.topology import StaticTopologyProvider, synthetic_inventory
+    from pcie_pool_b200.topology.cuda_nvml import cuda_lane_set
+
+    from dataclasses import replace
+
+    inv = synthetic_inventory(8, gpus_per_root=1)
+    # as seen from the VM: one NUMA node, a root port per GPU
+    inv = replace(inv, gpus=tuple(replace(g, numa_node=0) for g in inv.gpus),
+                  pcie_paths=tuple(replace(p, numa_node=0) for p in inv.pcie_paths))
+    bus = {i: _bus_of(inv, i) for i in range(8)}
+    groups = {d: ("slow" if d < 4 else "fast") for d in range(8)}
+    lanes, info = cuda_lane_set(4, 0, provider=StaticTopologyProvider(inv), bus_ids=bus, groups=groups)
+    assert lanes == [0, 4, 1, 5] and info["groups"]["0"] == "slow"
+    assert cuda_lane_set(2, 0, provider=StaticTopologyProvider(inv), bus_ids=bus, groups=groups)[0] == [0, 4]
+    # without a measurement the topology sees nothing shared: index order
+    plain, info = cuda_lane_set(4, 0, provider=StaticTopologyProvider(inv), bus_ids=bus)
+    assert "groups" not in info and plain == [0, 1, 2, 3]
+
+    class Broken:
+        def snapshot(self):
+            raise RuntimeError("no NVML here")
+
+    lanes, info = cuda_lane_set(4, 0, provider=Broken(), bus_ids=bus, groups=groups)
+    assert lanes == [0, 4, 1, 5] and "unavailable" in info["topology"]
+
+
+def _bus_of(inv, i):
+    from pcie_pool_b200.topology.cuda_nvml import _bdf
+
+    return _bdf(next(g for g in inv.gpus if g.device_id == i).pci_bus_id)
