@@ -122,28 +122,33 @@ class EngineDataPlane:
             self._engine = PoolEngine(self._devices, **self._engine_kw)
         return self._engine
 
-    def _lanes(self, plan, target: int, cache: bool):
+    def _lanes(self, plan, target: int):
         """Engine lanes of a plan.  The scheduler reuses plan objects for a
-        repeated intent shape, so plain-copy lanes (which nothing annotates)
-        are kept per plan; the cache holds the plan's assignments so their
-        identity stays unique."""
-        from ..parallel.engine import lanes_from_plan
+        repeated intent shape, so each plan's chunk arrays are kept; every
+        call gets fresh ``Lane`` records over them (a fused op annotates its
+        lanes with per-chunk fields, which must not leak into the next
+        transfer).  The cache holds the plan's assignments so their identity
+        stays unique."""
+        from ..parallel.engine import Lane, lanes_from_plan
 
         asg = plan.get("assignments")
-        if not cache or asg is None:
+        if asg is None:
             return lanes_from_plan(plan, target)
         key = (id(asg), int(target))
         with self._lock:
             hit = self._lane_cache.get(key)
             if hit is not None and hit[0] is asg:
                 self._lane_cache.move_to_end(key)
-                return list(hit[1])
-        lanes = lanes_from_plan(plan, target)
-        with self._lock:
-            self._lane_cache[key] = (asg, tuple(lanes))
-            while len(self._lane_cache) > 64:
-                self._lane_cache.popitem(last=False)
-        return lanes
+                base = hit[1]
+            else:
+                base = None
+        if base is None:
+            base = tuple(lanes_from_plan(plan, target))
+            with self._lock:
+                self._lane_cache[key] = (asg, base)
+                while len(self._lane_cache) > 64:
+                    self._lane_cache.popitem(last=False)
+        return [Lane(l.device, l.src_off, l.dst_off, l.bytes) for l in base]
 
     # -- buffer resolution ------------------------------------------------------------------
     def host_pointer(self, buf: BufferRegistration) -> int:
@@ -205,7 +210,7 @@ class EngineDataPlane:
         dev_ptr = self.device_pointer(dev_buf)
         # fused landing op named by the intent (validated by the daemon)
         spec = LandingSpec.from_metadata(intent.metadata) if intent is not None else None
-        lanes = self._lanes(ticket.plan, target, cache=spec is None or spec.op == "copy")
+        lanes = self._lanes(ticket.plan, target)
         eng = self.engine
         direction = H2D if h2d else D2H
         op_kw: dict = {}

@@ -336,8 +336,8 @@ def unit_addresses(spec: LandingSpec, base_of) -> "Any":
     k = spec.kv
     ids = np.asarray(k.block_ids, dtype=np.uint64)
     # one row per (layer, lane) base address, one column per block: stream order
-    bases = np.array([int(base_of(bid)) + lane * k.lane_stride for bid in k.buffers for lane in range(k.lanes)],
-                     dtype=np.uint64)
+    per_buffer = np.array([int(base_of(bid)) for bid in k.buffers], dtype=np.uint64)
+    bases = (per_buffer[:, None] + np.arange(k.lanes, dtype=np.uint64)[None, :] * np.uint64(k.lane_stride)).ravel()
     return (bases[:, None] + ids[None, :] * np.uint64(k.block_stride)).ravel()
 
 
