@@ -9,6 +9,12 @@ dispatch to the executor thread, completion and the receipt.  The timing is
 repeated after ``--history`` earlier intents to show that the per-intent
 cost does not grow with the daemon's history.  Prints one JSON line.
 
+``--landing kv`` times a fused paged-KV restore intent instead
+(``DaemonKVOffloader.restore``: a Llama-3-8B-shape cache of 32 layers, a
+32k-token request = 131,072 units of 32 KiB through a permuted block table,
+``units_per_chunk`` 128); the cache and host tensors are allocated but never
+touched, so no memory is moved.
+
 ``--protocol daemon`` times the daemon protocol alone, the same way on this
 package's daemon and, with ``--impl reference``, on the unmodified reference
 daemon installed under ``baseline/_ref``: per intent ``submit_transfer_intent``
@@ -164,10 +170,14 @@ def main(argv=None) -> int:
                    help="client: TurboBusClient.transfer over an instant engine; daemon: bare daemon protocol")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours",
                    help="daemon implementation for --protocol daemon")
+    p.add_argument("--landing", choices=["copy", "kv"], default="copy",
+                   help="kv: fused paged-KV restore intents (Llama-3-8B shape, 32k tokens)")
     a = p.parse_args(argv)
     n, chunk = parse_size(a.bytes), parse_size(a.chunk)
     if a.protocol == "daemon":
         return _daemon_protocol(a, n, chunk)
+    if a.landing == "kv":
+        return _kv_intents(a)
     daemon, client, sid = build(a.lanes, n)
     counter = iter(range(1 << 40))
 
@@ -203,6 +213,42 @@ def main(argv=None) -> int:
                       "cpu_ms_per_intent": round(cpu_first, 3),
                       "ms_per_intent_after_history": round(later, 3), "history": a.history,
                       "retained_transfers": len(daemon.describe().payload["transfer_queue"])}), flush=True)
+    return 0
+
+
+def _kv_intents(a) -> int:
+    import numpy as np
+    import torch
+
+    from .. import TurboBusClient
+    from ..adapters.kv_offload import DaemonKVOffloader
+    from ..e2e import build_inprocess_node
+
+    layers, blocks, req_blocks = 32, 4096, 2048
+    kvs = [torch.empty(2, blocks, 16, 8, 128, dtype=torch.bfloat16) for _ in range(layers)]
+    devs = list(range(a.lanes))
+    daemon, dc = build_inprocess_node(InstantEngine(), devs, 0, profile_dict(a.lanes) if a.lanes > 1 else None)
+    sid = dc.register_session(0, devs[1:], max_inflight_chunks=1 << 20).payload["session"]["session_id"]
+    dc.register_job("kv", session_id=sid)
+    off = DaemonKVOffloader(TurboBusClient(daemon=dc), dc, session_id=sid, job_id="kv", kv_caches=kvs,
+                            units_per_chunk=128, sync_stream=False)
+    host = torch.empty(off.prefix_bytes(req_blocks), dtype=torch.uint8)
+    rng = np.random.default_rng(0)
+    tables = [[int(x) for x in rng.permutation(blocks)[:req_blocks]] for _ in range(4)]
+    for i in range(5):
+        off.restore(tables[i % 4], host)
+    wall, cpu = [], []
+    for _ in range(5):
+        t0, c0 = time.perf_counter(), time.process_time()
+        k = max(1, a.intents // 5)
+        for i in range(k):
+            off.restore(tables[i % 4], host)
+        wall.append((time.perf_counter() - t0) * 1e3 / k)
+        cpu.append((time.process_time() - c0) * 1e3 / k)
+    print(json.dumps({"metric": "control-plane ms per fused KV restore intent (instant data plane)",
+                      "lanes": a.lanes, "units_per_intent": off.units_per_block * req_blocks,
+                      "bytes_per_intent": off.prefix_bytes(req_blocks), "ms_per_intent": round(statistics.median(wall), 3),
+                      "cpu_ms_per_intent": round(statistics.median(cpu), 3)}), flush=True)
     return 0
 
 
