@@ -215,3 +215,32 @@ def test_bench_lane_set_is_chosen_once_and_shared_by_every_rank(tmp_path):
     import tempfile
 
     (Path(tempfile.gettempdir()) / f"ppb_lane_set_{os.getpid()}_{port}.json").unlink(missing_ok=True)
+
+
+def test_bench_child_runs_report_results_crashes_and_stalls(tmp_path, monkeypatch):
+    """bench.py runs the reference arm's extra figures in child processes:
+    a result comes back as its JSON, a crash as its exit code and last error
+    line, a stall past the limit as an error after the child's process
+    group is killed."""
+    import os
+    import sys
+    import time
+
+    pkg = tmp_path / "childmods"
+    pkg.mkdir()
+    (pkg / "__init__.py").write_text("")
+    (pkg / "ok.py").write_text(
+        "import json, sys\npath = sys.argv[sys.argv.index('--json-out') + 1]\n"
+        "open(path, 'w').write(json.dumps({'value': 1.5, 'unit': 's'}))\n")
+    (pkg / "crash.py").write_text("import sys\nprint('reference exploded', file=sys.stderr)\nsys.exit(3)\n")
+    (pkg / "stall.py").write_text("import time\ntime.sleep(120)\n")
+    monkeypatch.setenv("PYTHONPATH", os.pathsep.join([str(tmp_path), os.environ.get("PYTHONPATH", "")]))
+    sys.path.insert(0, str(__import__("pathlib").Path(__file__).resolve().parents[1]))
+    import bench
+
+    assert bench._child_json(["childmods.ok"], 60) == {"value": 1.5, "unit": "s"}
+    r = bench._child_json(["childmods.crash"], 60)
+    assert "exit code 3" in r["error"] and "exploded" in r["error"]
+    t0 = time.monotonic()
+    r = bench._child_json(["childmods.stall"], 2)
+    assert "no result within 2 s" in r["error"] and time.monotonic() - t0 < 30
