@@ -53,6 +53,9 @@ def parse_args(argv=None):
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--optimizer", choices=["none", "streamed-adamw"], default="none",
                    help="ours: run the AdamW step on the offload path instead of plain grads/params moves")
+    p.add_argument("--lend-across-groups", action="store_true",
+                   help="ours: measure each GPU's rate with every link busy (topology.uplink_probe) and let the "
+                        "daemon lend busy GPUs of a faster uplink group to tenants of a slower one")
     p.add_argument("--json-out", default="")
     return p.parse_args(argv)
 
@@ -193,6 +196,10 @@ def run_ours(a) -> dict:
                             topology_provider=prov,
                             executor=IntentExecutor(EngineDataPlane(engine=eng, checksum=True),
                                                     max_workers=4 * len(gpus)))
+    if getattr(a, "lend_across_groups", False):
+        from ..topology.uplink_probe import probe_rates
+
+        daemon.set_uplink_rates(probe_rates(gpus)["concurrent"])
     dc = InProcessDaemonClient(daemon)
     sessions = setup_tenants(daemon, dc, gpus, T.job_of, a.gpus_per_job, T.n,
                              {g: (T.host_params[g].ptr, T.host_grads[g].ptr, T.dev_params[g].data_ptr(),
@@ -430,6 +437,7 @@ def main(argv=None) -> int:
             "leaked_quota_chunks": res.get("leaked_quota_chunks"), "open_reservations": res.get("open_reservations"),
             "config": {"model": f"decoder-7b ({a.layers} layers) data-parallel x{a.gpus_per_job}",
                        "jobs": a.jobs, "gpus_per_job": a.gpus_per_job, "active_jobs": a.active_jobs or a.jobs,
+                       "lend_across_groups": bool(getattr(a, "lend_across_groups", False)),
                        "shard_bytes_per_gpu": res["shard_bytes"], "bytes_per_step": nbytes, "chunk_bytes": a.chunk,
                        "data": "synthetic bf16 (params N(0,0.02), grads N(0,1e-3)), seeded"}}
     emit(line, a.json_out)

@@ -127,7 +127,8 @@ class TurboBusDaemon:
                  scheduler: DaemonScheduler | None = None, executor=None,
                  profile_store_path: str | None = None,
                  clock: Callable[[], float] = time.time, link_hold_seconds: float = 1.0,
-                 history_limit: int = 10000, audit_limit: int = 100000, lane_feedback: bool = True) -> None:
+                 history_limit: int = 10000, audit_limit: int = 100000, lane_feedback: bool = True,
+                 uplink_rates: Mapping[int, float] | None = None, lend_ratio: float = 1.25) -> None:
         self._lock = threading.RLock()
         self._changed = threading.Condition(self._lock)
         self._st = DaemonState()
@@ -160,12 +161,38 @@ class TurboBusDaemon:
 
         self._feedback = LaneBalancer(alpha=0.5) if lane_feedback else None
         self._published: dict[tuple[int, str], tuple[object, dict, dict]] = {}
+        # Lending across contention groups (off unless rates are given): a GPU
+        # whose link is busy with its own traffic, or held for it, may still
+        # relay for a target whose measured concurrent rate (all links busy)
+        # is lower by ``lend_ratio`` or more -- a GPU in a more contended
+        # uplink group.  The busy GPU's own uplink group has the headroom the
+        # borrower's lacks; the lane feedback then sizes the borrowed lanes.
+        self._uplink_rates: dict[int, float] = {}
+        self._lend_ratio = max(1.0, float(lend_ratio))
+        if uplink_rates:
+            self.set_uplink_rates(uplink_rates)
         self._executor = None
         self._profile_store = profile_store_path
         if profile_store_path:
             self._load_profiles(profile_store_path)
         if executor is not None:
             self.attach_executor(executor)
+
+    def set_uplink_rates(self, rates: Mapping[int, float] | None) -> None:
+        """Per-GPU host->device rate measured with every link busy
+        (``topology.uplink_probe.probe_rates(...)["concurrent"]``); None or
+        empty turns lending across contention groups off."""
+        with self._lock:
+            self._uplink_rates = {int(g): float(r) for g, r in (rates or {}).items() if float(r) > 0.0}
+
+    def _lendable(self, target: int) -> frozenset[int]:
+        """Busy or held GPUs that may still relay for ``target`` (see
+        ``set_uplink_rates``)."""
+        rates = self._uplink_rates
+        mine = rates.get(int(target))
+        if not rates or mine is None:
+            return frozenset()
+        return frozenset(g for g, r in rates.items() if g != int(target) and r >= self._lend_ratio * mine)
 
     # ---- accessors -------------------------------------------------------------------
     @property
@@ -1395,6 +1422,9 @@ class TurboBusDaemon:
         state = self._runtime_state(now, active_only=True)
         if exclude is not None:
             state = state_without_transfer(state, str(exclude))
+        lend = self._lendable(session.target_gpu)
+        if lend:
+            state = {**state, "lendable_relays": sorted(lend)}
         decision = self._scheduler.plan_transfer(
             session=plan_session, profile_entry=entry, relay_quotas=self._quotas, runtime_state=state,
             total_bytes=total_bytes, chunk_bytes=chunk_bytes,
@@ -1446,6 +1476,7 @@ class TurboBusDaemon:
         # lanes); another tenant's active path still blocks.
         dirs = {str(l.direction).lower() for l in leases}
         busy = busy_relays(state, queue_behind=(session.session_id, session.target_gpu, dirs))
+        busy -= self._lendable(session.target_gpu)
         for l in leases:
             if l.relay_device not in session.relay_gpus:
                 return "relay admission is delayed by session relay ownership"

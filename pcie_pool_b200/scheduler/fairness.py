@@ -104,6 +104,11 @@ def load_view(runtime_state: Mapping[str, object] | None, *, job_id: str | None,
                 # bandwidth to lend: relaying through it would only split the
                 # link between two transfers.
                 busy.add(int(rec["target_device"]))
+        # GPUs the daemon lends across contention groups despite their own
+        # traffic (its ``set_uplink_rates``)
+        lend = frozenset(int(g) for g in runtime_state.get("lendable_relays", ()) or ())
+        held -= lend
+        busy -= lend
         summary = runtime_state.get("summary", {})
         if isinstance(summary, Mapping):
             active = int(summary.get("active_transfer_count", 0) or 0)
