@@ -67,6 +67,14 @@ class KVUnits:
     block_stride: int
     num_blocks: int
     block_ids: tuple[int, ...]
+    # the same ids as a read-only int64 array, kept by the parser so the
+    # checks and the unit-address table need no second conversion
+    ids_array: Any = field(default=None, compare=False, repr=False, hash=False)
+
+    def ids(self):
+        import numpy as np
+
+        return self.ids_array if self.ids_array is not None else np.asarray(self.block_ids, dtype=np.int64)
 
     @property
     def units(self) -> int:
@@ -142,9 +150,10 @@ class LandingSpec:
                 ids = np.asarray(k["block_ids"], dtype=np.int64)
                 if ids.ndim != 1:
                     raise ValueError("block_ids must be a flat list")
+                ids.setflags(write=False)
                 kv = KVUnits(buffers=tuple(str(b) for b in k["buffers"]), lanes=int(k.get("lanes", 1)),
                              lane_stride=int(k.get("lane_stride", 0)), block_stride=int(k["block_stride"]),
-                             num_blocks=int(k["num_blocks"]), block_ids=tuple(ids.tolist()))
+                             num_blocks=int(k["num_blocks"]), block_ids=tuple(ids.tolist()), ids_array=ids)
             except (KeyError, TypeError, ValueError) as exc:
                 raise ValueError(f"landing kv layout is incomplete: {exc}") from None
         tensors = []
@@ -243,7 +252,8 @@ def _validate_units(spec, *, job_id, device_buffer, ranges, h2d, chunk_bytes, bu
         raise ValueError("landing kv layout needs buffers, lanes, blocks and block ids")
     if device_buffer.buffer_id not in k.buffers:
         raise ValueError("the intent's device buffer must be one of the kv buffers")
-    if min(k.block_ids) < 0 or max(k.block_ids) >= k.num_blocks:
+    ids = k.ids()
+    if int(ids.min()) < 0 or int(ids.max()) >= k.num_blocks:
         raise ValueError("landing block id outside the kv cache")
     if k.lane_stride < 0 or k.block_stride < u or k.block_stride % 16 or k.lane_stride % 16:
         raise ValueError("landing kv strides must be 16-byte aligned and hold a unit")
@@ -334,7 +344,7 @@ def unit_addresses(spec: LandingSpec, base_of) -> "Any":
     import numpy as np
 
     k = spec.kv
-    ids = np.asarray(k.block_ids, dtype=np.uint64)
+    ids = k.ids().astype(np.uint64)
     # one row per (layer, lane) base address, one column per block: stream order
     per_buffer = np.array([int(base_of(bid)) for bid in k.buffers], dtype=np.uint64)
     bases = (per_buffer[:, None] + np.arange(k.lanes, dtype=np.uint64)[None, :] * np.uint64(k.lane_stride)).ravel()
